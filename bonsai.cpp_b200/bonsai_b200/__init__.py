@@ -1,0 +1,185 @@
+"""ctypes binding of libbonsai_cuda.so (include/bonsai_cuda.h).
+
+This is the Python-side view of the C ABI that tests and the benchmark use.
+It mirrors the reference's operator surface: ``b1_linear_f32`` is the
+drop-in for ``b1_linear_f32_f32`` (src/b1_0_kernel.h:37-288), ``rope_2d_f32``
+for ``rope_2d_fwd_f32`` (src/b1_0_kernel.h:309-361), and the model entry
+points for one pass of ``build_diffuser_graph`` (src/diffuser_graph.cpp:231-561).
+
+Device tensors are passed as raw pointers (``tensor.data_ptr()``); PyTorch is
+used only to own device memory and streams.  There is no CPU fallback: if the
+shared library is missing or fails to load, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR.parent / "lib" / "libbonsai_cuda.so"
+
+BONSAI_EPI_F32 = 0
+BONSAI_EPI_F16 = 1
+BONSAI_EPI_GELU = 2
+BONSAI_EPI_RESID = 3
+BONSAI_EPI_SWIGLU = 5
+
+PRESET_KLEIN4B = 0
+PRESET_FLUX1 = 1
+
+_lib = None
+
+_c_int = ctypes.c_int
+_c_ll = ctypes.c_longlong
+_vp = ctypes.c_void_p
+_fp = ctypes.c_float
+
+# name -> (restype, argtypes); every symbol declared in include/bonsai_cuda.h
+SIGNATURES = {
+    "bonsai_last_error": (ctypes.c_char_p, []),
+    "bonsai_init": (_c_int, [_c_int]),
+    "bonsai_device_error": (_c_int, []),
+    "bonsai_launch_count": (_c_ll, []),
+    "bonsai_b1_upload": (_c_int, [_vp, _c_int, _c_int, _c_int, ctypes.POINTER(_vp)]),
+    "bonsai_b1_free": (_c_int, [_vp]),
+    "bonsai_b1_shape": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
+    "bonsai_b1_linear_f32": (_c_int, [_vp, _c_int, _vp, _vp, _vp]),
+    "bonsai_b1_gemm": (_c_int, [_vp, _c_ll, _c_int, _vp, _c_int, _vp, _c_ll, _vp, _vp]),
+    "bonsai_rope_2d_f32": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp]),
+    "bonsai_rope_tables": (_c_int, [_vp, _c_int, _c_int, _vp, _fp, _vp, _vp, _vp]),
+    "bonsai_rms_norm_f32": (_c_int, [_vp, _vp, _c_int, _c_int, _fp, _vp, _vp]),
+    "bonsai_ln_modulate": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _fp, _vp, _c_ll, _vp]),
+    "bonsai_ln_modulate_f32": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _fp, _vp, _vp]),
+    "bonsai_joint_attention": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _fp, _vp, _c_ll, _vp]),
+    "bonsai_qk_norm_rope": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _c_int, _fp, _vp, _vp, _vp]),
+    "bonsai_dit_create": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "bonsai_dit_destroy": (_c_int, [_vp]),
+    "bonsai_dit_forward": (_c_int, [_vp, _vp, _vp, _vp, _fp, _vp, _vp]),
+    "bonsai_dit_forward_host": (_c_int, [_vp, _vp, _vp, _vp, _fp, _vp, _vp]),
+    "bonsai_dit_set_state": (_c_int, [_vp, _vp, _vp, _vp]),
+    "bonsai_dit_get_state": (_c_int, [_vp, _vp, _vp]),
+    "bonsai_dit_double_block": (_c_int, [_vp, _c_int, _vp]),
+    "bonsai_dit_single_block": (_c_int, [_vp, _c_int, _vp]),
+    "bonsai_dit_weight": (_c_ll, [_vp, ctypes.c_char_p, _vp, _c_ll]),
+}
+
+
+class BonsaiError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """Load the shared library (raises if it is absent: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise BonsaiError(
+                f"{LIB_PATH} not found: build it with `make -C bonsai.cpp_b200` "
+                "(or __graft_entry__.build())")
+        L = ctypes.CDLL(str(LIB_PATH))
+        missing = []
+        for name, (res, args) in SIGNATURES.items():
+            try:
+                fn = getattr(L, name)
+            except AttributeError:
+                missing.append(name)
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        L.missing_symbols = missing
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = lib().bonsai_last_error().decode(errors="replace")
+        raise BonsaiError(f"{what or 'bonsai call'} failed with {rc}: {msg}")
+
+
+def stream_ptr(stream=None) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def init(device: int = 0) -> None:
+    check(lib().bonsai_init(device), "bonsai_init")
+
+
+def device_error() -> int:
+    return int(lib().bonsai_device_error())
+
+
+def launch_count() -> int:
+    return int(lib().bonsai_launch_count())
+
+
+class B1Weight:
+    """Device B1_0 weight uploaded from the reference's packed bytes."""
+
+    def __init__(self, packed: np.ndarray, out_dim: int, in_dim: int, swiglu_from: int = -1):
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        assert packed.size == out_dim * (in_dim // 32) * 6, "packed size mismatch"
+        h = _vp()
+        check(lib().bonsai_b1_upload(packed.ctypes.data, out_dim, in_dim, swiglu_from,
+                                     ctypes.byref(h)), "bonsai_b1_upload")
+        self.handle = h
+        self.out_dim = out_dim
+        self.in_dim = in_dim
+
+    def free(self):
+        if self.handle:
+            lib().bonsai_b1_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def b1_linear_f32(act, w: B1Weight, out, stream=None) -> None:
+    """Drop-in b1_linear_f32_f32: act f32 [T][K] -> out f32 [T][N] (device tensors)."""
+    assert act.is_contiguous() and out.is_contiguous()
+    T = act.shape[0]
+    check(lib().bonsai_b1_linear_f32(act.data_ptr(), T, w.handle, out.data_ptr(),
+                                     stream_ptr(stream)), "bonsai_b1_linear_f32")
+
+
+def b1_gemm(x16, w: B1Weight, mode: int, out, gate=None, stream=None) -> None:
+    """Fused-epilogue GEMM on f16 activations x16 [T][ldx]."""
+    T = x16.shape[0]
+    check(lib().bonsai_b1_gemm(x16.data_ptr(), x16.stride(0), T, w.handle, mode,
+                               out.data_ptr(), out.stride(0),
+                               gate.data_ptr() if gate is not None else None,
+                               stream_ptr(stream)), "bonsai_b1_gemm")
+
+
+# ----------------------------------------------------------------- host side
+def random_b1_packed(out_dim: int, in_dim: int, rng: np.random.Generator,
+                     scale_std: float = 0.02) -> np.ndarray:
+    """Seeded random packed B1_0 matrix [out_dim][in_dim/32*6] (uint8): signs
+    Bernoulli(0.5), scales |N(0, scale_std)| rounded to f16, in the layout of
+    convert_to_b1_0_packed.py:21-43."""
+    nb = in_dim // 32
+    signs = rng.integers(0, 2, size=(out_dim, nb, 32), dtype=np.uint8)
+    scales = np.abs(rng.standard_normal((out_dim, nb)) * scale_std).astype(np.float16)
+    raw = np.zeros((out_dim, nb, 6), dtype=np.uint8)
+    raw[:, :, 0:2] = scales.view(np.uint8).reshape(out_dim, nb, 2)
+    raw[:, :, 2:6] = np.packbits(signs, axis=-1, bitorder="little")
+    return raw.reshape(out_dim, nb * 6)
+
+
+def dequant_b1(packed: np.ndarray, out_dim: int, in_dim: int) -> np.ndarray:
+    """f32 [out_dim][in_dim] = +-scale per the B1_0 block rule
+    (tests/test_diffuser.py:24-33 dequant of the reference)."""
+    nb = in_dim // 32
+    raw = np.ascontiguousarray(packed, dtype=np.uint8).reshape(out_dim, nb, 6)
+    scales = raw[:, :, 0:2].copy().view(np.float16).reshape(out_dim, nb).astype(np.float32)
+    bits = np.unpackbits(raw[:, :, 2:6], axis=-1, bitorder="little").astype(np.float32)
+    return ((bits * 2.0 - 1.0) * scales[:, :, None]).reshape(out_dim, in_dim)

@@ -1,0 +1,76 @@
+// Internal declarations shared by the kernel translation units and the
+// host-side engine.  Nothing here is part of the public C ABI
+// (include/bonsai_cuda.h).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <string>
+
+namespace bonsai {
+
+// ------------------------------------------------------------------ status
+void set_error(const std::string& msg);  // stores the message for bonsai_last_error()
+int fail(int code, const std::string& msg);  // set_error + return code
+int cuda_status(cudaError_t e, const char* what);  // 0 or BONSAI_ERR_CUDA
+int launch_status(const char* what);  // checks cudaGetLastError() and counts the launch
+int* device_error_word();  // device address of the per-device error word (lazily resolved)
+int num_sms();
+
+// ------------------------------------------------------- B1_0 device weights
+// Device layout ("chunked"): the packed reference layout [N][K/32][6 bytes]
+// is retiled on upload into chunks of 128 output rows x 64 inputs.  Chunk
+// (ftile, kb) holds three arrays of 128 u32: the sign word of group 2kb, the
+// sign word of group 2kb+1 (both in "pair-split" bit order: bit j = input
+// 2j, bit j+16 = input 2j+1), and both fp16 scales packed (lo = group 2kb).
+// Rows beyond N and groups beyond K/32 are zero (scale 0).  The size is the
+// same 6 bytes per 32 weights as the packed file (plus tile padding).
+struct B1Weight {
+  int n_rows = 0;      // output features N
+  int k_in = 0;        // input features K
+  int n_ftiles = 0;    // ceil(N / 128)
+  int k_blocks = 0;    // ceil(K / 64)
+  int swiglu_from = -1;  // rows [swiglu_from, N) are stored gate/value interleaved
+  uint32_t* chunks = nullptr;  // n_ftiles * k_blocks * 384 words
+  int device = 0;
+};
+
+constexpr int kChunkWords = 384;  // 3 x 128 u32 per (128-row, 64-input) chunk
+
+// ------------------------------------------------------------- epilogues
+enum EpiMode : int {
+  EPI_F32 = 0,         // dst f32 [t][ld] at col_off + (row - row_begin)
+  EPI_F16 = 1,         // dst f16
+  EPI_GELU_F16 = 2,    // dst f16 = gelu_tanh(acc)
+  EPI_RESID_F32 = 3,   // dst f32 += gate[row - row_begin] * acc  (gate may be null -> 1)
+  EPI_QKV_F16 = 4,     // head-major scatter: dst[(which*heads + h)*seq_total + tok_off + t][d]
+  EPI_SWIGLU_F16 = 5,  // interleaved gate/value rows -> dst f16 silu(g)*v at col_off + (row-row_begin)/2
+};
+
+struct EpiSeg {
+  int mode = EPI_F32;
+  int row_begin = 0, row_end = 0;
+  void* dst = nullptr;
+  long long ld = 0;   // elements
+  int col_off = 0;
+  const float* gate = nullptr;
+  int heads = 0, seq_total = 0, tok_off = 0, head_dim = 128;
+};
+
+constexpr int kMaxSegs = 2;
+
+// Launch the tcgen05 B1_0 GEMM: for every token t < tokens and weight row n,
+// acc[t][n] = sum_k x[t][k] * W[n][k]; acc is routed through the segment that
+// covers n.  x is f16 (or bf16 when x_bf16) row-major with leading dimension
+// ldx (elements); it must be 16-byte aligned with ldx % 8 == 0.
+int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w,
+                   const EpiSeg* segs, int nseg, bool x_bf16, cudaStream_t st);
+
+// Retile packed reference bytes (device copy) into the chunked layout.
+int launch_b1_retile(const uint8_t* dev_packed, B1Weight& w, cudaStream_t st);
+
+// ------------------------------------------------------------ elementwise
+int launch_f32_to_f16(const float* src, __half* dst, long long n, cudaStream_t st);
+
+}  // namespace bonsai

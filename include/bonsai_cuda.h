@@ -1,0 +1,234 @@
+/*
+ * bonsai_cuda.h - C ABI of the B200 (sm_100a) diffuser-transformer engine.
+ *
+ * Drop-in boundary for bonsai.cpp's diffuser step.  The reference builds a
+ * ggml graph whose custom ops are recognised by a magic number in their
+ * user data (src/b1_0_kernel.h:32 "1B1B" b1_linear, src/b1_0_kernel.h:303
+ * "ROPE" rope_2d_fwd) next to built-in ggml ops (norm, rms_norm,
+ * flash_attn_ext, swiglu) called from build_diffuser_graph
+ * (src/diffuser_graph.cpp:231-561).  Every entry point here replaces one of
+ * those ops, one block, or the whole step, with the same tensors.
+ *
+ * Conventions
+ *   - All tensor arguments are DEVICE pointers unless the name says host_.
+ *   - Row-major; "[a][b]" means a rows of b contiguous elements.  A ggml
+ *     tensor with ne = {b, a} has exactly this layout.
+ *   - f16 = IEEE binary16 stored as uint16_t.  Activations that feed the
+ *     tensor cores are f16; the residual stream and drop-in outputs are f32.
+ *   - stream is a cudaStream_t passed as void* (NULL = legacy stream).
+ *     Calls are asynchronous and stream-ordered; none synchronises the host.
+ *   - Every function returns 0 on success or a negative BONSAI_ERR_* code;
+ *     bonsai_last_error() describes the most recent failure of the calling
+ *     thread.  Nothing aborts the process (the reference aborts on NaN /
+ *     missing weights: src/b1_0_kernel.h:195-198, src/diffuser.cpp:52-56).
+ */
+#ifndef BONSAI_CUDA_H
+#define BONSAI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BONSAI_OK 0
+#define BONSAI_ERR_ARG (-1)         /* bad argument / shape */
+#define BONSAI_ERR_UNSUPPORTED (-2) /* shape or mode not supported */
+#define BONSAI_ERR_CUDA (-3)        /* CUDA runtime error */
+#define BONSAI_ERR_DEVICE (-4)      /* a kernel reported a device-side error (bounded wait expired) */
+#define BONSAI_ERR_DRIVER (-5)      /* driver entry point (tensor-map encoder) unavailable */
+#define BONSAI_ERR_NOMEM (-6)       /* device allocation failed */
+
+/* Magic numbers of the reference's custom-op user data; a ggml backend that
+ * routes nodes to this library matches on them (src/b1_0_kernel.h:32, :303). */
+#define BONSAI_B1_MAGIC 0x31423142
+#define BONSAI_ROPE_MAGIC 0x524F5045
+
+/* B1_0 block format: 32 weights per 6-byte block = fp16 scale (LE) + u32
+ * sign bits (LE, bit i -> input 32*blk+i, 1 = +scale, 0 = -scale).
+ * src/diffuser_types.h:10-11, convert_to_b1_0_packed.py:21-43. */
+#define BONSAI_B1_BLOCK_SIZE 32
+#define BONSAI_B1_BLOCK_BYTES 6
+
+/* ------------------------------------------------------------- runtime */
+
+/* Message for the most recent failure on the calling thread ("" if none). */
+const char* bonsai_last_error(void);
+
+/* Select the CUDA device used by later calls from this thread and check it
+ * is an sm_100 part.  Replaces ggml_backend_cpu_init()
+ * (src/diffuser.cpp:214). */
+int bonsai_init(int device);
+
+/* Read and clear the device-side error word of the current device: 0, or the
+ * code of the first bounded wait that expired since the last call.
+ * Synchronises the device. */
+int bonsai_device_error(void);
+
+/* Number of kernel launches this library has issued on the current thread
+ * since the last call (launch accounting for benchmarks); resets to 0. */
+long long bonsai_launch_count(void);
+
+/* ------------------------------------------------------ B1_0 weights */
+
+typedef struct bonsai_b1_weight* bonsai_b1_t;
+
+/* Upload one packed B1_0 matrix exactly as written by
+ * convert_to_b1_0_packed.py and loaded by load_b1 (src/diffuser.cpp:39-50):
+ * host_packed = [out_dim][in_dim/32][6] bytes.  The device copy is retiled
+ * (same 6 bytes per 32 weights); the on-disk layout is unchanged.
+ * swiglu_from: -1, or the first row of a trailing [gate; value] pair of
+ * halves that should be stored interleaved so the SwiGLU epilogue can fuse
+ * (rows [swiglu_from, out_dim) must split into two equal halves).
+ * in_dim % 32 == 0 is required (src/diffuser.cpp:43). */
+int bonsai_b1_upload(const uint8_t* host_packed, int out_dim, int in_dim, int swiglu_from,
+                     bonsai_b1_t* out);
+int bonsai_b1_free(bonsai_b1_t w);
+int bonsai_b1_shape(bonsai_b1_t w, int* out_dim, int* in_dim);
+
+/* Drop-in for b1_linear_f32_f32 (src/b1_0_kernel.h:37-288) as invoked by
+ * b1_linear() (src/b1_0_kernel.h:290-300):
+ *   out[t][r] = sum_blk scale[r][blk] * sum_i (bit ? +act : -act)
+ * act: f32 [tokens][in_dim]; out: f32 [tokens][out_dim].
+ * The activations are rounded to f16 for the tensor cores (f32
+ * accumulation).  Uses an internal scratch buffer for the f16 copy of act,
+ * grown on demand with cudaMallocAsync on the given stream. */
+int bonsai_b1_linear_f32(const float* act, int tokens, bonsai_b1_t w, float* out, void* stream);
+
+/* Fused-epilogue B1_0 GEMM on f16 activations (the form the engine uses).
+ * x: f16 [tokens][ldx] (16-byte aligned, ldx % 8 == 0).  The accumulator
+ * acc[t][r] is written according to mode:
+ *   BONSAI_EPI_F32    out f32  [t][ld_out] at column r
+ *   BONSAI_EPI_F16    out f16  [t][ld_out] at column r
+ *   BONSAI_EPI_GELU   out f16  = gelu_tanh(acc)
+ *   BONSAI_EPI_RESID  out f32 += gate[r] * acc   (gate may be NULL = 1)
+ *                      (adaLN gate-residual, src/diffuser_graph.cpp:439-460, :538)
+ *   BONSAI_EPI_SWIGLU out f16 [t][ld_out] at column r/2 = silu(g)*v for a
+ *                      weight uploaded with swiglu_from = 0
+ *                      (ggml_swiglu, src/diffuser_graph.cpp:227-229)
+ */
+#define BONSAI_EPI_F32 0
+#define BONSAI_EPI_F16 1
+#define BONSAI_EPI_GELU 2
+#define BONSAI_EPI_RESID 3
+#define BONSAI_EPI_SWIGLU 5
+int bonsai_b1_gemm(const uint16_t* x, long long ldx, int tokens, bonsai_b1_t w, int mode,
+                   void* out, long long ld_out, const float* gate, void* stream);
+
+/* ------------------------------------------------------ pointwise ops */
+
+/* Drop-in for rope_2d_fwd_f32 (src/b1_0_kernel.h:309-361): for every
+ * (s, h, d) pair, (a, b) = (x[s][h][2d], x[s][h][2d+1]) ->
+ * (a*c - b*s, a*s + b*c) with c = cos_t[s][d], s = sin_t[s][d].
+ * x, out: f32 [seq][n_heads][head_dim]; cos_t, sin_t: f32 [seq][head_dim/2].
+ * out may equal x. */
+int bonsai_rope_2d_f32(const float* x, const float* cos_t, const float* sin_t, int head_dim,
+                       int n_heads, int seq, float* out, void* stream);
+
+/* RoPE angle tables of build_rope_cos_sin (src/diffuser_graph.cpp:126-182):
+ * freq[a][j] = 1 / theta^(2j/axes_dim[a]); pair d of the head belongs to the
+ * axis whose half-range contains it (axes concatenated in order);
+ * angle[s][d] = ids[s][a] * freq[a][j].  ids: f32 [seq][n_axes] (device);
+ * cos_out / sin_out: f32 [seq][sum(axes_dim)/2]. */
+int bonsai_rope_tables(const float* ids, int seq, int n_axes, const int* host_axes_dim,
+                       float theta, float* cos_out, float* sin_out, void* stream);
+
+/* Q/K RMSNorm of rms_norm_qk (src/diffuser_graph.cpp:71-79): for each row
+ * of head_dim values, y = x / sqrt(mean(x^2) + eps) * w.
+ * x, out: f32 [rows][head_dim]; w: f32 [head_dim]. */
+int bonsai_rms_norm_f32(const float* x, const float* w, int rows, int head_dim, float eps,
+                        float* out, void* stream);
+
+/* adaLN modulate of the blocks (src/diffuser_graph.cpp:347-352, :444-448,
+ * :479-480, :546-552): y = LayerNorm(x; eps, no affine) * (1 + scale) + shift.
+ * x: f32 [rows][dim]; shift, scale: f32 [dim]; y: f16 [rows][ld_y]. */
+int bonsai_ln_modulate(const float* x, int rows, int dim, const float* shift, const float* scale,
+                       float eps, uint16_t* y, long long ld_y, void* stream);
+
+/* Same, f32 output (the reference's own ggml_norm + mul/add chain). */
+int bonsai_ln_modulate_f32(const float* x, int rows, int dim, const float* shift,
+                           const float* scale, float eps, float* y, void* stream);
+
+/* ------------------------------------------------------ attention */
+
+/* Joint non-causal attention (ggml_flash_attn_ext with scale, no mask,
+ * GGML_PREC_F32: src/diffuser_graph.cpp:403-416, :506-519).
+ * q, k, v: f16 head-major [n_heads][seq][head_dim] (head_dim = 128).
+ * out: f16 token-major [seq][ld_out] with head h at columns h*head_dim.
+ * scale: softmax scale (the reference uses 1/sqrt(head_dim)). */
+int bonsai_joint_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int n_heads,
+                           int seq, int head_dim, float scale, uint16_t* out, long long ld_out,
+                           void* stream);
+
+/* Q/K RMSNorm + RoPE fused, in place on head-major f16 q or k
+ * [n_heads][seq][head_dim]: rows with token index < split use w_lo, the
+ * rest w_hi (double blocks normalise text and image tokens with different
+ * weights: src/diffuser_graph.cpp:371-374).  cos_t/sin_t: f32 [seq][head_dim/2]. */
+int bonsai_qk_norm_rope(uint16_t* qk, int n_heads, int seq, int head_dim, const float* w_lo,
+                        const float* w_hi, int split, float eps, const float* cos_t,
+                        const float* sin_t, void* stream);
+
+/* ------------------------------------------------------ whole model */
+
+/* Model presets.  KLEIN4B = the reference's compiled-in DiffuserParams
+ * (src/diffuser_types.h:13-30): 5 double + 20 single blocks, SwiGLU MLP
+ * 9216, axes (32,32,32,32), theta 2000, shared modulation, in 128, ctx 7680.
+ * FLUX1 = Flux.1-schnell dims: 19 + 38 blocks, GELU-tanh MLP 12288, axes
+ * (16,56,56), theta 10000, per-block modulation (B1_0), pooled 768, in 64,
+ * ctx 4096. */
+#define BONSAI_PRESET_KLEIN4B 0
+#define BONSAI_PRESET_FLUX1 1
+
+typedef struct bonsai_dit* bonsai_dit_t;
+
+typedef struct {
+  int preset;          /* BONSAI_PRESET_* */
+  int depth;           /* double blocks to run (0 = preset value) */
+  int depth_single;    /* single blocks to run (0 = preset value) */
+  int img_tokens;      /* image tokens (latent H*W after 2x2 packing) */
+  int txt_tokens;      /* text tokens */
+  int grid_h, grid_w;  /* image token grid for RoPE ids (grid_h*grid_w == img_tokens) */
+  unsigned long long seed; /* random-init weights (no checkpoint is read) */
+} bonsai_dit_config;
+
+/* Create a model with seeded random B1_0 block weights and f32 edge weights
+ * (signs Bernoulli(0.5), scales |N(0, 0.02)| as f16; f32 weights N(0, 0.02);
+ * norm weights N(1, 0.1)), plus the activation workspace for the given
+ * token counts.  The weights are generated on the host with the same
+ * generator the CPU oracle uses, so both see identical tensors. */
+int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out);
+int bonsai_dit_destroy(bonsai_dit_t m);
+
+/* One denoise-step forward of build_diffuser_graph (src/diffuser_graph.cpp:231-561)
+ * on device buffers: img f32 [img_tokens][in_ch], txt f32 [txt_tokens][ctx_dim],
+ * pooled f32 [768] (FLUX1 only, else NULL), timestep t (the graph input, i.e.
+ * already x1000 as src/diffuser.cpp:264 does); out f32 [img_tokens][in_ch]. */
+int bonsai_dit_forward(bonsai_dit_t m, const float* img, const float* txt, const float* pooled,
+                       float timestep, float* out, void* stream);
+
+/* Same with host buffers: copies in, runs, copies the prediction back and
+ * synchronises the stream (what a ggml backend's graph_compute does). */
+int bonsai_dit_forward_host(bonsai_dit_t m, const float* host_img, const float* host_txt,
+                            const float* host_pooled, float timestep, float* host_out,
+                            void* stream);
+
+/* Run only double block i (0-based) or single block i on the model's
+ * current hidden state; used by block-level parity tests.  The hidden
+ * state is f32 [txt_tokens + img_tokens][3072] (text rows first, as
+ * ggml_concat(h_txt, h_img) in src/diffuser_graph.cpp:468). */
+int bonsai_dit_set_state(bonsai_dit_t m, const float* hidden, const float* vec, void* stream);
+int bonsai_dit_get_state(bonsai_dit_t m, float* hidden, void* stream);
+int bonsai_dit_double_block(bonsai_dit_t m, int i, void* stream);
+int bonsai_dit_single_block(bonsai_dit_t m, int i, void* stream);
+
+/* Export the seeded host weights of the model (packed B1_0 bytes and f32
+ * tensors) by name, for the CPU oracle: returns the byte size when buf is
+ * NULL.  Names follow the reference's safetensors keys
+ * (src/diffuser.cpp:107-183). */
+long long bonsai_dit_weight(bonsai_dit_t m, const char* name, void* buf, long long cap);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BONSAI_CUDA_H */

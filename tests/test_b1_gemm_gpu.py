@@ -1,0 +1,125 @@
+"""B1_0 GEMM on the GPU vs exact references.
+
+Reference semantics: b1_linear_f32_f32 (src/b1_0_kernel.h:37-288),
+out[t][r] = sum_blk scale[r][blk] * sum_i (bit ? +x : -x).
+The kernel rounds activations to f16 and accumulates in f32, so it is
+compared (1) against an f64 dequantised product of the SAME f16-rounded
+activations (tight: only summation order differs) and (2) against the f32
+reference semantics with the acceptance bar of the reference's GPU-vs-CPU
+tests (cos >= 0.9999, max-abs <= 1e-2 * RMS; tests/c_ops/test_webgpu_ops.cpp:129).
+"""
+import numpy as np
+import pytest
+
+import bonsai_b200 as bb
+
+pytestmark = pytest.mark.gpu
+
+SWEEP_M = [1280, 4352, 8704]
+SWEEP_KN = [(3072, 9216), (3072, 3072), (3072, 12288), (12288, 3072), (3072, 21504), (15360, 3072)]
+
+
+def _cos(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
+
+
+def _case(M, K, N, seed):
+    rng = np.random.default_rng(seed)
+    packed = bb.random_b1_packed(N, K, rng)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    return packed, x
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (1, 64, 32),        # the reference's own unit-test shape (tests/c_ops/test_b1_linear.py:43-45)
+    (7, 96, 40),        # ragged: K % 64 == 32, N % 128 != 0, M < 32
+    (128, 128, 128),
+    (300, 3072, 200),
+    (129, 256, 384),
+    (256, 512, 1000),
+])
+def test_b1_linear_f32_small(gpu, M, K, N):
+    import torch
+    packed, x = _case(M, K, N, 1000 + M + K + N)
+    w = bb.B1Weight(packed, N, K)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    bb.b1_linear_f32(xd, w, out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    wd = bb.dequant_b1(packed, N, K).astype(np.float64)
+    x16 = x.astype(np.float16).astype(np.float64)
+    exact16 = x16 @ wd.T
+    rms = np.sqrt(np.mean(exact16 ** 2)) + 1e-30
+    assert np.max(np.abs(got - exact16)) <= 1e-4 * rms + 1e-6
+    ref32 = x.astype(np.float64) @ wd.T
+    assert _cos(got, ref32) >= 0.9999
+    assert np.max(np.abs(got - ref32)) <= 1e-2 * np.sqrt(np.mean(ref32 ** 2))
+
+
+def test_b1_zero_tokens_is_noop(gpu):
+    import torch
+    packed, _ = _case(1, 64, 32, 5)
+    w = bb.B1Weight(packed, 32, 64)
+    x = torch.zeros(0, 64, device="cuda")
+    out = torch.zeros(0, 32, device="cuda")
+    bb.b1_linear_f32(x, w, out)
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("K,N", SWEEP_KN)
+def test_b1_gemm_sweep_shapes(gpu, K, N):
+    """Every (K,N) of the BASELINE GEMM sweep at every M, vs a torch fp32
+    product of the dequantised weights and the same f16 activations."""
+    import torch
+    rng = np.random.default_rng(K * 7 + N)
+    packed = bb.random_b1_packed(N, K, rng)
+    w = bb.B1Weight(packed, N, K)
+    wd = torch.from_numpy(bb.dequant_b1(packed, N, K)).cuda()
+    for M in SWEEP_M:
+        g = torch.Generator(device="cuda").manual_seed(M)
+        x16 = torch.randn(M, K, device="cuda", generator=g).half()
+        out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+        bb.b1_gemm(x16, w, bb.BONSAI_EPI_F32, out)
+        ref = x16.float() @ wd.t()
+        torch.cuda.synchronize()
+        rms = ref.pow(2).mean().sqrt().item()
+        err = (out - ref).abs().max().item()
+        cos = torch.nn.functional.cosine_similarity(out.flatten().double(), ref.flatten().double(), dim=0).item()
+        assert cos >= 0.99999, (M, K, N, cos)
+        assert err <= 1e-3 * rms, (M, K, N, err, rms)
+
+
+def test_b1_gemm_epilogues(gpu):
+    import torch
+    M, K, N = 300, 1024, 512
+    rng = np.random.default_rng(77)
+    packed = bb.random_b1_packed(N, K, rng)
+    w = bb.B1Weight(packed, N, K)
+    wd = torch.from_numpy(bb.dequant_b1(packed, N, K)).cuda()
+    x16 = torch.randn(M, K, device="cuda").half()
+    ref = x16.float() @ wd.t()
+    # f16 store
+    o16 = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    bb.b1_gemm(x16, w, bb.BONSAI_EPI_F16, o16)
+    torch.testing.assert_close(o16.float(), ref.half().float(), rtol=2e-3, atol=2e-3)
+    # GELU-tanh
+    og = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    bb.b1_gemm(x16, w, bb.BONSAI_EPI_GELU, og)
+    torch.testing.assert_close(og.float(), torch.nn.functional.gelu(ref, approximate="tanh"),
+                               rtol=4e-3, atol=4e-3)
+    # gate-residual: h += g * acc
+    h0 = torch.randn(M, N, device="cuda")
+    gate = torch.randn(N, device="cuda")
+    h = h0.clone()
+    bb.b1_gemm(x16, w, bb.BONSAI_EPI_RESID, h, gate=gate)
+    torch.testing.assert_close(h, h0 + gate[None, :] * ref, rtol=1e-4, atol=1e-4)
+    # SwiGLU on [gate; value] halves (ggml_swiglu: silu(first half) * second half)
+    ws = bb.B1Weight(packed, N, K, swiglu_from=0)
+    osw = torch.empty(M, N // 2, device="cuda", dtype=torch.float16)
+    bb.b1_gemm(x16, ws, bb.BONSAI_EPI_SWIGLU, osw)
+    g_, v_ = ref[:, : N // 2], ref[:, N // 2:]
+    torch.testing.assert_close(osw.float(), torch.nn.functional.silu(g_) * v_, rtol=4e-3, atol=4e-3)
+    torch.cuda.synchronize()
