@@ -183,3 +183,99 @@ def dequant_b1(packed: np.ndarray, out_dim: int, in_dim: int) -> np.ndarray:
     scales = raw[:, :, 0:2].copy().view(np.float16).reshape(out_dim, nb).astype(np.float32)
     bits = np.unpackbits(raw[:, :, 2:6], axis=-1, bitorder="little").astype(np.float32)
     return ((bits * 2.0 - 1.0) * scales[:, :, None]).reshape(out_dim, in_dim)
+
+
+# ----------------------------------------------------------------- model
+class DitConfig(ctypes.Structure):
+    _fields_ = [("preset", ctypes.c_int), ("depth", ctypes.c_int), ("depth_single", ctypes.c_int),
+                ("img_tokens", ctypes.c_int), ("txt_tokens", ctypes.c_int),
+                ("grid_h", ctypes.c_int), ("grid_w", ctypes.c_int), ("seed", ctypes.c_ulonglong)]
+
+
+PRESET_DIMS = {
+    # preset: (depth, depth_single, mlp, swiglu, in_ch, ctx_dim, pooled, axes, theta, per_block_mod)
+    PRESET_KLEIN4B: (5, 20, 9216, True, 128, 7680, 0, (32, 32, 32, 32), 2000.0, False),
+    PRESET_FLUX1: (19, 38, 12288, False, 64, 4096, 768, (16, 56, 56), 10000.0, True),
+}
+HIDDEN, HEADS, HEAD_DIM = 3072, 24, 128
+
+
+class Dit:
+    """One diffuser transformer on the device (bonsai_dit_* entry points)."""
+
+    def __init__(self, preset: int, img_tokens: int, txt_tokens: int, grid_h: int, grid_w: int,
+                 depth: int = 0, depth_single: int = 0, seed: int = 1234):
+        d = PRESET_DIMS[preset]
+        self.preset = preset
+        self.depth = depth or d[0]
+        self.depth_single = depth_single or d[1]
+        self.mlp, self.swiglu, self.in_ch, self.ctx_dim, self.pooled = d[2], d[3], d[4], d[5], d[6]
+        self.axes, self.theta, self.per_block_mod = d[7], d[8], d[9]
+        self.img, self.txt, self.L = img_tokens, txt_tokens, img_tokens + txt_tokens
+        self.grid_h, self.grid_w = grid_h, grid_w
+        cfg = DitConfig(preset, depth, depth_single, img_tokens, txt_tokens, grid_h, grid_w, seed)
+        h = _vp()
+        check(lib().bonsai_dit_create(ctypes.byref(cfg), ctypes.byref(h)), "bonsai_dit_create")
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().bonsai_dit_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def weight(self, name: str) -> np.ndarray:
+        n = lib().bonsai_dit_weight(self.handle, name.encode(), None, 0)
+        if n < 0:
+            check(int(n), f"bonsai_dit_weight({name})")
+        buf = np.empty(n, np.uint8)
+        check(0 if lib().bonsai_dit_weight(self.handle, name.encode(), buf.ctypes.data, n) == n
+              else -1, f"bonsai_dit_weight({name})")
+        return buf
+
+    def weight_f32(self, name: str) -> np.ndarray:
+        return self.weight(name).view(np.float32)
+
+    def rope_ids(self) -> np.ndarray:
+        """Token ids [L][n_axes] (src/diffuser.cpp:240-249): text 0, image (.., y, x)."""
+        na = len(self.axes)
+        ids = np.zeros((self.L, na), np.float32)
+        for y in range(self.grid_h):
+            for x in range(self.grid_w):
+                ids[self.txt + y * self.grid_w + x, na - 2] = y
+                ids[self.txt + y * self.grid_w + x, na - 1] = x
+        return ids
+
+    def forward(self, img, txt, pooled, t: float, out, stream=None):
+        check(lib().bonsai_dit_forward(self.handle, img.data_ptr(),
+                                       txt.data_ptr() if txt is not None else None,
+                                       pooled.data_ptr() if pooled is not None else None,
+                                       float(t), out.data_ptr(), stream_ptr(stream)),
+              "bonsai_dit_forward")
+
+    def forward_host(self, img: np.ndarray, txt: np.ndarray, pooled, t: float,
+                     out: np.ndarray, stream=None):
+        check(lib().bonsai_dit_forward_host(self.handle, img.ctypes.data,
+                                            txt.ctypes.data if txt is not None else None,
+                                            pooled.ctypes.data if pooled is not None else None,
+                                            float(t), out.ctypes.data, stream_ptr(stream)),
+              "bonsai_dit_forward_host")
+
+    def set_state(self, hidden, vec, stream=None):
+        check(lib().bonsai_dit_set_state(self.handle, hidden.data_ptr(), vec.data_ptr(),
+                                         stream_ptr(stream)), "bonsai_dit_set_state")
+
+    def get_state(self, hidden, stream=None):
+        check(lib().bonsai_dit_get_state(self.handle, hidden.data_ptr(), stream_ptr(stream)),
+              "bonsai_dit_get_state")
+
+    def double_block(self, i: int, stream=None):
+        check(lib().bonsai_dit_double_block(self.handle, i, stream_ptr(stream)), "double_block")
+
+    def single_block(self, i: int, stream=None):
+        check(lib().bonsai_dit_single_block(self.handle, i, stream_ptr(stream)), "single_block")

@@ -1,0 +1,359 @@
+// Joint (text + image) non-causal attention for sm_100a.
+//
+// Replaces ggml_flash_attn_ext as the reference calls it
+// (src/diffuser_graph.cpp:403-416 double blocks, :506-519 single blocks):
+// softmax(Q K^T * scale) V per head, no mask, K and V in f16, f32 softmax.
+//
+// One CTA = one head x 128 queries.  Roles:
+//   warp 0      TMA: Q once, then K_j / V_j tiles (128 keys x 128 dims, two
+//               64-dim halves with 128-byte swizzle) into a 3-deep K ring and
+//               a 2-deep V ring.
+//   warp 1      one thread issues tcgen05.mma:
+//                 S_j = Q K_j^T   (A, B from SMEM; S double-buffered in TMEM)
+//                 O  += P_j V_j   (A = P from TMEM, B = V from SMEM, MN-major)
+//   warps 2-5   softmax: thread i owns query row i (TMEM lane i).  Online
+//               softmax in the log2 domain with lazy rescaling: the running
+//               max only moves (and O in TMEM is rescaled) when a tile's max
+//               exceeds it by more than 8 (p <= 2^8 fits f16 P exactly
+//               enough); the final 1/l normalisation makes the result exact.
+// TMEM: S0 [0,128) S1 [128,256) O [256,384) P [384,448) (f16 pairs).
+#include "internal.cuh"
+#include "ptx.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace bonsai {
+namespace attn {
+
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int HD = 128;
+constexpr int KS = 3;  // K ring depth
+constexpr int VS = 2;  // V ring depth
+constexpr int TILE_BYTES = BKV * HD * 2;  // 32 KB (two 16 KB halves)
+constexpr int HALF_BYTES = TILE_BYTES / 2;
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int S_COL = 0, O_COL = 256, P_COL = 384;
+constexpr int SMEM_BYTES = 1024 + TILE_BYTES * (1 + KS + VS) + 256;
+constexpr float kRescaleThreshold = 8.0f;
+
+struct Params {
+  int seq;
+  int n_heads;
+  float scale_log2;  // softmax scale * log2(e)
+  __half* out;
+  long long ld_out;
+  int* err;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap qmap,
+                     const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* qs = smem;
+  uint8_t* ks = qs + TILE_BYTES;
+  uint8_t* vs = ks + KS * TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + VS * TILE_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;  // [2]
+  uint64_t* p_ready = s_full + 2;
+  uint64_t* pv_done = p_ready + 1;
+  uint64_t* drain = pv_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const uint32_t lane = lane_id();
+  const int head = blockIdx.y;
+  const int q0 = blockIdx.x * BQ;
+  const int nkv = (p.seq + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    bar_init(q_full, 1);
+    for (int s = 0; s < KS; ++s) {
+      bar_init(&k_full[s], 1);
+      bar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VS; ++s) {
+      bar_init(&v_full[s], 1);
+      bar_init(&v_empty[s], 1);
+    }
+    bar_init(&s_full[0], 1);
+    bar_init(&s_full[1], 1);
+    bar_init(p_ready, 4);
+    bar_init(pv_done, 1);
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      bar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_3d(qs, &qmap, q_full, 0, q0, head);
+      tma_load_3d(qs + HALF_BYTES, &qmap, q_full, 64, q0, head);
+      bool ok = true;
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int sk = j % KS;
+        if (!wait_bar(&k_empty[sk], ((j / KS) & 1) ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
+          ok = false;
+          break;
+        }
+        bar_arrive_expect_tx(&k_full[sk], TILE_BYTES);
+        tma_load_3d(ks + sk * TILE_BYTES, &kmap, &k_full[sk], 0, j * BKV, head);
+        tma_load_3d(ks + sk * TILE_BYTES + HALF_BYTES, &kmap, &k_full[sk], 64, j * BKV, head);
+        const int sv = j % VS;
+        if (!wait_bar(&v_empty[sv], ((j / VS) & 1) ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
+          ok = false;
+          break;
+        }
+        bar_arrive_expect_tx(&v_full[sv], TILE_BYTES);
+        tma_load_3d(vs + sv * TILE_BYTES, &vmap, &v_full[sv], 0, j * BKV, head);
+        tma_load_3d(vs + sv * TILE_BYTES + HALF_BYTES, &vmap, &v_full[sv], 64, j * BKV, head);
+      }
+      if (!ok) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 1000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = make_idesc_f16(BQ, BKV, 0, 0, 0);   // K-major A and B
+      constexpr uint32_t idesc_o = make_idesc_f16(BQ, HD, 0, 0, 1);    // B (V) MN-major
+      const uint32_t q_addr = smem_u32(qs);
+      bool ok = wait_bar(q_full, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA);
+      auto issue_s = [&](int j) -> bool {
+        const int sk = j % KS;
+        if (!wait_bar(&k_full[sk], (j / KS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
+          return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(ks + sk * TILE_BYTES);
+        const uint32_t d = tmem + S_COL + (j & 1) * BKV;
+#pragma unroll
+        for (int k16 = 0; k16 < HD / 16; ++k16) {
+          const uint32_t off = (k16 >> 2) * HALF_BYTES + (k16 & 3) * 32;
+          mma_ss(d, make_smem_desc(q_addr + off, 16, 1024), make_smem_desc(k_addr + off, 16, 1024),
+                 idesc_s, k16 > 0 ? 1u : 0u);
+        }
+        tc_commit(&k_empty[sk]);
+        tc_commit(&s_full[j & 1]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && nkv > 1) ok = issue_s(1);
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (!wait_bar(p_ready, j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) break;
+        const int sv = j % VS;
+        if (!wait_bar(&v_full[sv], (j / VS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(vs + sv * TILE_BYTES);
+#pragma unroll
+        for (int k16 = 0; k16 < BKV / 16; ++k16) {
+          // 16 keys per step: rows k16*16.. of both 64-dim halves (LBO = half stride).
+          mma_ts(tmem + O_COL, tmem + P_COL + k16 * 8,
+                 make_smem_desc(v_addr + k16 * 16 * 128, HALF_BYTES, 1024), idesc_o,
+                 (j > 0 || k16 > 0) ? 1u : 0u);
+        }
+        tc_commit(&v_empty[sv]);
+        tc_commit(pv_done);
+        if (j + 2 < nkv) ok = issue_s(j + 2);
+      }
+      tc_commit(drain);
+      const uint32_t da = smem_u32(drain);
+      const unsigned long long t0 = globaltimer_ns();
+      while (!bar_try_wait(da, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          if (p.err) atomicCAS(p.err, 0, DEV_ERR_TIMEOUT_MMA);
+          break;
+        }
+      }
+    }
+  } else {
+    // softmax warps 2..5
+    const int qd = warp & 3;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const int row = qd * 32 + (int)lane;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      bool good = wait_bar(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+      if (!__all_sync(0xffffffffu, good)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[BKV];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(tmem + lane_base + S_COL + (j & 1) * BKV + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+        }
+      }
+      const int kbase = j * BKV;
+      if (kbase + BKV > p.seq) {
+#pragma unroll
+        for (int c = 0; c < BKV; ++c)
+          if (kbase + c >= p.seq) s[c] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < BKV; ++c) mx = fmaxf(mx, s[c]);
+      mx *= p.scale_log2;
+      float alpha = 1.0f;
+      if (j == 0) {
+        m = mx;
+      } else if (mx > m + kRescaleThreshold) {
+        alpha = ex2(m - mx);
+        m = mx;
+      }
+      uint32_t pk[BKV / 2];
+      float rs = 0.0f;
+#pragma unroll
+      for (int c = 0; c < BKV / 2; ++c) {
+        const float a = ex2(fmaf(s[2 * c], p.scale_log2, -m));
+        const float b = ex2(fmaf(s[2 * c + 1], p.scale_log2, -m));
+        const __half2 h2 = __floats2half2_rn(a, b);
+        const float2 back = __half22float2(h2);
+        rs += back.x + back.y;
+        pk[c] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      l = l * alpha + rs;
+      if (j > 0) {
+        good = wait_bar(pv_done, (j - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+        if (!__all_sync(0xffffffffu, good)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_base + O_COL + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tmem + lane_base + O_COL + c * 32, r);
+          }
+        }
+      }
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = pk[i];
+        tmem_st32(tmem + lane_base + P_COL, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = pk[32 + i];
+        tmem_st32(tmem + lane_base + P_COL + 32, r);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(p_ready);
+    }
+    if (ok) {
+      const bool good = wait_bar(pv_done, (nkv - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+      if (__all_sync(0xffffffffu, good)) {
+        tc_fence_after();
+        const float inv_l = 1.0f / l;
+        const int q = q0 + row;
+        __half* dst = p.out + (size_t)q * p.ld_out + (size_t)head * HD;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + O_COL + c * 32, r);
+          tmem_wait_ld();
+          if (q < p.seq) {
+            uint32_t hv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const __half2 h2 = __floats2half2_rn(__uint_as_float(r[2 * i]) * inv_l,
+                                                   __uint_as_float(r[2 * i + 1]) * inv_l);
+              hv[i] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(hv[4 * i], hv[4 * i + 1], hv[4 * i + 2], hv[4 * i + 3]);
+          }
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace attn
+
+int encode_tmap_heads(CUtensorMap* map, const void* base, int n_heads, int seq, int head_dim);
+
+int launch_attention(const __half* q, const __half* k, const __half* v, int n_heads, int seq,
+                     int head_dim, float scale, __half* out, long long ld_out, cudaStream_t st) {
+  if (seq == 0 || n_heads == 0) return 0;
+  if (head_dim != attn::HD) return fail(-2, "attention: head_dim must be 128");
+  if (!q || !k || !v || !out) return fail(-1, "attention: null tensor");
+  if (seq < 0 || n_heads < 0) return fail(-1, "attention: negative shape");
+  if (ld_out < (long long)n_heads * head_dim || (ld_out % 8) != 0 ||
+      (reinterpret_cast<uintptr_t>(out) & 15) != 0)
+    return fail(-1, "attention: out must be 16-byte aligned with ld_out % 8 == 0 and >= heads*128");
+  CUtensorMap qm, km, vm;
+  int rc = encode_tmap_heads(&qm, q, n_heads, seq, head_dim);
+  if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim);
+  if (!rc) rc = encode_tmap_heads(&vm, v, n_heads, seq, head_dim);
+  if (rc) return rc;
+  attn::Params p{};
+  p.seq = seq;
+  p.n_heads = n_heads;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = out;
+  p.ld_out = ld_out;
+  p.err = device_error_word();
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn::attention_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         attn::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "attention set smem attribute");
+    attr = true;
+  }
+  dim3 grid((seq + attn::BQ - 1) / attn::BQ, n_heads);
+  attn::attention_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, st>>>(qm, km, vm, p);
+  return launch_status("attention_kernel launch");
+}
+
+}  // namespace bonsai

@@ -1,0 +1,645 @@
+// DiT engine: weights, workspace and the denoise-step forward of
+// build_diffuser_graph (src/diffuser_graph.cpp:231-561) on sm_100a kernels.
+//
+// Stage order per step (same tensors as the reference graph):
+//   edges      img_in / txt_in linears, timestep embedding -> time MLP (+ the
+//              pooled-vector MLP for Flux.1) -> vec, silu(vec) (:283-311)
+//   modulation all per-block (Flux.1, B1_0) or shared (klein, f32) modulation
+//              vectors computed once from silu(vec) (:307-320, :470-473)
+//   double     19/5 double blocks on the text and image rows (:341-466)
+//   single     38/20 single blocks on the joint rows (:476-542)
+//   head       LayerNorm-modulate + proj_out on the image rows (:544-556)
+// The hidden state is one f32 [txt + img][3072] buffer with the text rows
+// first, so the reference's ggml_concat(h_txt, h_img) (:468) is free.
+#include "../../include/bonsai_cuda.h"
+#include "internal.cuh"
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace bonsai {
+namespace dit {
+
+// ----------------------------------------------------------- weight RNG
+// Counter-based generator: every element is a pure function of
+// (seed, tensor id, element index), so tensors can be regenerated on demand.
+__host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+__host__ __device__ __forceinline__ uint64_t tensor_key(uint64_t seed, uint64_t tid) {
+  return splitmix64(seed * 0x100000001B3ull + splitmix64(tid));
+}
+__device__ __forceinline__ float normal_from(uint64_t r) {
+  const uint32_t a = (uint32_t)(r >> 32), b = (uint32_t)r;
+  const float u1 = ((float)a + 1.0f) * 2.3283064365386963e-10f;  // (0, 1]
+  const float u2 = (float)b * 2.3283064365386963e-10f;
+  return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+// Packed B1_0 bytes [rows][K/32][6]: signs Bernoulli(0.5), scale |N(0, std)| -> f16.
+__global__ void gen_b1_kernel(uint8_t* __restrict__ dst, long long groups, uint64_t key,
+                              float scale_std) {
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < groups;
+       g += (long long)gridDim.x * blockDim.x) {
+    const uint64_t r1 = splitmix64(key + 2 * (uint64_t)g);
+    const uint64_t r2 = splitmix64(key + 2 * (uint64_t)g + 1);
+    const uint32_t sign = (uint32_t)r1;
+    const __half s = __float2half_rn(fabsf(normal_from(r2)) * scale_std);
+    const uint16_t sb = __half_as_ushort(s);
+    uint8_t* p = dst + g * 6;
+    p[0] = (uint8_t)(sb & 0xFF);
+    p[1] = (uint8_t)(sb >> 8);
+    p[2] = (uint8_t)(sign & 0xFF);
+    p[3] = (uint8_t)((sign >> 8) & 0xFF);
+    p[4] = (uint8_t)((sign >> 16) & 0xFF);
+    p[5] = (uint8_t)(sign >> 24);
+  }
+}
+
+__global__ void gen_f32_kernel(float* __restrict__ dst, long long n, uint64_t key, float mean,
+                               float stdv) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    dst[i] = mean + stdv * normal_from(splitmix64(key + (uint64_t)i));
+}
+
+// --------------------------------------------------------------- config
+struct Cfg {
+  int preset = BONSAI_PRESET_FLUX1;
+  int H = 3072, heads = 24, hd = 128;
+  int depth = 19, depth_single = 38;
+  int mlp = 12288;          // activation width
+  int mlp_in_rows = 12288;  // rows of the MLP-in linear (2*mlp for SwiGLU)
+  int in_ch = 64, ctx_dim = 4096, pooled = 768;
+  int n_axes = 3;
+  int axes[4] = {16, 56, 56, 0};
+  float theta = 10000.f;
+  bool per_block_mod = true;
+  bool edge_bias = true;
+  bool swiglu = false;
+  int img = 4096, txt = 512, L = 4608;
+  int grid_h = 64, grid_w = 64;
+  uint64_t seed = 1234;
+  int C() const { return H + mlp; }  // width of the single block's to_out input
+};
+
+enum Kind { KIND_B1 = 0, KIND_F32 = 1 };
+struct TensorInfo {
+  Kind kind;
+  long long rows, cols;  // B1: out_dim, in_dim; F32: numel in rows*cols
+  uint64_t tid;
+  float mean, stdv;
+};
+
+struct DoubleW {
+  B1Weight img_qkv, txt_qkv, img_out, txt_out, img_mlp_in, img_mlp_out, txt_mlp_in, txt_mlp_out;
+  float *nq_img, *nk_img, *nq_txt, *nk_txt;
+};
+struct SingleW {
+  B1Weight proj, out;
+  float *nq, *nk;
+};
+
+}  // namespace dit
+}  // namespace bonsai
+
+using namespace bonsai;
+using namespace bonsai::dit;
+
+struct bonsai_dit {
+  Cfg c;
+  std::map<std::string, TensorInfo> reg;
+  std::vector<void*> allocs;
+  std::vector<DoubleW> dbl;
+  std::vector<SingleW> sgl;
+  B1Weight mod_all;  // Flux.1: every block's modulation linear stacked (rows)
+  long long mod_rows = 0;
+  // f32 edge weights
+  float *img_in_w = nullptr, *img_in_b = nullptr, *txt_in_w = nullptr, *txt_in_b = nullptr;
+  float *time_w1 = nullptr, *time_b1 = nullptr, *time_w2 = nullptr, *time_b2 = nullptr;
+  float *vec_w1 = nullptr, *vec_b1 = nullptr, *vec_w2 = nullptr, *vec_b2 = nullptr;
+  float *mod_img_w = nullptr, *mod_txt_w = nullptr, *mod_single_w = nullptr;
+  float *norm_out_w = nullptr, *norm_out_b = nullptr, *proj_out_w = nullptr, *proj_out_b = nullptr;
+  // workspace
+  float* hidden = nullptr;   // [L][H]
+  __half* xm = nullptr;      // [L][H]
+  __half* qkv = nullptr;     // [3][heads][L][128]
+  __half* cat = nullptr;     // [L][C]: attention out at [0,H), MLP activation at [H, H+mlp)
+  float* tmp32 = nullptr;    // [img][H] (final LayerNorm-modulate)
+  float* mods = nullptr;     // Flux.1: [mod_rows]; klein: [6H img | 6H txt | 3H single]
+  float* fin = nullptr;      // [2H] norm_out modulation
+  float* te = nullptr;       // [256] timestep embedding
+  float* h256 = nullptr;     // [H] time MLP hidden
+  float* vec = nullptr;      // [H]
+  float* vtmp = nullptr;     // [H]
+  float* vec_silu = nullptr; // [H]
+  __half* vec_silu16 = nullptr;  // [8][H] (row 0 used; padded for TMA)
+  float* cos_t = nullptr;    // [L][64]
+  float* sin_t = nullptr;
+  float* pinned_te = nullptr;  // host pinned [256]
+  // device copies of caller inputs for the host-buffer entry point
+  float *in_img = nullptr, *in_txt = nullptr, *in_pooled = nullptr, *out_buf = nullptr;
+};
+
+namespace {
+
+int dev_alloc(bonsai_dit* m, void** p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e != cudaSuccess) return fail(BONSAI_ERR_NOMEM, "dit: cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+  m->allocs.push_back(*p);
+  return 0;
+}
+
+
+int gen_b1_into(const Cfg& c, const TensorInfo& ti, uint8_t* dst, cudaStream_t st) {
+  const long long groups = ti.rows * (ti.cols / 32);
+  const long long blocks = std::min<long long>((groups + 255) / 256, 65535LL * 8);
+  gen_b1_kernel<<<(unsigned)std::max<long long>(blocks, 1), 256, 0, st>>>(
+      dst, groups, tensor_key(c.seed, ti.tid), ti.stdv);
+  return launch_status("gen_b1 launch");
+}
+int gen_f32_into(const Cfg& c, const TensorInfo& ti, float* dst, cudaStream_t st) {
+  const long long n = ti.rows * ti.cols;
+  const long long blocks = std::min<long long>((n + 255) / 256, 65535LL * 8);
+  gen_f32_kernel<<<(unsigned)std::max<long long>(blocks, 1), 256, 0, st>>>(
+      dst, n, tensor_key(c.seed, ti.tid), ti.mean, ti.stdv);
+  return launch_status("gen_f32 launch");
+}
+
+// Register and materialise one B1_0 weight (generated packed, then retiled).
+int make_b1(bonsai_dit* m, const std::string& name, long long rows, long long cols,
+            int swiglu_from, B1Weight& w, uint8_t* staging) {
+  TensorInfo ti{KIND_B1, rows, cols, (uint64_t)m->reg.size() + 1, 0.f, 0.02f};
+  m->reg[name] = ti;
+  int rc = gen_b1_into(m->c, ti, staging, 0);
+  if (rc) return rc;
+  w = B1Weight{};
+  w.n_rows = (int)rows;
+  w.k_in = (int)cols;
+  w.n_ftiles = (int)((rows + 127) / 128);
+  w.k_blocks = (int)((cols + 63) / 64);
+  w.swiglu_from = swiglu_from;
+  cudaGetDevice(&w.device);
+  rc = dev_alloc(m, reinterpret_cast<void**>(&w.chunks),
+                 (size_t)w.n_ftiles * w.k_blocks * kChunkWords * 4);
+  if (rc) return rc;
+  return launch_b1_retile(staging, w, 0);
+}
+
+int make_f32(bonsai_dit* m, const std::string& name, long long rows, long long cols, float mean,
+             float stdv, float** out) {
+  TensorInfo ti{KIND_F32, rows, cols, (uint64_t)m->reg.size() + 1, mean, stdv};
+  m->reg[name] = ti;
+  int rc = dev_alloc(m, reinterpret_cast<void**>(out), (size_t)rows * cols * 4);
+  if (rc) return rc;
+  return gen_f32_into(m->c, ti, *out, 0);
+}
+
+EpiSeg seg_of(int mode, int row_begin, int row_end, void* dst, long long ld, int col_off,
+              const float* gate) {
+  EpiSeg s;
+  s.mode = mode;
+  s.row_begin = row_begin;
+  s.row_end = row_end;
+  s.dst = dst;
+  s.ld = ld;
+  s.col_off = col_off;
+  s.gate = gate;
+  return s;
+}
+
+EpiSeg seg_qkv(const Cfg& c, int row_end, __half* qkv, int tok_off) {
+  EpiSeg s;
+  s.mode = EPI_QKV_F16;
+  s.row_begin = 0;
+  s.row_end = row_end;
+  s.dst = qkv;
+  s.heads = c.heads;
+  s.seq_total = c.L;
+  s.tok_off = tok_off;
+  s.head_dim = c.hd;
+  return s;
+}
+
+#define RC(x)              \
+  do {                     \
+    int _rc = (x);         \
+    if (_rc) return _rc;   \
+  } while (0)
+
+// Modulation vectors of double block i: (img, txt) pointers to [6H].
+void double_mods(bonsai_dit* m, int i, const float** mi, const float** mt) {
+  const Cfg& c = m->c;
+  if (c.per_block_mod) {
+    *mi = m->mods + (size_t)i * 12 * c.H;
+    *mt = *mi + 6 * c.H;
+  } else {
+    *mi = m->mods;
+    *mt = m->mods + 6 * c.H;
+  }
+}
+const float* single_mods(bonsai_dit* m, int i) {
+  const Cfg& c = m->c;
+  if (c.per_block_mod) return m->mods + (size_t)c.depth * 12 * c.H + (size_t)i * 3 * c.H;
+  return m->mods + 12 * c.H;
+}
+
+// silu(vec) -> every modulation vector + the output-head modulation.
+int compute_mods(bonsai_dit* m, cudaStream_t st) {
+  const Cfg& c = m->c;
+  RC(launch_silu_f32(m->vec, c.H, m->vec_silu, st));
+  if (c.per_block_mod) {
+    RC(launch_f32_to_f16(m->vec_silu, m->vec_silu16, c.H, st));
+    EpiSeg s = seg_of(EPI_F32, 0, (int)m->mod_rows, m->mods, m->mod_rows, 0, nullptr);
+    RC(launch_b1_gemm(m->vec_silu16, c.H, 1, m->mod_all, &s, 1, false, st));
+  } else {
+    RC(launch_linear_f32(m->vec_silu, c.H, 1, c.H, m->mod_img_w, nullptr, 6 * c.H, m->mods, 6 * c.H, false, st));
+    RC(launch_linear_f32(m->vec_silu, c.H, 1, c.H, m->mod_txt_w, nullptr, 6 * c.H, m->mods + 6 * c.H, 6 * c.H, false, st));
+    RC(launch_linear_f32(m->vec_silu, c.H, 1, c.H, m->mod_single_w, nullptr, 3 * c.H, m->mods + 12 * c.H, 3 * c.H, false, st));
+  }
+  return launch_linear_f32(m->vec_silu, c.H, 1, c.H, m->norm_out_w, m->norm_out_b, 2 * c.H, m->fin,
+                           2 * c.H, false, st);
+}
+
+int run_double(bonsai_dit* m, int i, cudaStream_t st) {
+  const Cfg& c = m->c;
+  const DoubleW& w = m->dbl[i];
+  const int H = c.H, Lt = c.txt, Li = c.img, C = c.C();
+  const float *mi, *mt;
+  double_mods(m, i, &mi, &mt);
+  float* h_txt = m->hidden;
+  float* h_img = m->hidden + (size_t)Lt * H;
+  __half* x_txt = m->xm;
+  __half* x_img = m->xm + (size_t)Lt * H;
+  __half* a_txt = m->cat;
+  __half* a_img = m->cat + (size_t)Lt * C;
+  // attention sub-block: LN-modulate (:347-352), Q/K/V (:354-369) scattered head-major
+  RC(launch_ln_modulate_f16(h_txt, Lt, H, mt + 0 * H, mt + 1 * H, 1e-6f, x_txt, H, st));
+  RC(launch_ln_modulate_f16(h_img, Li, H, mi + 0 * H, mi + 1 * H, 1e-6f, x_img, H, st));
+  EpiSeg s = seg_qkv(c, 3 * H, m->qkv, 0);
+  RC(launch_b1_gemm(x_txt, H, Lt, w.txt_qkv, &s, 1, false, st));
+  s = seg_qkv(c, 3 * H, m->qkv, Lt);
+  RC(launch_b1_gemm(x_img, H, Li, w.img_qkv, &s, 1, false, st));
+  // rms_norm_qk (:371-374) + RoPE (:383-384), text rows use the added-stream weights
+  __half* q = m->qkv;
+  __half* k = m->qkv + (size_t)c.heads * c.L * c.hd;
+  __half* v = k + (size_t)c.heads * c.L * c.hd;
+  RC(launch_qk_norm_rope(q, k, c.heads, c.L, w.nq_txt, w.nq_img, w.nk_txt, w.nk_img, Lt, 1e-6f,
+                         m->cos_t, m->sin_t, st));
+  // joint attention over [txt; img] (:393-416)
+  RC(launch_attention(q, k, v, c.heads, c.L, c.hd, 1.0f / sqrtf((float)c.hd), m->cat, C, st));
+  // out projections + gate-residual (:434-442)
+  s = seg_of(EPI_RESID_F32, 0, H, h_txt, H, 0, mt + 2 * H);
+  RC(launch_b1_gemm(a_txt, C, Lt, w.txt_out, &s, 1, false, st));
+  s = seg_of(EPI_RESID_F32, 0, H, h_img, H, 0, mi + 2 * H);
+  RC(launch_b1_gemm(a_img, C, Li, w.img_out, &s, 1, false, st));
+  // MLP sub-block (:444-460): activation written into cat[:, H:H+mlp]
+  RC(launch_ln_modulate_f16(h_txt, Lt, H, mt + 3 * H, mt + 4 * H, 1e-6f, x_txt, H, st));
+  RC(launch_ln_modulate_f16(h_img, Li, H, mi + 3 * H, mi + 4 * H, 1e-6f, x_img, H, st));
+  const int act_mode = c.swiglu ? EPI_SWIGLU_F16 : EPI_GELU_F16;
+  s = seg_of(act_mode, 0, c.mlp_in_rows, a_txt, C, H, nullptr);
+  RC(launch_b1_gemm(x_txt, H, Lt, w.txt_mlp_in, &s, 1, false, st));
+  s = seg_of(act_mode, 0, c.mlp_in_rows, a_img, C, H, nullptr);
+  RC(launch_b1_gemm(x_img, H, Li, w.img_mlp_in, &s, 1, false, st));
+  s = seg_of(EPI_RESID_F32, 0, H, h_txt, H, 0, mt + 5 * H);
+  RC(launch_b1_gemm(a_txt + H, C, Lt, w.txt_mlp_out, &s, 1, false, st));
+  s = seg_of(EPI_RESID_F32, 0, H, h_img, H, 0, mi + 5 * H);
+  RC(launch_b1_gemm(a_img + H, C, Li, w.img_mlp_out, &s, 1, false, st));
+  return 0;
+}
+
+int run_single(bonsai_dit* m, int i, cudaStream_t st) {
+  const Cfg& c = m->c;
+  const SingleW& w = m->sgl[i];
+  const int H = c.H, L = c.L, C = c.C();
+  const float* md = single_mods(m, i);
+  // LN-modulate (:479-480)
+  RC(launch_ln_modulate_f16(m->hidden, L, H, md, md + H, 1e-6f, m->xm, H, st));
+  // to_qkv_mlp_proj (:482-486): rows [0,3H) -> head-major Q/K/V, rest -> activation in cat
+  EpiSeg segs[2];
+  segs[0] = seg_qkv(c, 3 * H, m->qkv, 0);
+  segs[1] = seg_of(c.swiglu ? EPI_SWIGLU_F16 : EPI_GELU_F16, 3 * H, 3 * H + c.mlp_in_rows, m->cat,
+                   C, H, nullptr);
+  RC(launch_b1_gemm(m->xm, H, L, w.proj, segs, 2, false, st));
+  __half* q = m->qkv;
+  __half* k = m->qkv + (size_t)c.heads * L * c.hd;
+  __half* v = k + (size_t)c.heads * L * c.hd;
+  // rms_norm_qk + RoPE (:490-499), attention (:501-519) into cat[:, 0:H]
+  RC(launch_qk_norm_rope(q, k, c.heads, L, w.nq, w.nq, w.nk, w.nk, L, 1e-6f, m->cos_t, m->sin_t, st));
+  RC(launch_attention(q, k, v, c.heads, L, c.hd, 1.0f / sqrtf((float)c.hd), m->cat, C, st));
+  // to_out on concat(attn, mlp_act) + gate-residual (:533-538)
+  EpiSeg s = seg_of(EPI_RESID_F32, 0, H, m->hidden, H, 0, md + 2 * H);
+  return launch_b1_gemm(m->cat, C, L, w.out, &s, 1, false, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
+  if (!cfg || !out) return fail(BONSAI_ERR_ARG, "dit_create: null argument");
+  *out = nullptr;
+  std::unique_ptr<bonsai_dit> m(new bonsai_dit());
+  Cfg& c = m->c;
+  if (cfg->preset == BONSAI_PRESET_KLEIN4B) {
+    // DiffuserParams (src/diffuser_types.h:13-30)
+    c.preset = BONSAI_PRESET_KLEIN4B;
+    c.depth = 5;
+    c.depth_single = 20;
+    c.mlp = 9216;
+    c.mlp_in_rows = 2 * 9216;
+    c.in_ch = 128;
+    c.ctx_dim = 7680;
+    c.pooled = 0;
+    c.n_axes = 4;
+    c.axes[0] = c.axes[1] = c.axes[2] = c.axes[3] = 32;
+    c.theta = 2000.f;
+    c.per_block_mod = false;
+    c.edge_bias = false;
+    c.swiglu = true;
+  } else if (cfg->preset != BONSAI_PRESET_FLUX1) {
+    return fail(BONSAI_ERR_ARG, "dit_create: unknown preset");
+  }
+  if (cfg->depth > 0) c.depth = std::min(cfg->depth, c.depth);
+  if (cfg->depth_single > 0) c.depth_single = std::min(cfg->depth_single, c.depth_single);
+  if (cfg->depth < 0 || cfg->depth_single < 0) return fail(BONSAI_ERR_ARG, "dit_create: negative depth");
+  c.img = cfg->img_tokens;
+  c.txt = cfg->txt_tokens;
+  c.L = c.img + c.txt;
+  c.grid_h = cfg->grid_h;
+  c.grid_w = cfg->grid_w;
+  c.seed = cfg->seed;
+  if (c.img <= 0 || c.txt < 0 || c.grid_h * c.grid_w != c.img)
+    return fail(BONSAI_ERR_ARG, "dit_create: need img_tokens > 0 == grid_h * grid_w and txt_tokens >= 0");
+  const int H = c.H;
+  const long long L = c.L;
+  cudaStream_t st = 0;
+
+  // ---------------------------------------------------------- weights
+  long long max_rows = 3LL * H + c.mlp_in_rows;
+  long long max_cols = std::max<long long>(H, c.mlp) + H;
+  long long staging_bytes = max_rows * (max_cols / 32) * 6;
+  if (c.per_block_mod) {
+    m->mod_rows = (long long)c.depth * 12 * H + (long long)c.depth_single * 3 * H;
+    staging_bytes = std::max(staging_bytes, m->mod_rows * (H / 32) * 6);
+  }
+  uint8_t* staging = nullptr;
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&staging), (size_t)staging_bytes));
+  m->dbl.resize(c.depth);
+  m->sgl.resize(c.depth_single);
+  const int mlp_swiglu_from = c.swiglu ? 0 : -1;
+  for (int i = 0; i < c.depth; ++i) {
+    DoubleW& w = m->dbl[i];
+    const std::string p = "double." + std::to_string(i) + ".";
+    RC(make_b1(m.get(), p + "img_qkv", 3 * H, H, -1, w.img_qkv, staging));
+    RC(make_b1(m.get(), p + "txt_qkv", 3 * H, H, -1, w.txt_qkv, staging));
+    RC(make_b1(m.get(), p + "img_out", H, H, -1, w.img_out, staging));
+    RC(make_b1(m.get(), p + "txt_out", H, H, -1, w.txt_out, staging));
+    RC(make_b1(m.get(), p + "img_mlp_in", c.mlp_in_rows, H, mlp_swiglu_from, w.img_mlp_in, staging));
+    RC(make_b1(m.get(), p + "img_mlp_out", H, c.mlp, -1, w.img_mlp_out, staging));
+    RC(make_b1(m.get(), p + "txt_mlp_in", c.mlp_in_rows, H, mlp_swiglu_from, w.txt_mlp_in, staging));
+    RC(make_b1(m.get(), p + "txt_mlp_out", H, c.mlp, -1, w.txt_mlp_out, staging));
+    RC(make_f32(m.get(), p + "img_norm_q", 1, c.hd, 1.f, 0.1f, &w.nq_img));
+    RC(make_f32(m.get(), p + "img_norm_k", 1, c.hd, 1.f, 0.1f, &w.nk_img));
+    RC(make_f32(m.get(), p + "txt_norm_q", 1, c.hd, 1.f, 0.1f, &w.nq_txt));
+    RC(make_f32(m.get(), p + "txt_norm_k", 1, c.hd, 1.f, 0.1f, &w.nk_txt));
+  }
+  for (int i = 0; i < c.depth_single; ++i) {
+    SingleW& w = m->sgl[i];
+    const std::string p = "single." + std::to_string(i) + ".";
+    RC(make_b1(m.get(), p + "proj", 3 * H + c.mlp_in_rows, H, c.swiglu ? 3 * H : -1, w.proj, staging));
+    RC(make_b1(m.get(), p + "out", H, c.C(), -1, w.out, staging));
+    RC(make_f32(m.get(), p + "norm_q", 1, c.hd, 1.f, 0.1f, &w.nq));
+    RC(make_f32(m.get(), p + "norm_k", 1, c.hd, 1.f, 0.1f, &w.nk));
+  }
+  if (c.per_block_mod) {
+    // Flux.1 per-block modulation linears (B1_0: 2-D tensors under the block
+    // prefixes are quantized by convert_to_b1_0_packed.py:46-54), stacked so
+    // one GEMV launch produces every block's vectors.
+    long long row = 0;
+    for (int i = 0; i < c.depth; ++i)
+      for (const char* s : {"img_mod", "txt_mod"}) {
+        TensorInfo ti{KIND_B1, 6LL * H, H, (uint64_t)m->reg.size() + 1, 0.f, 0.02f};
+        m->reg["double." + std::to_string(i) + "." + s] = ti;
+        RC(gen_b1_into(c, ti, staging + row * (H / 32) * 6, st));
+        row += 6LL * H;
+      }
+    for (int i = 0; i < c.depth_single; ++i) {
+      TensorInfo ti{KIND_B1, 3LL * H, H, (uint64_t)m->reg.size() + 1, 0.f, 0.02f};
+      m->reg["single." + std::to_string(i) + ".mod"] = ti;
+      RC(gen_b1_into(c, ti, staging + row * (H / 32) * 6, st));
+      row += 3LL * H;
+    }
+    B1Weight& w = m->mod_all;
+    w.n_rows = (int)m->mod_rows;
+    w.k_in = H;
+    w.n_ftiles = (int)((m->mod_rows + 127) / 128);
+    w.k_blocks = (H + 63) / 64;
+    cudaGetDevice(&w.device);
+    RC(dev_alloc(m.get(), reinterpret_cast<void**>(&w.chunks),
+                 (size_t)w.n_ftiles * w.k_blocks * kChunkWords * 4));
+    RC(launch_b1_retile(staging, w, st));
+  } else {
+    RC(make_f32(m.get(), "mod_img.w", 6LL * H, H, 0.f, 0.02f, &m->mod_img_w));
+    RC(make_f32(m.get(), "mod_txt.w", 6LL * H, H, 0.f, 0.02f, &m->mod_txt_w));
+    RC(make_f32(m.get(), "mod_single.w", 3LL * H, H, 0.f, 0.02f, &m->mod_single_w));
+  }
+  const float bstd = c.edge_bias ? 0.02f : 0.f;
+  RC(make_f32(m.get(), "img_in.w", H, c.in_ch, 0.f, 0.02f, &m->img_in_w));
+  RC(make_f32(m.get(), "txt_in.w", H, c.ctx_dim, 0.f, 0.02f, &m->txt_in_w));
+  RC(make_f32(m.get(), "time.w1", H, 256, 0.f, 0.02f, &m->time_w1));
+  RC(make_f32(m.get(), "time.w2", H, H, 0.f, 0.02f, &m->time_w2));
+  RC(make_f32(m.get(), "norm_out.w", 2LL * H, H, 0.f, 0.02f, &m->norm_out_w));
+  RC(make_f32(m.get(), "proj_out.w", c.in_ch, H, 0.f, 0.02f, &m->proj_out_w));
+  if (c.edge_bias) {
+    RC(make_f32(m.get(), "img_in.b", 1, H, 0.f, bstd, &m->img_in_b));
+    RC(make_f32(m.get(), "txt_in.b", 1, H, 0.f, bstd, &m->txt_in_b));
+    RC(make_f32(m.get(), "time.b1", 1, H, 0.f, bstd, &m->time_b1));
+    RC(make_f32(m.get(), "time.b2", 1, H, 0.f, bstd, &m->time_b2));
+    RC(make_f32(m.get(), "norm_out.b", 1, 2 * H, 0.f, bstd, &m->norm_out_b));
+    RC(make_f32(m.get(), "proj_out.b", 1, c.in_ch, 0.f, bstd, &m->proj_out_b));
+  }
+  if (c.pooled > 0) {
+    RC(make_f32(m.get(), "vec.w1", H, c.pooled, 0.f, 0.02f, &m->vec_w1));
+    RC(make_f32(m.get(), "vec.b1", 1, H, 0.f, bstd, &m->vec_b1));
+    RC(make_f32(m.get(), "vec.w2", H, H, 0.f, 0.02f, &m->vec_w2));
+    RC(make_f32(m.get(), "vec.b2", 1, H, 0.f, bstd, &m->vec_b2));
+  }
+
+  // -------------------------------------------------------- workspace
+  const long long C = c.C();
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->hidden), (size_t)L * H * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->xm), (size_t)L * H * 2));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->qkv), (size_t)3 * c.heads * L * c.hd * 2));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->cat), (size_t)L * C * 2));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->tmp32), (size_t)c.img * H * 4));
+  const long long nmods = c.per_block_mod ? m->mod_rows : 15LL * H;
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->mods), (size_t)nmods * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->fin), (size_t)2 * H * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->te), 256 * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->h256), (size_t)H * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->vec), (size_t)H * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->vtmp), (size_t)H * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->vec_silu), (size_t)H * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->vec_silu16), (size_t)8 * H * 2));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->cos_t), (size_t)L * 64 * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->sin_t), (size_t)L * 64 * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->in_img), (size_t)c.img * c.in_ch * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->in_txt), (size_t)std::max(c.txt, 1) * c.ctx_dim * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->in_pooled), (size_t)std::max(c.pooled, 1) * 4));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->out_buf), (size_t)c.img * c.in_ch * 4));
+  if (cudaMallocHost(&m->pinned_te, 256 * 4) != cudaSuccess)
+    return fail(BONSAI_ERR_NOMEM, "dit_create: pinned allocation failed");
+  cudaMemset(m->vec_silu16, 0, (size_t)8 * H * 2);
+
+  // RoPE ids (src/diffuser.cpp:240-249): text rows 0, image rows (.., y, x)
+  // on the last two axes; tables built once (they do not change per step).
+  {
+    std::vector<float> ids((size_t)L * c.n_axes, 0.f);
+    for (int y = 0; y < c.grid_h; ++y)
+      for (int x = 0; x < c.grid_w; ++x) {
+        const size_t t = (size_t)c.txt + (size_t)y * c.grid_w + x;
+        ids[t * c.n_axes + c.n_axes - 2] = (float)y;
+        ids[t * c.n_axes + c.n_axes - 1] = (float)x;
+      }
+    float* ids_d = nullptr;
+    RC(dev_alloc(m.get(), reinterpret_cast<void**>(&ids_d), ids.size() * 4));
+    int half = 0;
+    for (int a = 0; a < c.n_axes; ++a) half += c.axes[a] / 2;
+    if (half != 64) return fail(BONSAI_ERR_UNSUPPORTED, "dit_create: RoPE axes must cover head_dim 128");
+    std::vector<int> pa(half);
+    std::vector<float> pf(half);
+    rope_pair_table(c.axes, c.n_axes, c.theta, pa.data(), pf.data());
+    int* tab = nullptr;
+    RC(dev_alloc(m.get(), reinterpret_cast<void**>(&tab), (size_t)half * 8));
+    RC(cuda_status(cudaMemcpy(ids_d, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice), "ids copy"));
+    RC(cuda_status(cudaMemcpy(tab, pa.data(), half * 4, cudaMemcpyHostToDevice), "rope table copy"));
+    RC(cuda_status(cudaMemcpy(tab + half, pf.data(), half * 4, cudaMemcpyHostToDevice), "rope table copy"));
+    RC(launch_rope_tables(ids_d, (int)L, c.n_axes, tab, reinterpret_cast<float*>(tab + half), half,
+                          m->cos_t, m->sin_t, st));
+  }
+  RC(cuda_status(cudaDeviceSynchronize(), "dit_create"));
+  *out = m.release();
+  return 0;
+}
+
+int bonsai_dit_destroy(bonsai_dit_t m) {
+  if (!m) return 0;
+  cudaDeviceSynchronize();
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->pinned_te) cudaFreeHost(m->pinned_te);
+  delete m;
+  return 0;
+}
+
+static int dit_prepare_vec(bonsai_dit* m, const float* pooled, float timestep, cudaStream_t st) {
+  const Cfg& c = m->c;
+  // ggml_timestep_embedding(t, 256, 10000) with the [sin, cos] half swap
+  // (src/diffuser_graph.cpp:288-292), evaluated on the host in f32.
+  for (int j = 0; j < 128; ++j) {
+    const float freq = expf(-logf(10000.0f) * (float)j / 128.0f);
+    const float arg = timestep * freq;
+    m->pinned_te[j] = sinf(arg);
+    m->pinned_te[128 + j] = cosf(arg);
+  }
+  RC(cuda_status(cudaMemcpyAsync(m->te, m->pinned_te, 256 * 4, cudaMemcpyHostToDevice, st), "te copy"));
+  // time MLP (:294-305): vec = W2 silu(W1 te + b1) + b2
+  RC(launch_linear_f32(m->te, 256, 1, 256, m->time_w1, m->time_b1, c.H, m->h256, c.H, false, st));
+  RC(launch_linear_f32(m->h256, c.H, 1, c.H, m->time_w2, m->time_b2, c.H, m->vec, c.H, true, st));
+  if (c.pooled > 0) {
+    if (!pooled) return fail(BONSAI_ERR_ARG, "dit_forward: the Flux.1 preset needs the pooled vector");
+    RC(launch_linear_f32(pooled, c.pooled, 1, c.pooled, m->vec_w1, m->vec_b1, c.H, m->h256, c.H, false, st));
+    RC(launch_linear_f32(m->h256, c.H, 1, c.H, m->vec_w2, m->vec_b2, c.H, m->vtmp, c.H, true, st));
+    RC(launch_add_f32(m->vec, m->vtmp, c.H, m->vec, st));
+  }
+  return compute_mods(m, st);
+}
+
+int bonsai_dit_forward(bonsai_dit_t m, const float* img, const float* txt, const float* pooled,
+                       float timestep, float* out, void* stream) {
+  if (!m || !img || !out || (m->c.txt > 0 && !txt)) return fail(BONSAI_ERR_ARG, "dit_forward: null argument");
+  const Cfg& c = m->c;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // input projections (:283-286), text rows first in the hidden state
+  RC(launch_linear_f32(txt, c.ctx_dim, c.txt, c.ctx_dim, m->txt_in_w, m->txt_in_b, c.H, m->hidden,
+                       c.H, false, st));
+  RC(launch_linear_f32(img, c.in_ch, c.img, c.in_ch, m->img_in_w, m->img_in_b, c.H,
+                       m->hidden + (size_t)c.txt * c.H, c.H, false, st));
+  RC(dit_prepare_vec(m, pooled, timestep, st));
+  for (int i = 0; i < c.depth; ++i) RC(run_double(m, i, st));
+  for (int i = 0; i < c.depth_single; ++i) RC(run_single(m, i, st));
+  // output head (:544-556): norm_out modulation is (scale, shift)
+  const float* h_img = m->hidden + (size_t)c.txt * c.H;
+  RC(launch_ln_modulate_f32(h_img, c.img, c.H, m->fin + c.H, m->fin, 1e-6f, m->tmp32, c.H, st));
+  return launch_linear_f32(m->tmp32, c.H, c.img, c.H, m->proj_out_w, m->proj_out_b, c.in_ch, out,
+                           c.in_ch, false, st);
+}
+
+int bonsai_dit_forward_host(bonsai_dit_t m, const float* host_img, const float* host_txt,
+                            const float* host_pooled, float timestep, float* host_out,
+                            void* stream) {
+  if (!m || !host_img || !host_out) return fail(BONSAI_ERR_ARG, "dit_forward_host: null argument");
+  const Cfg& c = m->c;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RC(cuda_status(cudaMemcpyAsync(m->in_img, host_img, (size_t)c.img * c.in_ch * 4, cudaMemcpyHostToDevice, st), "img copy"));
+  if (c.txt > 0)
+    RC(cuda_status(cudaMemcpyAsync(m->in_txt, host_txt, (size_t)c.txt * c.ctx_dim * 4, cudaMemcpyHostToDevice, st), "txt copy"));
+  if (c.pooled > 0 && host_pooled)
+    RC(cuda_status(cudaMemcpyAsync(m->in_pooled, host_pooled, (size_t)c.pooled * 4, cudaMemcpyHostToDevice, st), "pooled copy"));
+  RC(bonsai_dit_forward(m, m->in_img, m->in_txt, c.pooled > 0 ? m->in_pooled : nullptr, timestep,
+                        m->out_buf, stream));
+  RC(cuda_status(cudaMemcpyAsync(host_out, m->out_buf, (size_t)c.img * c.in_ch * 4, cudaMemcpyDeviceToHost, st), "out copy"));
+  return cuda_status(cudaStreamSynchronize(st), "dit_forward_host sync");
+}
+
+int bonsai_dit_set_state(bonsai_dit_t m, const float* hidden, const float* vec, void* stream) {
+  if (!m || !hidden || !vec) return fail(BONSAI_ERR_ARG, "dit_set_state: null argument");
+  const Cfg& c = m->c;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RC(cuda_status(cudaMemcpyAsync(m->hidden, hidden, (size_t)c.L * c.H * 4, cudaMemcpyDefault, st), "hidden copy"));
+  RC(cuda_status(cudaMemcpyAsync(m->vec, vec, (size_t)c.H * 4, cudaMemcpyDefault, st), "vec copy"));
+  return compute_mods(m, st);
+}
+
+int bonsai_dit_get_state(bonsai_dit_t m, float* hidden, void* stream) {
+  if (!m || !hidden) return fail(BONSAI_ERR_ARG, "dit_get_state: null argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RC(cuda_status(cudaMemcpyAsync(hidden, m->hidden, (size_t)m->c.L * m->c.H * 4, cudaMemcpyDefault, st), "hidden copy"));
+  return cuda_status(cudaStreamSynchronize(st), "dit_get_state sync");
+}
+
+int bonsai_dit_double_block(bonsai_dit_t m, int i, void* stream) {
+  if (!m || i < 0 || i >= m->c.depth) return fail(BONSAI_ERR_ARG, "dit_double_block: bad block index");
+  return run_double(m, i, static_cast<cudaStream_t>(stream));
+}
+
+int bonsai_dit_single_block(bonsai_dit_t m, int i, void* stream) {
+  if (!m || i < 0 || i >= m->c.depth_single) return fail(BONSAI_ERR_ARG, "dit_single_block: bad block index");
+  return run_single(m, i, static_cast<cudaStream_t>(stream));
+}
+
+long long bonsai_dit_weight(bonsai_dit_t m, const char* name, void* buf, long long cap) {
+  if (!m || !name) return fail(BONSAI_ERR_ARG, "dit_weight: null argument");
+  auto it = m->reg.find(name);
+  if (it == m->reg.end()) return fail(BONSAI_ERR_ARG, std::string("dit_weight: unknown tensor ") + name);
+  const TensorInfo& ti = it->second;
+  const long long bytes = ti.kind == KIND_B1 ? ti.rows * (ti.cols / 32) * 6 : ti.rows * ti.cols * 4;
+  if (!buf) return bytes;
+  if (cap < bytes) return fail(BONSAI_ERR_ARG, "dit_weight: buffer too small");
+  void* tmp = nullptr;
+  if (cudaMalloc(&tmp, bytes) != cudaSuccess) return fail(BONSAI_ERR_NOMEM, "dit_weight: staging allocation failed");
+  int rc = ti.kind == KIND_B1 ? gen_b1_into(m->c, ti, static_cast<uint8_t*>(tmp), 0)
+                              : gen_f32_into(m->c, ti, static_cast<float*>(tmp), 0);
+  if (!rc) rc = cuda_status(cudaMemcpy(buf, tmp, bytes, cudaMemcpyDeviceToHost), "dit_weight copy");
+  cudaFree(tmp);
+  return rc ? rc : bytes;
+}
+
+}  // extern "C"

@@ -1,0 +1,141 @@
+// Edge ops of the step that sit outside the B1_0 path: the f32 dense
+// linears of the embedders, time / vector MLPs, shared modulation and the
+// output head (ggml_mul_mat with f32 weights, src/diffuser_graph.cpp:283-320,
+// :544-556), plus small elementwise helpers.  They are < 1% of the step's
+// FLOPs; the dense linear is a plain SIMT tiled kernel (f32 accumulate).
+#include "internal.cuh"
+
+#include <algorithm>
+
+namespace bonsai {
+namespace edge {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// y[o] = sum_i W[o][i] x[i] (+ b[o]); one warp per output row (coalesced W).
+__global__ void gemv_kernel(const float* __restrict__ x, const float* __restrict__ W,
+                            const float* __restrict__ b, int K, int N, float* __restrict__ y,
+                            int act_silu_in) {
+  const int warps = blockDim.x / 32;
+  const int o = blockIdx.x * warps + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (o >= N) return;
+  const float* wr = W + (size_t)o * K;
+  float s = 0.f;
+  if ((K & 3) == 0) {
+    const float4* w4 = reinterpret_cast<const float4*>(wr);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int i = lane; i < K / 4; i += 32) {
+      const float4 a = w4[i];
+      float4 v = x4[i];
+      if (act_silu_in) {
+        v.x = v.x / (1.f + expf(-v.x)); v.y = v.y / (1.f + expf(-v.y));
+        v.z = v.z / (1.f + expf(-v.z)); v.w = v.w / (1.f + expf(-v.w));
+      }
+      s += (a.x * v.x + a.y * v.y) + (a.z * v.z + a.w * v.w);
+    }
+  } else {
+    for (int i = lane; i < K; i += 32) {
+      float v = x[i];
+      if (act_silu_in) v = v / (1.f + expf(-v));
+      s += wr[i] * v;
+    }
+  }
+  s = warp_sum(s);
+  if (lane == 0) y[o] = s + (b ? b[o] : 0.f);
+}
+
+// Tiled y[t][o] = sum_i W[o][i] x[t][i] (+ b[o]); 64 x 64 tile, 4 x 4 per thread.
+constexpr int TB = 64, TK = 16;
+__global__ void __launch_bounds__(256) linear_kernel(const float* __restrict__ x, long long ldx,
+                                                     int T, int K, const float* __restrict__ W,
+                                                     const float* __restrict__ b, int N,
+                                                     float* __restrict__ y, long long ldy) {
+  __shared__ float xs[TK][TB + 4];
+  __shared__ float ws[TK][TB + 4];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int t0 = blockIdx.y * TB, o0 = blockIdx.x * TB;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += TK) {
+    for (int i = threadIdx.x; i < TB * TK; i += 256) {
+      const int r = i / TK, c = i % TK;
+      const int t = t0 + r, o = o0 + r, kk = k0 + c;
+      xs[c][r] = (t < T && kk < K) ? x[(size_t)t * ldx + kk] : 0.f;
+      ws[c][r] = (o < N && kk < K) ? W[(size_t)o * K + kk] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < TK; ++c) {
+      float xv[4], wv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        xv[i] = xs[c][ty * 4 + i];
+        wv[i] = ws[c][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] += xv[i] * wv[j];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + ty * 4 + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int o = o0 + tx * 4 + j;
+      if (o < N) y[(size_t)t * ldy + o] = acc[i][j] + (b ? b[o] : 0.f);
+    }
+  }
+}
+
+__global__ void silu_kernel(const float* __restrict__ x, long long n, float* __restrict__ y) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = x[i] / (1.f + expf(-x[i]));
+}
+
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, long long n,
+                           float* __restrict__ y) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = a[i] + b[i];
+}
+
+}  // namespace edge
+
+int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* W, const float* b,
+                      int N, float* y, long long ldy, bool silu_in, cudaStream_t st) {
+  if (T == 0 || N == 0) return 0;
+  if (T == 1) {
+    const int wpb = 8;
+    edge::gemv_kernel<<<(N + wpb - 1) / wpb, wpb * 32, 0, st>>>(x, W, b, K, N, y, silu_in ? 1 : 0);
+    return launch_status("gemv launch");
+  }
+  if (silu_in) return fail(-2, "linear_f32: silu input only supported for T == 1");
+  dim3 grid((N + edge::TB - 1) / edge::TB, (T + edge::TB - 1) / edge::TB);
+  edge::linear_kernel<<<grid, 256, 0, st>>>(x, ldx, T, K, W, b, N, y, ldy);
+  return launch_status("linear_f32 launch");
+}
+
+int launch_silu_f32(const float* x, long long n, float* y, cudaStream_t st) {
+  if (n == 0) return 0;
+  const long long blocks = std::min<long long>((n + 255) / 256, 4096);
+  edge::silu_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, n, y);
+  return launch_status("silu launch");
+}
+
+int launch_add_f32(const float* a, const float* b, long long n, float* y, cudaStream_t st) {
+  if (n == 0) return 0;
+  const long long blocks = std::min<long long>((n + 255) / 256, 4096);
+  edge::add_kernel<<<(unsigned)blocks, 256, 0, st>>>(a, b, n, y);
+  return launch_status("add launch");
+}
+
+}  // namespace bonsai

@@ -70,7 +70,39 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w,
 // Retile packed reference bytes (device copy) into the chunked layout.
 int launch_b1_retile(const uint8_t* dev_packed, B1Weight& w, cudaStream_t st);
 
-// ------------------------------------------------------------ elementwise
+// ------------------------------------------------------------- attention
+// q, k, v: f16 [n_heads][seq][128]; out: f16 [seq][ld_out], head h at columns h*128.
+int launch_attention(const __half* q, const __half* k, const __half* v, int n_heads, int seq,
+                     int head_dim, float scale, __half* out, long long ld_out, cudaStream_t st);
+
+// ------------------------------------------------------------ pointwise
 int launch_f32_to_f16(const float* src, __half* dst, long long n, cudaStream_t st);
+int launch_ln_modulate_f16(const float* x, int rows, int dim, const float* shift,
+                           const float* scale, float eps, __half* y, long long ld_y,
+                           cudaStream_t st);
+int launch_ln_modulate_f32(const float* x, int rows, int dim, const float* shift,
+                           const float* scale, float eps, float* y, long long ld_y,
+                           cudaStream_t st);
+// q and k head-major [n_heads][seq][128] f16, in place (k may be null).
+int launch_qk_norm_rope(__half* q, __half* k, int n_heads, int seq, const float* wq_lo,
+                        const float* wq_hi, const float* wk_lo, const float* wk_hi, int split,
+                        float eps, const float* cos_t, const float* sin_t, cudaStream_t st);
+int launch_rope_2d_f32(const float* x, const float* c, const float* s, int head_dim, int n_heads,
+                       int seq, float* out, cudaStream_t st);
+int launch_rms_norm_f32(const float* x, const float* w, int rows, int dim, float eps, float* y,
+                        cudaStream_t st);
+int launch_rope_tables(const float* ids, int seq, int n_axes, const int* pair_axis_dev,
+                       const float* pair_freq_dev, int half, float* cos_out, float* sin_out,
+                       cudaStream_t st);
+// Host-side pair -> (axis, frequency) map of compute_rope_freqs_data
+// (src/diffuser_graph.cpp:126-140) with the axes concatenated in order.
+void rope_pair_table(const int* axes_dim, int n_axes, float theta, int* pair_axis,
+                     float* pair_freq);
+
+// ------------------------------------------------------------ edge ops
+int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* W, const float* b,
+                      int N, float* y, long long ldy, bool silu_in, cudaStream_t st);
+int launch_silu_f32(const float* x, long long n, float* y, cudaStream_t st);
+int launch_add_f32(const float* a, const float* b, long long n, float* y, cudaStream_t st);
 
 }  // namespace bonsai

@@ -77,6 +77,30 @@ ORC_EXPORT void orc_b1_linear(const float* act, int tokens, int in_dim, const ui
   }
 }
 
+/* The B1_0 linear used inside the oracle's blocks.  By default the C
+ * restatement above; orc_use_reference_b1() swaps in the reference's own
+ * b1_linear_f32_f32 (oracle/_ref, AVX2 build) so a block runs the
+ * reference's exact kernel for every linear. */
+typedef void (*ref_b1_fn)(const float*, int, int, const uint8_t*, int, float*, int);
+static ref_b1_fn g_ref_b1 = 0;
+static int g_ref_threads = 1;
+ORC_EXPORT void orc_use_reference_b1(void* fn, int nthreads) {
+  g_ref_b1 = (ref_b1_fn)fn;
+  g_ref_threads = nthreads > 0 ? nthreads : 1;
+}
+static void block_b1(const float* act, int tokens, int in_dim, const uint8_t* w, int out_dim,
+                     float* out) {
+  if (g_ref_b1)
+    g_ref_b1(act, tokens, in_dim, w, out_dim, out, g_ref_threads);
+  else
+    orc_b1_linear(act, tokens, in_dim, w, out_dim, out);
+}
+
+/* Attention input rounding: 1 (default) rounds q, k, v to f16 as the
+ * reference's graph does; 0 gives the fp32 dequantised-weight oracle. */
+static int g_attn_f16 = 1;
+ORC_EXPORT void orc_set_attention_f16(int on) { g_attn_f16 = on; }
+
 /* Dense f32 linear, ggml_mul_mat(W, x) with W [out][in] (src/diffuser_graph.cpp:283-311):
  * y[t][o] = sum_i W[o][i] * x[t][i] (+ bias[o] when given). */
 ORC_EXPORT void orc_linear_f32(const float* x, int tokens, int in_dim, const float* W,
@@ -228,9 +252,9 @@ ORC_EXPORT void orc_attention(const float* q, const float* k, const float* v, in
   float* k16 = (float*)malloc(n * sizeof(float));
   float* v16 = (float*)malloc(n * sizeof(float));
   for (size_t i = 0; i < n; ++i) {
-    q16[i] = round_f16(q[i]);
-    k16[i] = round_f16(k[i]);
-    v16[i] = round_f16(v[i]);
+    q16[i] = g_attn_f16 ? round_f16(q[i]) : q[i];
+    k16[i] = g_attn_f16 ? round_f16(k[i]) : k[i];
+    v16[i] = g_attn_f16 ? round_f16(v[i]) : v[i];
   }
 #pragma omp parallel
   {
@@ -319,6 +343,30 @@ static void qk_norm_rope(float* qkv, int L, const orc_dims* D, const float* wq_l
   }
 }
 
+/* Exported form of the fused Q/K RMSNorm + RoPE for head-major tensors:
+ * x f32 [n_heads][seq][hd] in place; tokens < split use w_lo else w_hi. */
+ORC_EXPORT void orc_qk_norm_rope_heads(float* x, int n_heads, int seq, int hd, const float* w_lo,
+                                       const float* w_hi, int split, float eps,
+                                       const float* cos_t, const float* sin_t) {
+  const int half = hd / 2;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int h = 0; h < n_heads; ++h)
+    for (int t = 0; t < seq; ++t) {
+      float* r = x + ((size_t)h * seq + t) * hd;
+      const float* w = t < split ? w_lo : w_hi;
+      double s2 = 0.0;
+      for (int i = 0; i < hd; ++i) s2 += (double)r[i] * r[i];
+      const float sc = 1.0f / sqrtf((float)(s2 / hd) + eps);
+      float tmp[512];
+      for (int i = 0; i < hd; ++i) tmp[i] = (r[i] * sc) * w[i];
+      for (int d = 0; d < half; ++d) {
+        const float cv = cos_t[(size_t)t * half + d], sv = sin_t[(size_t)t * half + d];
+        r[2 * d] = tmp[2 * d] * cv - tmp[2 * d + 1] * sv;
+        r[2 * d + 1] = tmp[2 * d] * sv + tmp[2 * d + 1] * cv;
+      }
+    }
+}
+
 /* Split a [L][3H] qkv buffer into q, k, v [L][H] (head-interleaved rows). */
 static void split3(const float* qkv, int L, int H, float* q, float* k, float* v) {
   for (int t = 0; t < L; ++t) {
@@ -370,7 +418,7 @@ ORC_EXPORT void orc_double_block(const orc_dims* D, int L_txt, int L_img, float*
     const float* m = mods[sidx];
     orc_ln_modulate(hs[sidx], Ls[sidx], H, m + 0 * H, m + 1 * H, 1e-6f,
                     xm + (size_t)offs[sidx] * H);
-    orc_b1_linear(xm + (size_t)offs[sidx] * H, Ls[sidx], H, wqkv[sidx], 3 * H,
+    block_b1(xm + (size_t)offs[sidx] * H, Ls[sidx], H, wqkv[sidx], 3 * H,
                   qkv + (size_t)offs[sidx] * 3 * H);
   }
   /* rms_norm_qk (:371-374) with per-stream weights, RoPE (:383-384) */
@@ -381,17 +429,17 @@ ORC_EXPORT void orc_double_block(const orc_dims* D, int L_txt, int L_img, float*
   for (int sidx = 0; sidx < 2; ++sidx) {
     const float* m = mods[sidx];
     /* out projections (:434-437) and gate-residual (:440-442) */
-    orc_b1_linear(att + (size_t)offs[sidx] * H, Ls[sidx], H, wout[sidx], H, y);
+    block_b1(att + (size_t)offs[sidx] * H, Ls[sidx], H, wout[sidx], H, y);
     for (int t = 0; t < Ls[sidx]; ++t)
       for (int i = 0; i < H; ++i) hs[sidx][(size_t)t * H + i] += m[2 * H + i] * y[(size_t)t * H + i];
     /* MLP sub-block (:444-460) */
     orc_ln_modulate(hs[sidx], Ls[sidx], H, m + 3 * H, m + 4 * H, 1e-6f, xm);
-    orc_b1_linear(xm, Ls[sidx], H, wmi[sidx], mlp_in_rows, mi);
+    block_b1(xm, Ls[sidx], H, wmi[sidx], mlp_in_rows, mi);
     if (D->preset == 0)
       orc_swiglu(mi, Ls[sidx], D->mlp, ma, D->mlp);
     else
       orc_gelu(mi, Ls[sidx], D->mlp, ma, D->mlp);
-    orc_b1_linear(ma, Ls[sidx], D->mlp, wmo[sidx], H, y);
+    block_b1(ma, Ls[sidx], D->mlp, wmo[sidx], H, y);
     for (int t = 0; t < Ls[sidx]; ++t)
       for (int i = 0; i < H; ++i) hs[sidx][(size_t)t * H + i] += m[5 * H + i] * y[(size_t)t * H + i];
   }
@@ -421,7 +469,7 @@ ORC_EXPORT void orc_single_block(const orc_dims* D, int L, float* h, const float
   float* att = (float*)malloc(sizeof(float) * (size_t)L * H);
   float* y = (float*)malloc(sizeof(float) * (size_t)L * H);
   orc_ln_modulate(h, L, H, mod + 0, mod + H, 1e-6f, xm); /* :479-480 */
-  orc_b1_linear(xm, L, H, w_proj, P, proj);               /* :482 */
+  block_b1(xm, L, H, w_proj, P, proj);               /* :482 */
   for (int t = 0; t < L; ++t) {                            /* views :484-486 */
     memcpy(qkv + (size_t)t * 3 * H, proj + (size_t)t * P, sizeof(float) * 3 * H);
     memcpy(mi + (size_t)t * mlp_in_rows, proj + (size_t)t * P + 3 * H, sizeof(float) * mlp_in_rows);
@@ -434,7 +482,7 @@ ORC_EXPORT void orc_single_block(const orc_dims* D, int L, float* h, const float
     orc_swiglu(mi, L, D->mlp, cat + H, C);
   else
     orc_gelu(mi, L, D->mlp, cat + H, C);
-  orc_b1_linear(cat, L, C, w_out, H, y); /* :536 */
+  block_b1(cat, L, C, w_out, H, y); /* :536 */
   for (int t = 0; t < L; ++t)           /* :538 */
     for (int i = 0; i < H; ++i) h[(size_t)t * H + i] += mod[2 * H + i] * y[(size_t)t * H + i];
   free(xm); free(proj); free(qkv); free(mi); free(q); free(k); free(v); free(cat); free(att); free(y);
