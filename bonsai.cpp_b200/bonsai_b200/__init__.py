@@ -43,6 +43,8 @@ SIGNATURES = {
     "bonsai_init": (_c_int, [_c_int]),
     "bonsai_device_error": (_c_int, []),
     "bonsai_launch_count": (_c_ll, []),
+    "bonsai_profile_start": (_c_int, []),
+    "bonsai_profile_stop": (_c_int, [ctypes.c_char_p, _c_int]),
     "bonsai_b1_upload": (_c_int, [_vp, _c_int, _c_int, _c_int, ctypes.POINTER(_vp)]),
     "bonsai_b1_free": (_c_int, [_vp]),
     "bonsai_b1_shape": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
@@ -116,6 +118,19 @@ def device_error() -> int:
 
 def launch_count() -> int:
     return int(lib().bonsai_launch_count())
+
+
+def profile_start() -> None:
+    check(lib().bonsai_profile_start(), "bonsai_profile_start")
+
+
+def profile_stop() -> dict:
+    import json
+    buf = ctypes.create_string_buffer(1 << 16)
+    n = lib().bonsai_profile_stop(buf, len(buf))
+    if n < 0:
+        check(n, "bonsai_profile_stop")
+    return json.loads(buf.value.decode())
 
 
 class B1Weight:

@@ -6,6 +6,8 @@
 
 #include <cuda_fp16.h>
 #include <algorithm>
+#include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -93,6 +95,32 @@ int launch_status(const char* what) {
   g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
   return BONSAI_ERR_CUDA;
 }
+// ------------------------------------------------------------ profiling
+// When enabled, each launch site brackets its kernel with two CUDA events
+// recorded on the launching stream and logs the algorithmic work of the
+// launch; bonsai_profile_stop() turns that into per-kernel totals.
+namespace {
+struct ProfRec {
+  const char* kind;
+  cudaEvent_t e0, e1;
+  double flop, bytes;
+};
+thread_local bool g_prof_on = false;
+thread_local std::vector<ProfRec> g_prof;
+}  // namespace
+
+ProfScope::ProfScope(const char* kind, double flop, double bytes, cudaStream_t st) : st_(st) {
+  if (!g_prof_on) return;
+  ProfRec r{kind, nullptr, nullptr, flop, bytes};
+  if (cudaEventCreate(&r.e0) != cudaSuccess || cudaEventCreate(&r.e1) != cudaSuccess) return;
+  cudaEventRecord(r.e0, st);
+  g_prof.push_back(r);
+  idx_ = (long long)g_prof.size() - 1;
+}
+ProfScope::~ProfScope() {
+  if (idx_ >= 0 && idx_ < (long long)g_prof.size()) cudaEventRecord(g_prof[idx_].e1, st_);
+}
+
 int* device_error_word() { return dev_info().err_word; }
 int num_sms() { return dev_info().sms; }
 
@@ -142,6 +170,58 @@ int bonsai_init(int device) {
   dev_info();
   g_last_error.clear();
   return 0;
+}
+
+int bonsai_profile_start(void) {
+  for (auto& r : g_prof) {
+    cudaEventDestroy(r.e0);
+    cudaEventDestroy(r.e1);
+  }
+  g_prof.clear();
+  g_prof_on = true;
+  return 0;
+}
+
+int bonsai_profile_stop(char* json, int cap) {
+  g_prof_on = false;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "profile sync");
+  struct Acc {
+    long long n = 0;
+    double ms = 0, flop = 0, bytes = 0;
+  };
+  std::vector<std::pair<std::string, Acc>> acc;
+  for (auto& r : g_prof) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.e0, r.e1);
+    auto it = std::find_if(acc.begin(), acc.end(), [&](auto& a) { return a.first == r.kind; });
+    if (it == acc.end()) {
+      acc.push_back({r.kind, Acc{}});
+      it = acc.end() - 1;
+    }
+    it->second.n += 1;
+    it->second.ms += ms;
+    it->second.flop += r.flop;
+    it->second.bytes += r.bytes;
+    cudaEventDestroy(r.e0);
+    cudaEventDestroy(r.e1);
+  }
+  g_prof.clear();
+  std::string out = "{";
+  for (size_t i = 0; i < acc.size(); ++i) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "%s\"%s\": {\"launches\": %lld, \"ms\": %.6f, \"flop\": %.6e, \"bytes\": %.6e}",
+             i ? ", " : "", acc[i].first.c_str(), acc[i].second.n, acc[i].second.ms,
+             acc[i].second.flop, acc[i].second.bytes);
+    out += buf;
+  }
+  out += "}";
+  if (json && cap > 0) {
+    const size_t n = std::min<size_t>(out.size(), (size_t)cap - 1);
+    memcpy(json, out.data(), n);
+    json[n] = 0;
+  }
+  return (int)out.size();
 }
 
 int bonsai_device_error(void) {

@@ -352,6 +352,8 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
     attr = true;
   }
   dim3 grid((seq + attn::BQ - 1) / attn::BQ, n_heads);
+  ProfScope prof("attention", 4.0 * (double)seq * seq * head_dim * n_heads,
+                 4.0 * (double)seq * n_heads * head_dim * 2, st);
   attn::attention_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, st>>>(qm, km, vm, p);
   return launch_status("attention_kernel launch");
 }

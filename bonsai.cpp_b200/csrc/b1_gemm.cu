@@ -487,6 +487,15 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
     if (e != cudaSuccess) return cuda_status(e, "b1_gemm set smem attribute");
     attr_set[x_bf16 ? 1 : 0] = true;
   }
+  double out_bytes = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const double rows = segs[i].row_end - segs[i].row_begin;
+    const int m = segs[i].mode;
+    const double per = (m == EPI_F32) ? 4 : (m == EPI_RESID_F32) ? 8 : (m == EPI_SWIGLU_F16) ? 1 : 2;
+    out_bytes += rows * tokens * per;
+  }
+  ProfScope prof("b1_gemm", 2.0 * tokens * w.n_rows * (double)w.k_in,
+                 (double)tokens * w.k_in * 2 + (double)w.n_rows * w.k_in * 6 / 32 + out_bytes, st);
   kern<<<grid, gemm::NUM_THREADS, gemm::SMEM_BYTES, st>>>(xmap, p);
   return launch_status("b1_gemm_kernel launch");
 }

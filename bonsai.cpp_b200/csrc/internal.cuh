@@ -15,6 +15,16 @@ void set_error(const std::string& msg);  // stores the message for bonsai_last_e
 int fail(int code, const std::string& msg);  // set_error + return code
 int cuda_status(cudaError_t e, const char* what);  // 0 or BONSAI_ERR_CUDA
 int launch_status(const char* what);  // checks cudaGetLastError() and counts the launch
+// RAII per-launch timer used by bonsai_profile_start/stop: records a CUDA
+// event before and after the launch on its stream when profiling is on.
+class ProfScope {
+ public:
+  ProfScope(const char* kind, double flop, double bytes, cudaStream_t st);
+  ~ProfScope();
+ private:
+  cudaStream_t st_;
+  long long idx_ = -1;
+};
 int* device_error_word();  // device address of the per-device error word (lazily resolved)
 int num_sms();
 

@@ -214,6 +214,7 @@ static int ln_mod_impl(const float* x, int rows, int dim, const float* shift, co
                      reinterpret_cast<uintptr_t>(scale)) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(y) & (sizeof(OutT) == 2 ? 7 : 15)) == 0;
   const int n4 = dim / 4;
+  ProfScope prof("ln_modulate", 0.0, (double)rows * dim * (4 + sizeof(OutT)), st);
   if (vec && n4 <= 24 * 32)
     pw::ln_modulate_kernel<24, OutT><<<row_grid(rows, wpb), wpb * 32, 0, st>>>(x, rows, dim, shift, scale, eps, y, ld_y);
   else if (vec && n4 <= 48 * 32)
@@ -242,6 +243,7 @@ int launch_qk_norm_rope(__half* q, __half* k, int n_heads, int seq, const float*
     return fail(-1, "qk_norm_rope: null argument");
   const long long rows = (long long)n_heads * seq * (k ? 2 : 1);
   const int wpb = 8;
+  ProfScope prof("qk_norm_rope", 0.0, (double)rows * 128 * 4, st);
   pw::qk_norm_rope_kernel<<<row_grid(rows, wpb), wpb * 32, 0, st>>>(
       q, k, n_heads, seq, wq_lo, wq_hi, wk_lo, wk_hi, split, eps, cos_t, sin_t);
   return launch_status("qk_norm_rope launch");

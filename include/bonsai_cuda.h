@@ -70,6 +70,14 @@ int bonsai_device_error(void);
  * since the last call (launch accounting for benchmarks); resets to 0. */
 long long bonsai_launch_count(void);
 
+/* Per-kernel timing for benchmarks and tracing: between start and stop,
+ * every launch of the library is bracketed by two CUDA events recorded on
+ * its own stream.  stop synchronises the device and writes a JSON object
+ * {kernel: {"launches", "ms", "flop", "bytes"}} (algorithmic work) into
+ * json (truncated to cap); it returns the full length.  Per thread. */
+int bonsai_profile_start(void);
+int bonsai_profile_stop(char* json, int cap);
+
 /* ------------------------------------------------------ B1_0 weights */
 
 typedef struct bonsai_b1_weight* bonsai_b1_t;
