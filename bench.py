@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""Benchmark: ms per 1024^2 Flux.1-schnell denoise step on B200.
+
+Workload (one image per GPU): 19 double + 38 single
+blocks, hidden 3072, 24 x 128 heads, GELU MLP 12288, 4096 image tokens
+(16-ch 128x128 latent, 2x2-packed) + 512 text tokens, pooled [768]; every
+block linear (QKV, out-proj, MLP, per-block modulation) is B1_0 with
+random-init weights (signs Bernoulli(0.5), scales |N(0,0.02)| as f16);
+synthetic N(0,1) inputs.  A "step" is one transformer forward
+(bonsai_dit_forward) at timestep t = 1000 * (1 - i/steps).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl bonsai|reference]
+
+N > 1 runs under torch.distributed.run, one rank per GPU, each rank its own
+image (data parallel, no collective on the data path; weak scaling).
+--impl reference times the reference's own CPU path (its b1_linear_f32_f32
+AVX2 kernel compiled into oracle/_ref, plus the CPU restatement of the
+ggml built-ins) on a bounded sample and extrapolates to ms per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "bonsai.cpp_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np
+
+H, HEADS, HD = 3072, 24, 128
+MLP = 12288
+IMG, TXT, GRID, POOLED, IN_CH, CTX = 4096, 512, 64, 768, 64, 4096
+DEPTH, SINGLE = 19, 38
+L = IMG + TXT
+METRIC = "ms/denoise step @1024² Flux-DiT (1–8 B200); B1_0 GEMM & attn % of bf16 peak"
+WORKLOAD = ("flux1-schnell DiT denoise step @1024^2: 19 double + 38 single blocks, "
+            "L = 512 text + 4096 image tokens, all block linears B1_0 (1-bit)")
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"],
+                "bf16_sustained": d["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def step_flops():
+    """Algorithmic FLOPs of one step (GEMM 2*M*N*K, attention 4*L^2*D*H)."""
+    attn = 4.0 * L * L * HD * HEADS
+    dbl = 2.0 * L * H * (3 * H + H + MLP) + 2.0 * L * MLP * H + attn
+    sgl = 2.0 * L * H * (3 * H + MLP) + 2.0 * L * (H + MLP) * H + attn
+    mods = 2.0 * H * (DEPTH * 12 * H + SINGLE * 3 * H)
+    edges = 2.0 * (TXT * CTX * H + IMG * IN_CH * H + IMG * H * IN_CH + 256 * H + 2 * H * H
+                   + POOLED * H + 2 * H * H)
+    return DEPTH * dbl + SINGLE * sgl + mods + edges
+
+
+# ------------------------------------------------------------ CPU reference
+class CpuSample:
+    """Bounded sample of the reference CPU path at the bench workload.
+
+    One double block and one single block at the full token count
+    (L = 4608), with the reference's own b1_linear_f32_f32 (AVX2 build in
+    oracle/_ref, all host threads) on 1/ROW_FRAC of each linear's output
+    rows, attention for 1 of the 24 heads, and the remaining ops (LayerNorm-
+    modulate, Q/K RMSNorm + RoPE, GELU) in full through the CPU restatement
+    of the ggml built-ins.  Each part's time is scaled by the work it
+    skipped, then ms/step = 19 * double + 38 * single + edges.
+    """
+    ROW_FRAC = 16
+
+    def __init__(self, threads: int):
+        import ctypes
+        from oracle import pyoracle as O
+        self.O = O
+        self.threads = threads
+        self.fast = ctypes.CDLL(str(ROOT / "oracle/_build/libbonsai_oracle_fast.so"))
+        vp, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+        self.fast.orc_attention.argtypes = [vp, vp, vp, i, i, i, f, vp]
+        self.fast.orc_ln_modulate.argtypes = [vp, i, i, vp, vp, f, vp]
+        self.fast.orc_gelu.argtypes = [vp, i, i, vp, i]
+        self.fast.orc_qk_norm_rope_heads.argtypes = [vp, i, i, i, vp, vp, i, f, vp, vp]
+        self.fast.orc_linear_f32.argtypes = [vp, i, i, vp, vp, i, vp]
+        self.fast.orc_set_threads.argtypes = [i]
+        self.fast.orc_set_threads(threads)
+        R = O.ref()
+        self.kind = "reference" if R is not None else "port"
+        rng = np.random.default_rng(77)
+        self.rng = rng
+        self.x = rng.standard_normal((L, MLP + H)).astype(np.float32)  # activations (any row/col slice)
+        self.h = rng.standard_normal((L, H)).astype(np.float32)
+        self.y = np.zeros((L, MLP + H), np.float32)
+        self.shift = rng.standard_normal(H).astype(np.float32)
+        self.scale = rng.standard_normal(H).astype(np.float32)
+        self.qkh = rng.standard_normal((1, L, HD)).astype(np.float32)
+        self.nw = (1 + 0.1 * rng.standard_normal(HD)).astype(np.float32)
+        ids = np.zeros((L, 3), np.float32)
+        for y in range(GRID):
+            for x in range(GRID):
+                ids[TXT + y * GRID + x, 1:] = (y, x)
+        self.cos, self.sin = O.rope_cos_sin(ids, [16, 56, 56], 10000.0)
+        self.q1 = rng.standard_normal((L, 1, HD)).astype(np.float32)
+        self.att = np.zeros((L, HD), np.float32)
+        self.w = {}
+
+    def _packed(self, rows, K):
+        key = (rows, K)
+        if key not in self.w:
+            nb = K // 32
+            raw = np.zeros((rows, nb, 6), np.uint8)
+            raw[:, :, 0:2] = (np.abs(self.rng.standard_normal((rows, nb))) * 0.02).astype(
+                np.float16).view(np.uint8).reshape(rows, nb, 2)
+            raw[:, :, 2:6] = self.rng.integers(0, 256, size=(rows, nb, 4), dtype=np.uint8)
+            self.w[key] = raw.reshape(rows, nb * 6)
+        return self.w[key]
+
+    def _lin(self, tokens, K, N):
+        """Time the reference B1 kernel on N/ROW_FRAC rows; return the full-N estimate (s)."""
+        O = self.O
+        n = max(1, N // self.ROW_FRAC)
+        w = self._packed(n, K)
+        act = np.ascontiguousarray(self.x[:tokens, :K])
+        out = np.zeros((tokens, n), np.float32)
+        t0 = time.perf_counter()
+        if self.kind == "reference":
+            O.ref().ref_b1_linear(act.ctypes.data, tokens, K, w.ctypes.data, n, out.ctypes.data,
+                                  self.threads)
+        else:
+            O.lib().orc_b1_linear(act.ctypes.data, tokens, K, w.ctypes.data, n, out.ctypes.data)
+        return (time.perf_counter() - t0) * N / n
+
+    def _timed(self, fn):
+        t0 = time.perf_counter()
+        fn()
+        return time.perf_counter() - t0
+
+    def _ln(self, rows):
+        return self._timed(lambda: self.fast.orc_ln_modulate(
+            self.h.ctypes.data, rows, H, self.shift.ctypes.data, self.scale.ctypes.data, 1e-6,
+            self.y.ctypes.data))
+
+    def _qk(self):  # q and k of all 24 heads: time one head's rows x 48
+        return 2 * HEADS * self._timed(lambda: self.fast.orc_qk_norm_rope_heads(
+            self.qkh.ctypes.data, 1, L, HD, self.nw.ctypes.data, self.nw.ctypes.data, TXT, 1e-6,
+            self.cos.ctypes.data, self.sin.ctypes.data))
+
+    def _attn(self):  # 1 of 24 heads, scaled
+        return HEADS * self._timed(lambda: self.fast.orc_attention(
+            self.q1.ctypes.data, self.q1.ctypes.data, self.q1.ctypes.data, L, 1, HD,
+            float(HD ** -0.5), self.att.ctypes.data))
+
+    def _gelu(self, rows):
+        return self._timed(lambda: self.fast.orc_gelu(self.x.ctypes.data, rows, MLP,
+                                                      self.y.ctypes.data, MLP))
+
+    def run(self):
+        """One sampled step; returns (extrapolated ms per denoise step, sample seconds)."""
+        t_start = time.perf_counter()
+        dbl = 2 * self._ln(L) + self._qk() + self._attn() + self._gelu(L)
+        for tok in (TXT, IMG):
+            dbl += (self._lin(tok, H, 3 * H) + self._lin(tok, H, H) + self._lin(tok, H, MLP)
+                    + self._lin(tok, MLP, H))
+        sgl = self._ln(L) + self._qk() + self._attn() + self._gelu(L)
+        sgl += self._lin(L, H, 3 * H + MLP) + self._lin(L, H + MLP, H)
+        mods = self._lin(1, H, DEPTH * 12 * H + SINGLE * 3 * H)
+        edges = self._lin(TXT, CTX, H)  # text embedder (dominant edge op), B1-rate proxy
+        ms = 1000.0 * (DEPTH * dbl + SINGLE * sgl + mods + edges)
+        return ms, time.perf_counter() - t_start
+
+    def describe(self):
+        return (f"1 double + 1 single block at L=4608 per sample: reference b1_linear_f32_f32 "
+                f"(AVX2, oracle/_ref) on 1/{self.ROW_FRAC} of each linear's output rows, attention "
+                f"on 1 of 24 heads, LayerNorm/RMSNorm/RoPE/GELU in full (CPU restatement of the "
+                f"ggml built-ins); scaled to 19 double + 38 single blocks + modulation + edges")
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    cs = CpuSample(threads)
+    for _ in range(args.warmup):
+        cs.run()
+    vals = []
+    for _ in range(args.steps):
+        ms, _ = cs.run()
+        vals.append(ms)
+    v = statistics.mean(vals)
+    line = {
+        "metric": METRIC, "value": round(v, 1), "unit": "ms", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 1),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "parallelism": "host threads", "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": round(v, 1), "unit": "ms", "cores": threads, "kind": cs.kind,
+                         "sample": cs.describe()},
+        "e2e": {"value": round(v, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU arm
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank: int, log: str | None = None):
+        self.log = log
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.gpu = vis.split(",")[local_rank] if vis else str(local_rank)
+        self.proc = None
+
+    def start(self):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", self.gpu], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.seek(0)
+        raw = self.f.read()
+        if self.log:
+            Path(self.log).write_text(raw)
+        rows = [r.split(",") for r in raw.strip().splitlines() if r.count(",") >= 8]
+        self.f.close()
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in rows for j in range(4) if r[5 + j].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def run_bonsai(args):
+    import torch
+    import bonsai_b200 as bb
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    bb.init(local)
+    model = bb.Dit(bb.PRESET_FLUX1, IMG, TXT, GRID, GRID, seed=1234)
+
+    rng = np.random.default_rng(1000 + rank)
+    img_h = torch.from_numpy(rng.standard_normal((IMG, IN_CH)).astype(np.float32)).pin_memory()
+    txt_h = torch.from_numpy(rng.standard_normal((TXT, CTX)).astype(np.float32)).pin_memory()
+    pooled_h = torch.from_numpy(rng.standard_normal(POOLED).astype(np.float32)).pin_memory()
+    out_h = torch.empty(IMG, IN_CH).pin_memory()
+    img_d, txt_d, pooled_d = img_h.cuda(), txt_h.cuda(), pooled_h.cuda()
+    out_d = torch.empty(IMG, IN_CH, device="cuda")
+    K, W = args.steps, args.warmup
+    ts = [1000.0 * (1.0 - (i % 4) / 4.0) for i in range(max(K, W))]  # schnell's 4-step schedule
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream()
+    for i in range(W):
+        model.forward(img_d, txt_d, pooled_d, ts[i], out_d)
+    torch.cuda.synchronize()
+    assert bb.device_error() == 0
+
+    # ---- timed region: device-resident inputs
+    clocks = ClockSampler(local, os.environ.get("BONSAI_CLOCK_LOG"))
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    bb.launch_count()
+    bb.profile_start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        model.forward(img_d, txt_d, pooled_d, ts[i], out_d)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = bb.launch_count()
+    prof = bb.profile_stop()
+    clk = clocks.stop()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / K)
+    assert bb.device_error() == 0
+
+    # ---- end to end through the host-buffer C-ABI entry point
+    out_np = out_h.numpy()
+    img_np, txt_np, pooled_np = img_h.numpy(), txt_h.numpy(), pooled_h.numpy()
+    for i in range(2):
+        model.forward_host(img_np, txt_np, pooled_np, ts[i], out_np)
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(K):
+        model.forward_host(img_np, txt_np, pooled_np, ts[i], out_np)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1) / K)
+    finite = bool(np.isfinite(out_np).all())
+
+    pk = peaks()
+    g = prof.get("b1_gemm", {})
+    a = prof.get("attention", {})
+    gemm_tf = g["flop"] / (g["ms"] / 1e3) / 1e12 if g else None
+    attn_tf = a["flop"] / (a["ms"] / 1e3) / 1e12 if a else None
+    per_step = {k: {"launches": v["launches"] / K, "ms": round(v["ms"] / K, 4),
+                    "share": round(v["ms"] / sum(x["ms"] for x in prof.values()), 4)}
+                for k, v in prof.items()}
+    line = {
+        "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": world, "img_tokens": IMG,
+                   "txt_tokens": TXT, "parallelism": f"dp{world} (one image per GPU, no collective)",
+                   "l2": "inputs larger than L2: every step streams all 2.2 GB of B1_0 weights"},
+        "images_per_s": round(world * 1000.0 / ms, 3),
+        "step_tflops": round(step_flops() / (ms / 1e3) / 1e12, 1),
+        "roofline": {"bound": "tensor", "kernel": "b1_gemm", "achieved": round(gemm_tf, 1),
+                     "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
+                     "frac": round(gemm_tf / pk["bf16_sustained"], 4),
+                     "peak_kind": f"{pk['source']} sustained bf16 (dense GEMM under the power cap)",
+                     "frac_of_burst": round(gemm_tf / pk["bf16"], 4), "traffic": None},
+        "attention_roofline": {"bound": "tensor", "kernel": "attention",
+                               "achieved": round(attn_tf, 1), "peak": pk["bf16_sustained"],
+                               "unit": "TFLOP/s", "frac": round(attn_tf / pk["bf16_sustained"], 4),
+                               "frac_of_burst": round(attn_tf / pk["bf16"], 4)},
+        "kernels_per_step": per_step,
+        "gpu_launches": launches,
+        "clocks": clk,
+        "e2e": {"value": round(ms_e2e, 3), "unit": "ms",
+                "h2d_bytes_per_step": (IMG * IN_CH + TXT * CTX + POOLED + 256) * 4,
+                "d2h_bytes_per_step": IMG * IN_CH * 4, "output_finite": finite},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        cs = CpuSample(threads)
+        cpu_ms, sample_s = cs.run()
+        line["cpu_baseline"] = {"value": round(cpu_ms, 1), "unit": "ms", "cores": threads,
+                                "kind": cs.kind, "sample": cs.describe(),
+                                "sample_seconds": round(sample_s, 2)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["bonsai", "reference"], default="bonsai")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_bonsai(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

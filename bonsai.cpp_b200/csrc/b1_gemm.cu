@@ -41,9 +41,10 @@ constexpr int A_COL0 = 256;    // A stages at 256 + s*32 (64 f16 = 32 columns)
 
 constexpr int WARP_TMA = 0;
 constexpr int WARP_MMA = 1;
-constexpr int WARP_EXP0 = 2;  // warps 2..5
-constexpr int WARP_EPI0 = 6;  // warps 6..9
-constexpr int NUM_THREADS = 320;
+constexpr int EXP_WARPS = 8;   // two per TMEM lane quarter, alternating k-blocks
+constexpr int WARP_EXP0 = 2;   // warps 2..9
+constexpr int WARP_EPI0 = WARP_EXP0 + EXP_WARPS;  // warps 10..13
+constexpr int NUM_THREADS = (WARP_EPI0 + 4) * 32;
 
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * X_STAGE_BYTES +
                            STAGES * RAW_STAGE_BYTES + 256 /*barriers etc*/;
@@ -210,14 +211,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
-  } else if (warp >= WARP_EXP0 && warp < WARP_EXP0 + 4) {
+  } else if (warp >= WARP_EXP0 && warp < WARP_EXP0 + EXP_WARPS) {
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int r = q * 32 + (int)lane;   // weight row within the tile
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    // The two warps of a quarter take alternate pipeline iterations, so each
+    // has two k-blocks of MMA time to hide its tcgen05.st round trip.
+    const uint32_t parity = (uint32_t)((warp - WARP_EXP0) >> 2);
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        if ((it & 1u) != parity) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         bool good = wait_bar(&rawfull[s], ph, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER) &&

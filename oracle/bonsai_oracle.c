@@ -259,7 +259,7 @@ ORC_EXPORT void orc_attention(const float* q, const float* k, const float* v, in
 #pragma omp parallel
   {
     float* sc = (float*)malloc(sizeof(float) * (size_t)seq);
-    double* acc = (double*)malloc(sizeof(double) * (size_t)hd);
+    float* acc = (float*)malloc(sizeof(float) * (size_t)hd);
 #pragma omp for collapse(2) schedule(static)
     for (int h = 0; h < n_heads; ++h)
       for (int i = 0; i < seq; ++i) {
@@ -267,22 +267,27 @@ ORC_EXPORT void orc_attention(const float* q, const float* k, const float* v, in
         float mx = -INFINITY;
         for (int j = 0; j < seq; ++j) {
           const float* kj = k16 + ((size_t)j * n_heads + h) * hd;
-          float s = 0.0f;
-          for (int d = 0; d < hd; ++d) s += qi[d] * kj[d];
+          /* eight fixed partial sums: a deterministic order that vectorises */
+          float part[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          int d = 0;
+          for (; d + 8 <= hd; d += 8)
+            for (int u = 0; u < 8; ++u) part[u] += qi[d + u] * kj[d + u];
+          float s = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+          for (; d < hd; ++d) s += qi[d] * kj[d];
           s *= scale;
           sc[j] = s;
           if (s > mx) mx = s;
         }
-        double l = 0.0;
-        for (int d = 0; d < hd; ++d) acc[d] = 0.0;
+        float l = 0.0f;
+        for (int d = 0; d < hd; ++d) acc[d] = 0.0f;
         for (int j = 0; j < seq; ++j) {
           const float p = expf(sc[j] - mx);
           l += p;
           const float* vj = v16 + ((size_t)j * n_heads + h) * hd;
-          for (int d = 0; d < hd; ++d) acc[d] += (double)p * vj[d];
+          for (int d = 0; d < hd; ++d) acc[d] += p * vj[d];
         }
         float* o = out + (size_t)i * n_heads * hd + (size_t)h * hd;
-        for (int d = 0; d < hd; ++d) o[d] = (float)(acc[d] / l);
+        for (int d = 0; d < hd; ++d) o[d] = acc[d] / l;
       }
     free(sc);
     free(acc);
