@@ -41,10 +41,13 @@ constexpr int A_COL0 = 256;    // A stages at 256 + s*32 (64 f16 = 32 columns)
 
 constexpr int WARP_TMA = 0;
 constexpr int WARP_MMA = 1;
-constexpr int EXP_WARPS = 8;   // two per TMEM lane quarter, alternating k-blocks
-constexpr int WARP_EXP0 = 2;   // warps 2..9
-constexpr int WARP_EPI0 = WARP_EXP0 + EXP_WARPS;  // warps 10..13
-constexpr int NUM_THREADS = (WARP_EPI0 + 4) * 32;
+constexpr int EXP_PER_Q = 2;   // expansion warps per TMEM lane quarter (round-robin k-blocks)
+constexpr int EXP_WARPS = 4 * EXP_PER_Q;
+constexpr int WARP_EXP0 = 2;
+constexpr int EPI_PER_Q = 2;   // epilogue warps per lane quarter (split the token columns)
+constexpr int EPI_WARPS = 4 * EPI_PER_Q;
+constexpr int WARP_EPI0 = WARP_EXP0 + EXP_WARPS;
+constexpr int NUM_THREADS = (WARP_EPI0 + EPI_WARPS) * 32;
 
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * X_STAGE_BYTES +
                            STAGES * RAW_STAGE_BYTES + 256 /*barriers etc*/;
@@ -60,14 +63,21 @@ struct Params {
   int* err;
 };
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
-  const float k0 = 0.7978845608028654f;
-  const float u = k0 * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(u));
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))); hardware tanh (the
+  // result is rounded to f16 right after, well below tanh.approx's error).
+  const float k0 = 0.7978845608028654f;
+  const float u = k0 * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanh_hw(u));
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 // Expand one 32-input group: pair-split sign word p, f16 scale bits s.
 // Output word j holds inputs (2j, 2j+1) as f16 +-s (low half = input 2j).
@@ -119,7 +129,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       bar_init(&dfull[b], 1);
-      bar_init(&dempty[b], 4);
+      bar_init(&dempty[b], EPI_WARPS);
     }
     bar_init(drain, 1);
     *abort_flag = 0;
@@ -215,14 +225,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int r = q * 32 + (int)lane;   // weight row within the tile
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    // The two warps of a quarter take alternate pipeline iterations, so each
-    // has two k-blocks of MMA time to hide its tcgen05.st round trip.
-    const uint32_t parity = (uint32_t)((warp - WARP_EXP0) >> 2);
+    // The EXP_PER_Q warps of a quarter take pipeline iterations round-robin.
+    // Each warp overlaps the tcgen05.st of one k-block with the expansion of
+    // its next one: the stage is published (wait::st, arrive) only after the
+    // following k-block's values are in registers.
+    const uint32_t slot = (uint32_t)((warp - WARP_EXP0) >> 2);
     uint32_t it = 0;
+    int pending = -1;  // stage whose tcgen05.st is in flight
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       for (int kb = 0; kb < k_blocks; ++kb, ++it) {
-        if ((it & 1u) != parity) continue;
+        if (it % EXP_PER_Q != slot) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         bool good = wait_bar(&rawfull[s], ph, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER) &&
@@ -239,15 +252,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t v[32];
         expand_group(p0, bf16_from_f16_scale<kBF16>(sc & 0xFFFFu), v);
         expand_group(p1, bf16_from_f16_scale<kBF16>(sc >> 16), v + 16);
+        if (pending >= 0) {
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) bar_arrive(&full[pending]);
+        }
         tmem_st32(tmem + lane_base + A_COL0 + s * 32, v);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) bar_arrive(&full[s]);
+        pending = s;
       }
     }
-  } else if (warp >= WARP_EPI0 && warp < WARP_EPI0 + 4) {
+    if (pending >= 0) {
+      // Publish the last stage (also on the abort path: the MMA side is
+      // bounded and ignores it).
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(&full[pending]);
+    }
+  } else if (warp >= WARP_EPI0 && warp < WARP_EPI0 + EPI_WARPS) {
     const int q = warp & 3;
+    const int eh = (warp - WARP_EPI0) >> 2;  // which half of the token columns
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint32_t lt = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
@@ -267,70 +292,75 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // Segments are tile-aligned in every caller, but stay correct per row.
       EpiSeg sg;
       if (si >= 0) sg = p.seg[si];
+      const int mode = si >= 0 ? sg.mode : -1;
       const int rr = row - sg.row_begin;
       float gate = 1.0f;
-      if (si >= 0 && sg.mode == EPI_RESID_F32 && sg.gate) gate = sg.gate[rr];
-      size_t qkv_base = 0;
-      if (si >= 0 && sg.mode == EPI_QKV_F16) {
+      if (mode == EPI_RESID_F32 && sg.gate) gate = sg.gate[rr];
+      // Per-thread destination of token t: base + t * stride (elements).
+      size_t base = 0;
+      uint32_t stride = (uint32_t)sg.ld;
+      if (mode == EPI_QKV_F16) {
         const int hd = sg.head_dim;
         const int which = rr / (sg.heads * hd);
         const int rem = rr - which * sg.heads * hd;
         const int h = rem / hd;
         const int d = rem - h * hd;
-        qkv_base = ((size_t)(which * sg.heads + h) * sg.seq_total + sg.tok_off) * hd + d;
+        base = ((size_t)(which * sg.heads + h) * sg.seq_total + sg.tok_off) * hd + d;
+        stride = (uint32_t)hd;
+      } else if (mode == EPI_SWIGLU_F16) {
+        base = (size_t)sg.col_off + (rr >> 1);
+      } else if (mode >= 0) {
+        base = (size_t)sg.col_off + rr;
       }
+      const bool warp_swiglu = __any_sync(0xffffffffu, mode == EPI_SWIGLU_F16);
 
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int cc = 0; cc < BN / 32 / EPI_PER_Q; ++cc) {
+        const int c = eh * (BN / 32 / EPI_PER_Q) + cc;
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + D_COL0 + b * BN + c * 32, v);
         tmem_wait_ld();
         const int t0 = ttile * BN + c * 32;
-        const bool mine_swiglu = si >= 0 && sg.mode == EPI_SWIGLU_F16;
-        if (__any_sync(0xffffffffu, mine_swiglu)) {
+        const int nt = min(32, p.tokens - t0);
+        if (warp_swiglu) {
           // Rows are stored gate/value interleaved; the even lane owns the pair.
+          __half* dst = reinterpret_cast<__half*>(sg.dst) + base + (size_t)t0 * stride;
+          const bool own = mode == EPI_SWIGLU_F16 && (rr & 1) == 0;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float a = __uint_as_float(v[j]);
             const float o = __shfl_xor_sync(0xffffffffu, a, 1);
-            const int t = t0 + j;
-            if (mine_swiglu && (rr & 1) == 0 && t < p.tokens) {
-              __half* dst = reinterpret_cast<__half*>(sg.dst);
-              dst[(size_t)t * sg.ld + sg.col_off + (rr >> 1)] = __float2half_rn(silu(a) * o);
-            }
+            if (own && j < nt) dst[j * stride] = __float2half_rn(silu(a) * o);
           }
           continue;
         }
-        if (si < 0) continue;
+        if (mode < 0 || nt <= 0) continue;
+        if (mode == EPI_F16 || mode == EPI_QKV_F16) {
+          __half* dst = reinterpret_cast<__half*>(sg.dst) + base + (size_t)t0 * stride;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int t = t0 + j;
-          if (t >= p.tokens) break;
-          const float a = __uint_as_float(v[j]);
-          switch (sg.mode) {
-            case EPI_F32:
-              reinterpret_cast<float*>(sg.dst)[(size_t)t * sg.ld + sg.col_off + rr] = a;
-              break;
-            case EPI_F16:
-              reinterpret_cast<__half*>(sg.dst)[(size_t)t * sg.ld + sg.col_off + rr] =
-                  __float2half_rn(a);
-              break;
-            case EPI_GELU_F16:
-              reinterpret_cast<__half*>(sg.dst)[(size_t)t * sg.ld + sg.col_off + rr] =
-                  __float2half_rn(gelu_tanh(a));
-              break;
-            case EPI_RESID_F32: {
-              float* d = reinterpret_cast<float*>(sg.dst) + (size_t)t * sg.ld + sg.col_off + rr;
-              *d = *d + gate * a;
-              break;
-            }
-            case EPI_QKV_F16:
-              reinterpret_cast<__half*>(sg.dst)[qkv_base + (size_t)t * sg.head_dim] =
-                  __float2half_rn(a);
-              break;
-            default:
-              break;
+          for (int j = 0; j < 32; ++j)
+            if (j < nt) dst[j * stride] = __float2half_rn(__uint_as_float(v[j]));
+        } else if (mode == EPI_GELU_F16) {
+          __half* dst = reinterpret_cast<__half*>(sg.dst) + base + (size_t)t0 * stride;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nt) dst[j * stride] = __float2half_rn(gelu_tanh(__uint_as_float(v[j])));
+        } else if (mode == EPI_RESID_F32) {
+          float* dst = reinterpret_cast<float*>(sg.dst) + base + (size_t)t0 * stride;
+#pragma unroll
+          for (int h16 = 0; h16 < 32; h16 += 16) {
+            float old[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) old[j] = h16 + j < nt ? dst[(h16 + j) * stride] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (h16 + j < nt) dst[(h16 + j) * stride] = fmaf(gate, __uint_as_float(v[h16 + j]), old[j]);
           }
+        } else if (mode == EPI_F32) {
+          float* dst = reinterpret_cast<float*>(sg.dst) + base + (size_t)t0 * stride;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nt) dst[j * stride] = __uint_as_float(v[j]);
         }
       }
       tc_fence_before();
