@@ -4,19 +4,23 @@
 // (src/diffuser_graph.cpp:403-416 double blocks, :506-519 single blocks):
 // softmax(Q K^T * scale) V per head, no mask, K and V in f16, f32 softmax.
 //
-// One CTA = one head x 128 queries.  Roles:
-//   warp 0      TMA: Q once, then K_j / V_j tiles (128 keys x 128 dims, two
-//               64-dim halves with 128-byte swizzle) into a 3-deep K ring and
-//               a 2-deep V ring.
+// One CTA = one head x 256 queries, processed as two 128-query tiles that
+// ping-pong on the tensor core: while the softmax warps of one tile work,
+// the MMA thread runs the other tile's P*V and its next Q*K^T.
+//   warp 0      TMA: Q0/Q1 once, then K_j / V_j tiles (128 keys x 128 dims,
+//               two 64-dim halves, 128-byte swizzle) through 2-deep rings.
 //   warp 1      one thread issues tcgen05.mma:
-//                 S_j = Q K_j^T   (A, B from SMEM; S double-buffered in TMEM)
-//                 O  += P_j V_j   (A = P from TMEM, B = V from SMEM, MN-major)
-//   warps 2-5   softmax: thread i owns query row i (TMEM lane i).  Online
-//               softmax in the log2 domain with lazy rescaling: the running
-//               max only moves (and O in TMEM is rescaled) when a tile's max
-//               exceeds it by more than 8 (p <= 2^8 fits f16 P exactly
-//               enough); the final 1/l normalisation makes the result exact.
-// TMEM: S0 [0,128) S1 [128,256) O [256,384) P [384,448) (f16 pairs).
+//                 S_g  = Q_g K_j^T   (A, B from SMEM)          g = 0, 1
+//                 O_g += P_g V_j     (A = P_g from TMEM, B = V MN-major)
+//   warps 2-5   softmax of tile 0, warps 6-9 softmax of tile 1: thread i owns
+//               query row i (TMEM lane i).  Online softmax in the log2 domain
+//               with lazy rescaling: the running max only moves (and O_g in
+//               TMEM is rescaled) when a tile's max exceeds it by more than 8
+//               (p <= 2^8 stays accurate in f16); the final 1/l is exact.
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// P_g (f16 pairs, 64 columns) overwrites the first half of S_g once the
+// softmax has read S_g; the next S_g is issued after P_g V_j in the same
+// in-order MMA stream.
 #include "internal.cuh"
 #include "ptx.cuh"
 
@@ -25,17 +29,17 @@
 namespace bonsai {
 namespace attn {
 
-constexpr int BQ = 128;
+constexpr int BQ = 128;   // queries per tile (two tiles per CTA)
 constexpr int BKV = 128;
 constexpr int HD = 128;
-constexpr int KS = 3;  // K ring depth
+constexpr int KS = 2;  // K ring depth
 constexpr int VS = 2;  // V ring depth
 constexpr int TILE_BYTES = BKV * HD * 2;  // 32 KB (two 16 KB halves)
 constexpr int HALF_BYTES = TILE_BYTES / 2;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;
 constexpr int TMEM_COLS = 512;
-constexpr int S_COL = 0, O_COL = 256, P_COL = 384;
-constexpr int SMEM_BYTES = 1024 + TILE_BYTES * (1 + KS + VS) + 256;
+constexpr int S_COL = 0, O_COL = 256;
+constexpr int SMEM_BYTES = 1024 + TILE_BYTES * (2 + KS + VS) + 256;
 constexpr float kRescaleThreshold = 8.0f;
 
 struct Params {
@@ -60,8 +64,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* qs = smem;
-  uint8_t* ks = qs + TILE_BYTES;
+  uint8_t* qs = smem;  // Q0 then Q1
+  uint8_t* ks = qs + 2 * TILE_BYTES;
   uint8_t* vs = ks + KS * TILE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(vs + VS * TILE_BYTES);
   uint64_t* q_full = bars;
@@ -69,17 +73,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* k_empty = k_full + KS;
   uint64_t* v_full = k_empty + KS;
   uint64_t* v_empty = v_full + VS;
-  uint64_t* s_full = v_empty + VS;  // [2]
-  uint64_t* p_ready = s_full + 2;
-  uint64_t* pv_done = p_ready + 1;
-  uint64_t* drain = pv_done + 1;
+  uint64_t* s_full = v_empty + VS;   // [2] one per query tile
+  uint64_t* p_ready = s_full + 2;    // [2]
+  uint64_t* pv_done = p_ready + 2;   // [2]
+  uint64_t* drain = pv_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
   const uint32_t lane = lane_id();
   const int head = blockIdx.y;
-  const int q0 = blockIdx.x * BQ;
+  const int q0 = blockIdx.x * 2 * BQ;
   const int nkv = (p.seq + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
@@ -92,10 +96,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bar_init(&v_full[s], 1);
       bar_init(&v_empty[s], 1);
     }
-    bar_init(&s_full[0], 1);
-    bar_init(&s_full[1], 1);
-    bar_init(p_ready, 4);
-    bar_init(pv_done, 1);
+    for (int g = 0; g < 2; ++g) {
+      bar_init(&s_full[g], 1);
+      bar_init(&p_ready[g], 4);
+      bar_init(&pv_done[g], 1);
+    }
     bar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -114,9 +119,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      bar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_3d(qs, &qmap, q_full, 0, q0, head);
-      tma_load_3d(qs + HALF_BYTES, &qmap, q_full, 64, q0, head);
+      bar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      for (int g = 0; g < 2; ++g) {
+        tma_load_3d(qs + g * TILE_BYTES, &qmap, q_full, 0, q0 + g * BQ, head);
+        tma_load_3d(qs + g * TILE_BYTES + HALF_BYTES, &qmap, q_full, 64, q0 + g * BQ, head);
+      }
       bool ok = true;
       for (int j = 0; j < nkv && ok; ++j) {
         const int sk = j % KS;
@@ -146,43 +153,54 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (elect_one()) {
       constexpr uint32_t idesc_s = make_idesc_f16(BQ, BKV, 0, 0, 0);   // K-major A and B
       constexpr uint32_t idesc_o = make_idesc_f16(BQ, HD, 0, 0, 1);    // B (V) MN-major
-      const uint32_t q_addr = smem_u32(qs);
       bool ok = wait_bar(q_full, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA);
-      auto issue_s = [&](int j) -> bool {
+      // S_g = Q_g K_j^T into S_g (g = query tile); the K stage is released
+      // after the second tile's product.
+      auto issue_s = [&](int j, int g) -> bool {
         const int sk = j % KS;
-        if (!wait_bar(&k_full[sk], (j / KS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
+        if (g == 0 &&
+            !wait_bar(&k_full[sk], (j / KS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
           return false;
         tc_fence_after();
+        const uint32_t q_addr = smem_u32(qs + g * TILE_BYTES);
         const uint32_t k_addr = smem_u32(ks + sk * TILE_BYTES);
-        const uint32_t d = tmem + S_COL + (j & 1) * BKV;
+        const uint32_t d = tmem + S_COL + g * BKV;
 #pragma unroll
         for (int k16 = 0; k16 < HD / 16; ++k16) {
           const uint32_t off = (k16 >> 2) * HALF_BYTES + (k16 & 3) * 32;
           mma_ss(d, make_smem_desc(q_addr + off, 16, 1024), make_smem_desc(k_addr + off, 16, 1024),
                  idesc_s, k16 > 0 ? 1u : 0u);
         }
-        tc_commit(&k_empty[sk]);
-        tc_commit(&s_full[j & 1]);
+        tc_commit(&s_full[g]);
+        if (g == 1) tc_commit(&k_empty[sk]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      if (ok && nkv > 1) ok = issue_s(1);
-      for (int j = 0; j < nkv && ok; ++j) {
-        if (!wait_bar(p_ready, j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) break;
+      // O_g += P_g V_j; the V stage is released after the second tile's product.
+      auto issue_pv = [&](int j, int g) -> bool {
+        if (!wait_bar(&p_ready[g], j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) return false;
         const int sv = j % VS;
-        if (!wait_bar(&v_full[sv], (j / VS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) break;
+        if (g == 0 &&
+            !wait_bar(&v_full[sv], (j / VS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
+          return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(vs + sv * TILE_BYTES);
 #pragma unroll
         for (int k16 = 0; k16 < BKV / 16; ++k16) {
           // 16 keys per step: rows k16*16.. of both 64-dim halves (LBO = half stride).
-          mma_ts(tmem + O_COL, tmem + P_COL + k16 * 8,
+          mma_ts(tmem + O_COL + g * HD, tmem + S_COL + g * BKV + k16 * 8,
                  make_smem_desc(v_addr + k16 * 16 * 128, HALF_BYTES, 1024), idesc_o,
                  (j > 0 || k16 > 0) ? 1u : 0u);
         }
-        tc_commit(&v_empty[sv]);
-        tc_commit(pv_done);
-        if (j + 2 < nkv) ok = issue_s(j + 2);
+        tc_commit(&pv_done[g]);
+        if (g == 1) tc_commit(&v_empty[sv]);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0) && issue_s(0, 1);
+      for (int j = 0; j < nkv && ok; ++j) {
+        ok = issue_pv(j, 0);
+        if (ok && j + 1 < nkv) ok = issue_s(j + 1, 0);
+        if (ok) ok = issue_pv(j, 1);
+        if (ok && j + 1 < nkv) ok = issue_s(j + 1, 1);
       }
       tc_commit(drain);
       const uint32_t da = smem_u32(drain);
@@ -195,14 +213,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else {
-    // softmax warps 2..5
+    // softmax warps: 2..5 -> query tile 0, 6..9 -> query tile 1
+    const int g = (warp - 2) >> 2;
     const int qd = warp & 3;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + S_COL + g * BKV;
+    const uint32_t o_addr = tmem + lane_base + O_COL + g * HD;
     const int row = qd * 32 + (int)lane;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      bool good = wait_bar(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+      bool good = wait_bar(&s_full[g], j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
       if (!__all_sync(0xffffffffu, good)) {
         ok = false;
         break;
@@ -213,7 +234,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t r[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tmem + lane_base + S_COL + (j & 1) * BKV + c * 32, r);
+          tmem_ld32(s_addr + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
@@ -242,14 +263,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int c = 0; c < BKV / 2; ++c) {
         const float a = ex2(fmaf(s[2 * c], p.scale_log2, -m));
         const float b = ex2(fmaf(s[2 * c + 1], p.scale_log2, -m));
+        rs += a + b;
         const __half2 h2 = __floats2half2_rn(a, b);
-        const float2 back = __half22float2(h2);
-        rs += back.x + back.y;
         pk[c] = *reinterpret_cast<const uint32_t*>(&h2);
       }
       l = l * alpha + rs;
       if (j > 0) {
-        good = wait_bar(pv_done, (j - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+        // P_g and O_g are free once the previous P_g V has completed.
+        good = wait_bar(&pv_done[g], (j - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
         if (!__all_sync(0xffffffffu, good)) {
           ok = false;
           break;
@@ -259,11 +280,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
-            tmem_ld32(tmem + lane_base + O_COL + c * 32, r);
+            tmem_ld32(o_addr + c * 32, r);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tmem + lane_base + O_COL + c * 32, r);
+            tmem_st32(o_addr + c * 32, r);
           }
         }
       }
@@ -271,27 +292,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t r[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) r[i] = pk[i];
-        tmem_st32(tmem + lane_base + P_COL, r);
+        tmem_st32(s_addr, r);
 #pragma unroll
         for (int i = 0; i < 32; ++i) r[i] = pk[32 + i];
-        tmem_st32(tmem + lane_base + P_COL + 32, r);
+        tmem_st32(s_addr + 32, r);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) bar_arrive(p_ready);
+      if (lane == 0) bar_arrive(&p_ready[g]);
     }
     if (ok) {
-      const bool good = wait_bar(pv_done, (nkv - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+      const bool good =
+          wait_bar(&pv_done[g], (nkv - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
       if (__all_sync(0xffffffffu, good)) {
         tc_fence_after();
         const float inv_l = 1.0f / l;
-        const int q = q0 + row;
+        const int q = q0 + g * BQ + row;
         __half* dst = p.out + (size_t)q * p.ld_out + (size_t)head * HD;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem + lane_base + O_COL + c * 32, r);
+          tmem_ld32(o_addr + c * 32, r);
           tmem_wait_ld();
           if (q < p.seq) {
             uint32_t hv[16];
@@ -351,7 +373,7 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
     if (e != cudaSuccess) return cuda_status(e, "attention set smem attribute");
     attr = true;
   }
-  dim3 grid((seq + attn::BQ - 1) / attn::BQ, n_heads);
+  dim3 grid((seq + 2 * attn::BQ - 1) / (2 * attn::BQ), n_heads);
   ProfScope prof("attention", 4.0 * (double)seq * seq * head_dim * n_heads,
                  4.0 * (double)seq * n_heads * head_dim * 2, st);
   attn::attention_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, st>>>(qm, km, vm, p);
