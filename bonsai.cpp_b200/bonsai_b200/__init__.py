@@ -49,6 +49,7 @@ SIGNATURES = {
     "bonsai_b1_free": (_c_int, [_vp]),
     "bonsai_b1_shape": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "bonsai_b1_linear_f32": (_c_int, [_vp, _c_int, _vp, _vp, _vp]),
+    "bonsai_b1_linear_f32_noalloc": (_c_int, [_vp, _c_int, _vp, _vp, _vp]),
     "bonsai_b1_gemm": (_c_int, [_vp, _c_ll, _c_int, _vp, _c_int, _vp, _c_ll, _vp, _vp]),
     "bonsai_rope_2d_f32": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp]),
     "bonsai_rope_tables": (_c_int, [_vp, _c_int, _c_int, _vp, _fp, _vp, _vp, _vp]),

@@ -142,9 +142,6 @@ int launch_f32_to_f16(const float* src, __half* dst, long long n, cudaStream_t s
 
 using namespace bonsai;
 
-struct bonsai_b1_weight {
-  B1Weight w;
-};
 
 extern "C" {
 

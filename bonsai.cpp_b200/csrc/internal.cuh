@@ -116,3 +116,8 @@ int launch_silu_f32(const float* x, long long n, float* y, cudaStream_t st);
 int launch_add_f32(const float* a, const float* b, long long n, float* y, cudaStream_t st);
 
 }  // namespace bonsai
+
+// Opaque handle behind bonsai_b1_t (include/bonsai_cuda.h).
+struct bonsai_b1_weight {
+  bonsai::B1Weight w;
+};

@@ -104,6 +104,22 @@ int bonsai_b1_shape(bonsai_b1_t w, int* out_dim, int* in_dim);
  * grown on demand with cudaMallocAsync on the given stream. */
 int bonsai_b1_linear_f32(const float* act, int tokens, bonsai_b1_t w, float* out, void* stream);
 
+/* Same operation as bonsai_b1_linear_f32, for callers that cannot let the
+ * library allocate device memory (no counterpart in the reference).  Hosts
+ * that own every device byte through their own allocator (a ggml graph
+ * allocator), code being recorded into a CUDA graph, or loops that must not
+ * block on an allocation use this form: it calls no cudaMalloc/cudaFree or
+ * allocating library routine.  The f16 copy of act lives in one fixed
+ * 8 MiB device array inside the library (tokens * in_dim <= 4,194,304
+ * elements; larger calls return BONSAI_ERR_UNSUPPORTED), which every GPU that
+ * loads the library keeps until the process exits.  The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress) with the
+ * device current: make that first call before any stream capture.  All calls
+ * share the one array, so calls that may overlap on the GPU (different
+ * streams, or different host threads on one device) race: serialise them. */
+int bonsai_b1_linear_f32_noalloc(const float* act, int tokens, bonsai_b1_t w, float* out,
+                                 void* stream);
+
 /* Fused-epilogue B1_0 GEMM on f16 activations (the form the engine uses).
  * x: f16 [tokens][ldx] (16-byte aligned, ldx % 8 == 0).  The accumulator
  * acc[t][r] is written according to mode:
