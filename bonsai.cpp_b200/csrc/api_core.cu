@@ -122,6 +122,9 @@ ProfScope::~ProfScope() {
 }
 
 int* device_error_word() { return dev_info().err_word; }
+long long launch_counter() { return g_launches; }
+void launch_counter_add(long long n) { g_launches += n; }
+bool profiling_active() { return g_prof_on; }
 int num_sms() { return dev_info().sms; }
 
 int launch_f32_to_f16(const float* src, __half* dst, long long n, cudaStream_t st) {

@@ -143,7 +143,14 @@ struct bonsai_dit {
   __half* vec_silu16 = nullptr;  // [8][H] (row 0 used; padded for TMA)
   float* cos_t = nullptr;    // [L][64]
   float* sin_t = nullptr;
-  float* pinned_te = nullptr;  // host pinned [256]
+  // CUDA graph of the step body (everything after the timestep copy), keyed
+  // by the caller's buffer pointers; captured on a private stream, replayed
+  // on the caller's stream.
+  cudaStream_t cap_stream = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  const void* graph_key[4] = {nullptr, nullptr, nullptr, nullptr};
+  long long graph_kernels = 0;
+  int forwards = 0;
   // device copies of caller inputs for the host-buffer entry point
   float *in_img = nullptr, *in_txt = nullptr, *in_pooled = nullptr, *out_buf = nullptr;
 };
@@ -495,8 +502,7 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->in_txt), (size_t)std::max(c.txt, 1) * c.ctx_dim * 4));
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->in_pooled), (size_t)std::max(c.pooled, 1) * 4));
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->out_buf), (size_t)c.img * c.in_ch * 4));
-  if (cudaMallocHost(&m->pinned_te, 256 * 4) != cudaSuccess)
-    return fail(BONSAI_ERR_NOMEM, "dit_create: pinned allocation failed");
+  RC(cuda_status(cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking), "capture stream"));
   cudaMemset(m->vec_silu16, 0, (size_t)8 * H * 2);
 
   // RoPE ids (src/diffuser.cpp:240-249): text rows 0, image rows (.., y, x)
@@ -533,23 +539,30 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
 int bonsai_dit_destroy(bonsai_dit_t m) {
   if (!m) return 0;
   cudaDeviceSynchronize();
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
   for (void* p : m->allocs) cudaFree(p);
-  if (m->pinned_te) cudaFreeHost(m->pinned_te);
   delete m;
   return 0;
 }
 
-static int dit_prepare_vec(bonsai_dit* m, const float* pooled, float timestep, cudaStream_t st) {
-  const Cfg& c = m->c;
-  // ggml_timestep_embedding(t, 256, 10000) with the [sin, cos] half swap
-  // (src/diffuser_graph.cpp:288-292), evaluated on the host in f32.
+// ggml_timestep_embedding(t, 256, 10000) with the [sin, cos] half swap
+// (src/diffuser_graph.cpp:288-292), evaluated on the host in f32 and copied
+// into the device buffer m->te.  The source is a stack array (pageable): the
+// runtime stages it before returning, so back-to-back calls cannot race on it.
+static int dit_upload_timestep(bonsai_dit* m, float timestep, cudaStream_t st) {
+  float te[256];
   for (int j = 0; j < 128; ++j) {
     const float freq = expf(-logf(10000.0f) * (float)j / 128.0f);
     const float arg = timestep * freq;
-    m->pinned_te[j] = sinf(arg);
-    m->pinned_te[128 + j] = cosf(arg);
+    te[j] = sinf(arg);
+    te[128 + j] = cosf(arg);
   }
-  RC(cuda_status(cudaMemcpyAsync(m->te, m->pinned_te, 256 * 4, cudaMemcpyHostToDevice, st), "te copy"));
+  return cuda_status(cudaMemcpyAsync(m->te, te, sizeof(te), cudaMemcpyHostToDevice, st), "te copy");
+}
+
+static int dit_prepare_vec(bonsai_dit* m, const float* pooled, cudaStream_t st) {
+  const Cfg& c = m->c;
   // time MLP (:294-305): vec = W2 silu(W1 te + b1) + b2
   RC(launch_linear_f32(m->te, 256, 1, 256, m->time_w1, m->time_b1, c.H, m->h256, c.H, false, st));
   RC(launch_linear_f32(m->h256, c.H, 1, c.H, m->time_w2, m->time_b2, c.H, m->vec, c.H, true, st));
@@ -562,17 +575,17 @@ static int dit_prepare_vec(bonsai_dit* m, const float* pooled, float timestep, c
   return compute_mods(m, st);
 }
 
-int bonsai_dit_forward(bonsai_dit_t m, const float* img, const float* txt, const float* pooled,
-                       float timestep, float* out, void* stream) {
-  if (!m || !img || !out || (m->c.txt > 0 && !txt)) return fail(BONSAI_ERR_ARG, "dit_forward: null argument");
+// Everything of the step after the timestep upload (all stream-ordered kernel
+// launches with fixed pointers).
+static int dit_forward_body(bonsai_dit* m, const float* img, const float* txt, const float* pooled,
+                            float* out, cudaStream_t st) {
   const Cfg& c = m->c;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   // input projections (:283-286), text rows first in the hidden state
   RC(launch_linear_f32(txt, c.ctx_dim, c.txt, c.ctx_dim, m->txt_in_w, m->txt_in_b, c.H, m->hidden,
-                       c.H, false, st));
+                       c.H, false, st, m->tmp32, (long long)c.img * c.H));
   RC(launch_linear_f32(img, c.in_ch, c.img, c.in_ch, m->img_in_w, m->img_in_b, c.H,
                        m->hidden + (size_t)c.txt * c.H, c.H, false, st));
-  RC(dit_prepare_vec(m, pooled, timestep, st));
+  RC(dit_prepare_vec(m, pooled, st));
   for (int i = 0; i < c.depth; ++i) RC(run_double(m, i, st));
   for (int i = 0; i < c.depth_single; ++i) RC(run_single(m, i, st));
   // output head (:544-556): norm_out modulation is (scale, shift)
@@ -580,6 +593,54 @@ int bonsai_dit_forward(bonsai_dit_t m, const float* img, const float* txt, const
   RC(launch_ln_modulate_f32(h_img, c.img, c.H, m->fin + c.H, m->fin, 1e-6f, m->tmp32, c.H, st));
   return launch_linear_f32(m->tmp32, c.H, c.img, c.H, m->proj_out_w, m->proj_out_b, c.in_ch, out,
                            c.in_ch, false, st);
+}
+
+int bonsai_dit_forward(bonsai_dit_t m, const float* img, const float* txt, const float* pooled,
+                       float timestep, float* out, void* stream) {
+  if (!m || !img || !out || (m->c.txt > 0 && !txt)) return fail(BONSAI_ERR_ARG, "dit_forward: null argument");
+  if (m->c.pooled > 0 && !pooled)
+    return fail(BONSAI_ERR_ARG, "dit_forward: the Flux.1 preset needs the pooled vector");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RC(dit_upload_timestep(m, timestep, st));
+  // The first call runs eagerly (it also performs one-time kernel set-up);
+  // later calls replay a CUDA graph of the body.  Profiling runs eagerly so
+  // every launch keeps its own events.
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  const bool use_graph = m->forwards++ > 0 && !profiling_active() && cs == cudaStreamCaptureStatusNone;
+  if (!use_graph) return dit_forward_body(m, img, txt, pooled, out, st);
+  const void* key[4] = {img, txt, pooled, out};
+  if (!m->graph || memcmp(key, m->graph_key, sizeof(key)) != 0) {
+    if (m->graph) {
+      cudaGraphExecDestroy(m->graph);
+      m->graph = nullptr;
+    }
+    // the body must see the timestep copy and the caller's earlier work:
+    // capture on the private stream, launch on the caller's.
+    const long long before = launch_counter();
+    RC(cuda_status(cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeThreadLocal),
+                   "begin capture"));
+    int rc = dit_forward_body(m, img, txt, pooled, out, m->cap_stream);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(m->cap_stream, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return cuda_status(e, "end capture");
+    e = cudaGraphInstantiate(&m->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+      m->graph = nullptr;
+      return cuda_status(e, "graph instantiate");
+    }
+    m->graph_kernels = launch_counter() - before;
+    launch_counter_add(-m->graph_kernels);  // counted again when replayed below
+    memcpy(m->graph_key, key, sizeof(key));
+  }
+  RC(cuda_status(cudaGraphLaunch(m->graph, st), "graph launch"));
+  launch_counter_add(m->graph_kernels);
+  return 0;
 }
 
 int bonsai_dit_forward_host(bonsai_dit_t m, const float* host_img, const float* host_txt,

@@ -95,6 +95,84 @@ __global__ void __launch_bounds__(256) linear_kernel(const float* __restrict__ x
   }
 }
 
+// Larger tiled f32 linear for the big edge GEMMs: 128 x 128 outputs per
+// 256-thread block, 8 x 8 per thread, k-slices of 8 double-buffered in SMEM.
+constexpr int LB = 128, LK = 8;
+// blockIdx.z selects a K slice [z*kspan, (z+1)*kspan) whose partial sum goes to
+// y + z * zstride (bias only from slice 0 when it writes the final output).
+__global__ void __launch_bounds__(256) linear128_kernel(const float* __restrict__ x,
+                                                        long long ldx, int T, int K,
+                                                        const float* __restrict__ W,
+                                                        const float* __restrict__ b, int N,
+                                                        float* __restrict__ y, long long ldy,
+                                                        int kspan, long long zstride) {
+  __shared__ __align__(16) float xs[2][LK][LB];
+  __shared__ __align__(16) float ws[2][LK][LB];
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;
+  const int t0 = blockIdx.y * LB, o0 = blockIdx.x * LB;
+  // loader mapping: thread -> (row = tid / 2, k4 = (tid % 2) * 4)
+  const int lr = tid >> 1, lk = (tid & 1) * 4;
+  auto load = [&](int buf, int k0) {
+    const int t = t0 + lr, o = o0 + lr;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int kk = k0 + lk + u;
+      xs[buf][lk + u][lr] = (t < T && kk < K) ? x[(size_t)t * ldx + kk] : 0.f;
+      ws[buf][lk + u][lr] = (o < N && kk < K) ? W[(size_t)o * K + kk] : 0.f;
+    }
+  };
+  const int kb = blockIdx.z * kspan;
+  K = min(K, kb + kspan);  // this block's slice is [kb, K)
+  y += blockIdx.z * zstride;
+  float acc[8][8] = {};
+  load(0, kb);
+  __syncthreads();
+  int buf = 0;
+  for (int k0 = kb; k0 < K; k0 += LK) {
+    if (k0 + LK < K) load(buf ^ 1, k0 + LK);
+#pragma unroll
+    for (int c = 0; c < LK; ++c) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&xs[buf][c][ty * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&xs[buf][c][ty * 8 + 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&ws[buf][c][tx * 8]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&ws[buf][c][tx * 8 + 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+    buf ^= 1;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int t = t0 + ty * 8 + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int o = o0 + tx * 8 + j;
+      if (o < N) y[(size_t)t * ldy + o] = acc[i][j] + (b ? b[o] : 0.f);
+    }
+  }
+}
+
+// y[t][o] = sum_z part[z][t][o] + b[o] (fixed order: deterministic).
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int T, int N,
+                                     const float* __restrict__ b, float* __restrict__ y,
+                                     long long ldy) {
+  const long long n = (long long)T * N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int z = 0; z < splits; ++z) acc += part[z * n + i];
+    const int t = (int)(i / N), o = (int)(i % N);
+    y[(size_t)t * ldy + o] = acc + (b ? b[o] : 0.f);
+  }
+}
+
 __global__ void silu_kernel(const float* __restrict__ x, long long n, float* __restrict__ y) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x)
@@ -111,7 +189,8 @@ __global__ void add_kernel(const float* __restrict__ a, const float* __restrict_
 }  // namespace edge
 
 int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* W, const float* b,
-                      int N, float* y, long long ldy, bool silu_in, cudaStream_t st) {
+                      int N, float* y, long long ldy, bool silu_in, cudaStream_t st,
+                      float* workspace, long long workspace_elems) {
   if (T == 0 || N == 0) return 0;
   if (T == 1) {
     const int wpb = 8;
@@ -119,8 +198,33 @@ int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* 
     return launch_status("gemv launch");
   }
   if (silu_in) return fail(-2, "linear_f32: silu input only supported for T == 1");
-  dim3 grid((N + edge::TB - 1) / edge::TB, (T + edge::TB - 1) / edge::TB);
-  edge::linear_kernel<<<grid, 256, 0, st>>>(x, ldx, T, K, W, b, N, y, ldy);
+  ProfScope prof("linear_f32", 2.0 * T * N * (double)K, 4.0 * ((double)T * K + (double)N * K + (double)T * N), st);
+  if ((long long)T * N >= 64LL * 128 * 128) {
+    dim3 grid((N + edge::LB - 1) / edge::LB, (T + edge::LB - 1) / edge::LB);
+    // Split K so that the grid covers the GPU twice, when a workspace for the
+    // partial sums is available (deterministic reduction afterwards).
+    int splits = 1;
+    const long long blocks = (long long)grid.x * grid.y;
+    while (splits < 8 && blocks * splits < 2LL * num_sms() && K / (splits * 2) >= 256 &&
+           workspace && (long long)(splits * 2) * T * N <= workspace_elems)
+      splits *= 2;
+    if (splits > 1) {
+      const int kspan = (((K + splits - 1) / splits) + edge::LK - 1) / edge::LK * edge::LK;
+      grid.z = splits;
+      edge::linear128_kernel<<<grid, 256, 0, st>>>(x, ldx, T, K, W, nullptr, N, workspace, N,
+                                                   kspan, (long long)T * N);
+      int rc = launch_status("linear_f32 split-K launch");
+      if (rc) return rc;
+      const long long n = (long long)T * N;
+      edge::splitk_reduce_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 4096), 256, 0, st>>>(
+          workspace, splits, T, N, b, y, ldy);
+      return launch_status("linear_f32 split-K reduce");
+    }
+    edge::linear128_kernel<<<grid, 256, 0, st>>>(x, ldx, T, K, W, b, N, y, ldy, K, 0);
+  } else {
+    dim3 grid((N + edge::TB - 1) / edge::TB, (T + edge::TB - 1) / edge::TB);
+    edge::linear_kernel<<<grid, 256, 0, st>>>(x, ldx, T, K, W, b, N, y, ldy);
+  }
   return launch_status("linear_f32 launch");
 }
 

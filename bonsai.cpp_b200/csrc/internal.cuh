@@ -25,7 +25,10 @@ class ProfScope {
   cudaStream_t st_;
   long long idx_ = -1;
 };
-int* device_error_word();  // device address of the per-device error word (lazily resolved)
+int* device_error_word();
+long long launch_counter();           // launches counted on this thread so far
+void launch_counter_add(long long n);  // account for kernels replayed from a CUDA graph
+bool profiling_active();              // bonsai_profile_start() in effect on this thread  // device address of the per-device error word (lazily resolved)
 int num_sms();
 
 // ------------------------------------------------------- B1_0 device weights
@@ -110,8 +113,10 @@ void rope_pair_table(const int* axes_dim, int n_axes, float theta, int* pair_axi
                      float* pair_freq);
 
 // ------------------------------------------------------------ edge ops
+// workspace (optional): f32 scratch for split-K partial sums of large-K, few-tile shapes.
 int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* W, const float* b,
-                      int N, float* y, long long ldy, bool silu_in, cudaStream_t st);
+                      int N, float* y, long long ldy, bool silu_in, cudaStream_t st,
+                      float* workspace = nullptr, long long workspace_elems = 0);
 int launch_silu_f32(const float* x, long long n, float* y, cudaStream_t st);
 int launch_add_f32(const float* a, const float* b, long long n, float* y, cudaStream_t st);
 

@@ -74,6 +74,68 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, int rows, int di
   }
 }
 
+// One 128-thread block per row: each thread keeps VPT float4 of the row in
+// registers (dim <= 512 * VPT), block-wide two-pass statistics.  Small
+// per-thread state lets 16 rows per SM be in flight, which the one-warp-
+// per-row form above cannot reach for dim = 3072.
+template <int VPT, typename OutT>
+__global__ void __launch_bounds__(128) ln_modulate_block_kernel(
+    const float* __restrict__ x, int rows, int dim, const float* __restrict__ shift,
+    const float* __restrict__ scale, float eps, OutT* __restrict__ y, long long ld_y) {
+  __shared__ float red[2][4];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * dim);
+  const int n4 = dim / 4;
+  float4 v[VPT];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = tid + i * 128;
+    v[i] = idx < n4 ? xr[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  s = warp_sum(s);
+  if (lane == 0) red[0][wid] = s;
+  __syncthreads();
+  const float mean = ((red[0][0] + red[0][1]) + (red[0][2] + red[0][3])) / dim;
+  float s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = tid + i * 128;
+    if (idx < n4) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      s2 += (a * a + b * b) + (c * c + d * d);
+    }
+  }
+  s2 = warp_sum(s2);
+  if (lane == 0) red[1][wid] = s2;
+  __syncthreads();
+  const float var = ((red[1][0] + red[1][1]) + (red[1][2] + red[1][3])) / dim;
+  const float rstd = 1.0f / sqrtf(var + eps);
+  const float4* sh4 = reinterpret_cast<const float4*>(shift);
+  const float4* sc4 = reinterpret_cast<const float4*>(scale);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = tid + i * 128;
+    if (idx >= n4) continue;
+    const float4 sh = sh4[idx], sc = sc4[idx];
+    const float o0 = ((v[i].x - mean) * rstd) * (sc.x + 1.0f) + sh.x;
+    const float o1 = ((v[i].y - mean) * rstd) * (sc.y + 1.0f) + sh.y;
+    const float o2 = ((v[i].z - mean) * rstd) * (sc.z + 1.0f) + sh.z;
+    const float o3 = ((v[i].w - mean) * rstd) * (sc.w + 1.0f) + sh.w;
+    if constexpr (sizeof(OutT) == 2) {
+      __half2 a = __floats2half2_rn(o0, o1), b = __floats2half2_rn(o2, o3);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&a);
+      pk.y = *reinterpret_cast<uint32_t*>(&b);
+      *reinterpret_cast<uint2*>(y + (size_t)row * ld_y + idx * 4) = pk;
+    } else {
+      *reinterpret_cast<float4*>(y + (size_t)row * ld_y + idx * 4) = make_float4(o0, o1, o2, o3);
+    }
+  }
+}
+
 // Generic (any dim) three-pass version for rows that do not fit registers.
 template <typename OutT>
 __global__ void ln_modulate_generic_kernel(const float* __restrict__ x, int rows, int dim,
@@ -109,6 +171,7 @@ __global__ void ln_modulate_generic_kernel(const float* __restrict__ x, int rows
 // followed by the pair rotation of rope_2d_fwd_f32 (src/b1_0_kernel.h:339-352).
 // Tokens < split use the *_lo weights (text stream of a double block).
 // One warp per row; lane handles elements 4*lane .. 4*lane+3 (two pairs).
+constexpr int QK_HEADS_PER_WARP = 4;
 __global__ void qk_norm_rope_kernel(__half* __restrict__ q, __half* __restrict__ k, int n_heads,
                                     int seq, const float* __restrict__ wq_lo,
                                     const float* __restrict__ wq_hi,
@@ -116,33 +179,46 @@ __global__ void qk_norm_rope_kernel(__half* __restrict__ q, __half* __restrict__
                                     const float* __restrict__ wk_hi, int split, float eps,
                                     const float* __restrict__ cos_t,
                                     const float* __restrict__ sin_t) {
+  // work item = (tensor, head group, token); token fastest so neighbouring
+  // warps share cos/sin rows in L1/L2.
   const int warps = blockDim.x / 32;
   const long long gw = (long long)blockIdx.x * warps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const long long rows = (long long)n_heads * seq;
-  const long long total = k ? 2 * rows : rows;
+  const int groups = (n_heads + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP;
+  const long long per_tensor = (long long)groups * seq;
+  const long long total = k ? 2 * per_tensor : per_tensor;
   if (gw >= total) return;
-  const bool is_k = gw >= rows;
-  const long long r = is_k ? gw - rows : gw;
+  const bool is_k = gw >= per_tensor;
+  const long long r = is_k ? gw - per_tensor : gw;
   const int t = (int)(r % seq);
-  __half* base = (is_k ? k : q) + r * 128;
+  const int h0 = (int)(r / seq) * QK_HEADS_PER_WARP;
+  const int nh = min(QK_HEADS_PER_WARP, n_heads - h0);
+  __half* base = (is_k ? k : q) + ((size_t)h0 * seq + t) * 128 + lane * 4;
+  const size_t hstride = (size_t)seq * 128;
   const float* w = is_k ? (t < split ? wk_lo : wk_hi) : (t < split ? wq_lo : wq_hi);
-  const uint2 raw = *reinterpret_cast<const uint2*>(base + lane * 4);
-  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-  const float ss = warp_sum((a.x * a.x + a.y * a.y) + (b.x * b.x + b.y * b.y));
-  const float sc = 1.0f / sqrtf(ss / 128.0f + eps);
+  uint2 raw[QK_HEADS_PER_WARP];
+#pragma unroll
+  for (int i = 0; i < QK_HEADS_PER_WARP; ++i)
+    if (i < nh) raw[i] = *reinterpret_cast<const uint2*>(base + i * hstride);
   const float4 w4 = *reinterpret_cast<const float4*>(w + lane * 4);
-  const float x0 = (a.x * sc) * w4.x, x1 = (a.y * sc) * w4.y;
-  const float x2 = (b.x * sc) * w4.z, x3 = (b.y * sc) * w4.w;
   const float2 c2 = *reinterpret_cast<const float2*>(cos_t + (size_t)t * 64 + lane * 2);
   const float2 s2 = *reinterpret_cast<const float2*>(sin_t + (size_t)t * 64 + lane * 2);
-  const __half2 o01 = __floats2half2_rn(x0 * c2.x - x1 * s2.x, x0 * s2.x + x1 * c2.x);
-  const __half2 o23 = __floats2half2_rn(x2 * c2.y - x3 * s2.y, x2 * s2.y + x3 * c2.y);
-  uint2 out;
-  out.x = *reinterpret_cast<const uint32_t*>(&o01);
-  out.y = *reinterpret_cast<const uint32_t*>(&o23);
-  *reinterpret_cast<uint2*>(base + lane * 4) = out;
+#pragma unroll
+  for (int i = 0; i < QK_HEADS_PER_WARP; ++i) {
+    if (i >= nh) break;
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw[i].x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw[i].y));
+    const float ss = warp_sum((a.x * a.x + a.y * a.y) + (b.x * b.x + b.y * b.y));
+    const float sc = 1.0f / sqrtf(ss / 128.0f + eps);
+    const float x0 = (a.x * sc) * w4.x, x1 = (a.y * sc) * w4.y;
+    const float x2 = (b.x * sc) * w4.z, x3 = (b.y * sc) * w4.w;
+    const __half2 o01 = __floats2half2_rn(x0 * c2.x - x1 * s2.x, x0 * s2.x + x1 * c2.x);
+    const __half2 o23 = __floats2half2_rn(x2 * c2.y - x3 * s2.y, x2 * s2.y + x3 * c2.y);
+    uint2 out;
+    out.x = *reinterpret_cast<const uint32_t*>(&o01);
+    out.y = *reinterpret_cast<const uint32_t*>(&o23);
+    *reinterpret_cast<uint2*>(base + i * hstride) = out;
+  }
 }
 
 // --------------------------------------------------------- f32 drop-ins
@@ -215,7 +291,9 @@ static int ln_mod_impl(const float* x, int rows, int dim, const float* shift, co
                    (reinterpret_cast<uintptr_t>(y) & (sizeof(OutT) == 2 ? 7 : 15)) == 0;
   const int n4 = dim / 4;
   ProfScope prof("ln_modulate", 0.0, (double)rows * dim * (4 + sizeof(OutT)), st);
-  if (vec && n4 <= 24 * 32)
+  if (vec && n4 <= 6 * 128)
+    pw::ln_modulate_block_kernel<6, OutT><<<rows, 128, 0, st>>>(x, rows, dim, shift, scale, eps, y, ld_y);
+  else if (vec && n4 <= 24 * 32)
     pw::ln_modulate_kernel<24, OutT><<<row_grid(rows, wpb), wpb * 32, 0, st>>>(x, rows, dim, shift, scale, eps, y, ld_y);
   else if (vec && n4 <= 48 * 32)
     pw::ln_modulate_kernel<48, OutT><<<row_grid(rows, wpb), wpb * 32, 0, st>>>(x, rows, dim, shift, scale, eps, y, ld_y);
@@ -242,9 +320,11 @@ int launch_qk_norm_rope(__half* q, __half* k, int n_heads, int seq, const float*
   if (!q || !wq_lo || !wq_hi || !cos_t || !sin_t || (k && (!wk_lo || !wk_hi)))
     return fail(-1, "qk_norm_rope: null argument");
   const long long rows = (long long)n_heads * seq * (k ? 2 : 1);
+  const long long items = (long long)((n_heads + pw::QK_HEADS_PER_WARP - 1) / pw::QK_HEADS_PER_WARP) *
+                          seq * (k ? 2 : 1);
   const int wpb = 8;
   ProfScope prof("qk_norm_rope", 0.0, (double)rows * 128 * 4, st);
-  pw::qk_norm_rope_kernel<<<row_grid(rows, wpb), wpb * 32, 0, st>>>(
+  pw::qk_norm_rope_kernel<<<row_grid(items, wpb), wpb * 32, 0, st>>>(
       q, k, n_heads, seq, wq_lo, wq_hi, wk_lo, wk_hi, split, eps, cos_t, sin_t);
   return launch_status("qk_norm_rope launch");
 }
