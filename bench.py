@@ -43,6 +43,8 @@ L = IMG + TXT
 METRIC = "ms/denoise step @1024² Flux-DiT (1–8 B200); B1_0 GEMM & attn % of bf16 peak"
 WORKLOAD = ("flux1-schnell DiT denoise step @1024^2: 19 double + 38 single blocks, "
             "L = 512 text + 4096 image tokens, all block linears B1_0 (1-bit)")
+WORKLOAD_2048 = ("flux1-schnell DiT denoise step @2048^2: 19 double + 38 single blocks, "
+                 "L = 512 text + 16384 image tokens, one image split across the GPUs")
 
 
 def peaks():
@@ -291,9 +293,18 @@ def run_bonsai(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     bb.init(local)
+    split = args.workload == "2048"
+    global IMG, GRID, L
+    if split:  # BASELINE config 5(b): 128 x 128 latent tokens + 512 text tokens
+        IMG, GRID = 16384, 128
+        L = IMG + TXT
     model = bb.Dit(bb.PRESET_FLUX1, IMG, TXT, GRID, GRID, seed=1234)
+    if split:
+        from bonsai_b200 import headsplit
+        if world > 1:
+            model.set_partition(rank, world)
 
-    rng = np.random.default_rng(1000 + rank)
+    rng = np.random.default_rng(1000 + (0 if split else rank))  # split: one shared image
     img_h = torch.from_numpy(rng.standard_normal((IMG, IN_CH)).astype(np.float32)).pin_memory()
     txt_h = torch.from_numpy(rng.standard_normal((TXT, CTX)).astype(np.float32)).pin_memory()
     pooled_h = torch.from_numpy(rng.standard_normal(POOLED).astype(np.float32)).pin_memory()
@@ -315,8 +326,15 @@ def run_bonsai(args):
         return float(t.item())
 
     stream = torch.cuda.current_stream()
+
+    def step(t):
+        if split:
+            headsplit.forward(model, img_d, txt_d, pooled_d, t, out_d)
+        else:
+            model.forward(img_d, txt_d, pooled_d, t, out_d)
+
     for i in range(W):
-        model.forward(img_d, txt_d, pooled_d, ts[i], out_d)
+        step(ts[i])
     torch.cuda.synchronize()
     assert bb.device_error() == 0
 
@@ -329,7 +347,7 @@ def run_bonsai(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(K):
-        model.forward(img_d, txt_d, pooled_d, ts[i], out_d)
+        step(ts[i])
     e1.record(stream)
     torch.cuda.synchronize()
     launches = bb.launch_count()
@@ -345,7 +363,7 @@ def run_bonsai(args):
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     p0.record(stream)
     for i in range(K):
-        model.forward(img_d, txt_d, pooled_d, ts[i], out_d)
+        step(ts[i])
     p1.record(stream)
     torch.cuda.synchronize()
     prof = bb.profile_stop()
@@ -354,14 +372,25 @@ def run_bonsai(args):
     # ---- end to end through the host-buffer C-ABI entry point
     out_np = out_h.numpy()
     img_np, txt_np, pooled_np = img_h.numpy(), txt_h.numpy(), pooled_h.numpy()
+    def step_host(t):
+        if split:  # copies in, partitioned step, prediction out
+            img_d.copy_(img_h, non_blocking=True)
+            txt_d.copy_(txt_h, non_blocking=True)
+            pooled_d.copy_(pooled_h, non_blocking=True)
+            headsplit.forward(model, img_d, txt_d, pooled_d, t, out_d)
+            out_h.copy_(out_d, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        else:
+            model.forward_host(img_np, txt_np, pooled_np, t, out_np)
+
     for i in range(2):
-        model.forward_host(img_np, txt_np, pooled_np, ts[i], out_np)
+        step_host(ts[i])
     barrier()
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for i in range(K):
-        model.forward_host(img_np, txt_np, pooled_np, ts[i], out_np)
+        step_host(ts[i])
     f1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -378,13 +407,17 @@ def run_bonsai(args):
                 for k, v in prof.items()}
     line = {
         "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": K,
-        "warmup": W, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "weak",
+        "warmup": W, "ms_per_step": round(ms, 3), "higher_is_better": False,
+        "scaling": "strong" if split else "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": world, "img_tokens": IMG,
-                   "txt_tokens": TXT, "parallelism": f"dp{world} (one image per GPU, no collective)",
+        "config": {"workload": WORKLOAD_2048 if split else WORKLOAD,
+                   "global_batch": 1 if split else world, "img_tokens": IMG,
+                   "txt_tokens": TXT,
+                   "parallelism": (f"head/row split over {world} GPUs (NCCL all-gather + all-to-all per block)"
+                                   if split else f"dp{world} (one image per GPU, no collective)"),
                    "l2": "inputs larger than L2: every step streams all 2.2 GB of B1_0 weights"},
-        "images_per_s": round(world * 1000.0 / ms, 3),
-        "step_tflops": round(step_flops() / (ms / 1e3) / 1e12, 1),
+        "images_per_s": round((1 if split else world) * 1000.0 / ms, 3),
+        "step_tflops": round(step_flops() / (ms / 1e3) / 1e12 * (1 if split else world), 1),
         "roofline": {"bound": "tensor", "kernel": "b1_gemm", "achieved": round(gemm_tf, 1),
                      "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
                      "frac": round(gemm_tf / pk["bf16_sustained"], 4),
@@ -404,7 +437,7 @@ def run_bonsai(args):
                 "h2d_bytes_per_step": (IMG * IN_CH + TXT * CTX + POOLED + 256) * 4,
                 "d2h_bytes_per_step": IMG * IN_CH * 4, "output_finite": finite},
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not split:
         threads = os.cpu_count() or 1
         with stdout_to_stderr():
             cs = CpuSample(threads)
@@ -427,6 +460,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["bonsai", "reference"], default="bonsai")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["1024", "2048"], default="1024",
+                    help="1024: config 4, one image per GPU (data parallel, default); "
+                         "2048: config 5(b), one 2048^2 image split by heads/rows across the GPUs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -67,6 +67,11 @@ SIGNATURES = {
     "bonsai_dit_double_block": (_c_int, [_vp, _c_int, _vp]),
     "bonsai_dit_single_block": (_c_int, [_vp, _c_int, _vp]),
     "bonsai_dit_weight": (_c_ll, [_vp, ctypes.c_char_p, _vp, _c_ll]),
+    "bonsai_dit_set_partition": (_c_int, [_vp, _c_int, _c_int]),
+    "bonsai_dit_buffer": (_c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(_c_ll)]),
+    "bonsai_dit_begin": (_c_int, [_vp, _vp, _vp, _vp, _fp, _vp]),
+    "bonsai_dit_phase": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp]),
+    "bonsai_dit_end": (_c_int, [_vp, _vp, _vp]),
 }
 
 
@@ -290,8 +295,46 @@ class Dit:
         check(lib().bonsai_dit_get_state(self.handle, hidden.data_ptr(), stream_ptr(stream)),
               "bonsai_dit_get_state")
 
+    # ---- partitioned (multi-GPU) driving, see bonsai_b200.headsplit
+    def set_partition(self, rank: int, world: int):
+        check(lib().bonsai_dit_set_partition(self.handle, rank, world), "bonsai_dit_set_partition")
+
+    def buffer(self, name: str, dtype, shape):
+        """Engine buffer as a torch tensor view (no copy)."""
+        import torch
+        ptr, nbytes = _vp(), _c_ll()
+        check(lib().bonsai_dit_buffer(self.handle, name.encode(), ctypes.byref(ptr),
+                                      ctypes.byref(nbytes)), f"bonsai_dit_buffer({name})")
+        return _wrap_device(ptr.value, nbytes.value, dtype, shape)
+
+    def begin(self, img, txt, pooled, t: float, stream=None):
+        check(lib().bonsai_dit_begin(self.handle, img.data_ptr(),
+                                     txt.data_ptr() if txt is not None else None,
+                                     pooled.data_ptr() if pooled is not None else None,
+                                     float(t), stream_ptr(stream)), "bonsai_dit_begin")
+
+    def phase(self, kind: int, block: int, phase: int, stream=None):
+        check(lib().bonsai_dit_phase(self.handle, kind, block, phase, stream_ptr(stream)),
+              "bonsai_dit_phase")
+
+    def end(self, out, stream=None):
+        check(lib().bonsai_dit_end(self.handle, out.data_ptr(), stream_ptr(stream)), "bonsai_dit_end")
+
     def double_block(self, i: int, stream=None):
         check(lib().bonsai_dit_double_block(self.handle, i, stream_ptr(stream)), "double_block")
 
     def single_block(self, i: int, stream=None):
         check(lib().bonsai_dit_single_block(self.handle, i, stream_ptr(stream)), "single_block")
+
+
+def _wrap_device(ptr: int, nbytes: int, dtype, shape):
+    """A torch tensor aliasing device memory owned by the engine (no copy)."""
+    import torch
+
+    class _Holder:
+        def __init__(self, p, n):
+            self.__cuda_array_interface__ = {
+                "shape": (n,), "typestr": "|u1", "data": (p, False), "version": 3}
+
+    flat = torch.as_tensor(_Holder(ptr, nbytes), device="cuda")
+    return flat.view(dtype).view(shape)

@@ -52,11 +52,20 @@ constexpr int NUM_THREADS = (WARP_EPI0 + EPI_WARPS) * 32;
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * X_STAGE_BYTES +
                            STAGES * RAW_STAGE_BYTES + 256 /*barriers etc*/;
 
+__device__ __forceinline__ int sel_ftile(int fidx, int fcount, const int* fbase) {
+  const int g = fidx / fcount;
+  return fbase[g] + (fidx - g * fcount);
+}
+
 struct Params {
   int tokens;
   int n_rows;
   int n_ftiles, n_ttiles, k_blocks;
   int num_tiles;
+  // Weight-tile selection: the nf = fgroups * fcount selected feature tiles
+  // are fbase[g] + i (g < fgroups, i < fcount).
+  int nf, fcount, fgroups;
+  int fbase[kMaxTileGroups];
   const uint32_t* chunks;
   int nseg;
   EpiSeg seg[kMaxSegs];
@@ -152,8 +161,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int ttile = tile / p.n_ftiles;
-        const int ftile = tile - ttile * p.n_ftiles;
+        const int ttile = tile / p.nf;
+        const int ftile = sel_ftile(tile - ttile * p.nf, p.fcount, p.fbase);
         const uint32_t* wsrc = p.chunks + (size_t)ftile * k_blocks * kChunkWords;
         for (int kb = 0; kb < k_blocks; ++kb, ++it) {
           const int s = it % STAGES;
@@ -276,8 +285,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint32_t lt = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
-      const int ttile = tile / p.n_ftiles;
-      const int ftile = tile - ttile * p.n_ftiles;
+      const int ttile = tile / p.nf;
+      const int ftile = sel_ftile(tile - ttile * p.nf, p.fcount, p.fbase);
       const uint32_t b = lt & 1;
       const uint32_t dph = (lt >> 1) & 1;
       const bool good = wait_bar(&dfull[b], dph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE);
@@ -490,7 +499,7 @@ int launch_b1_retile(const uint8_t* dev_packed, B1Weight& w, cudaStream_t st) {
 }
 
 int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, const EpiSeg* segs,
-                   int nseg, bool x_bf16, cudaStream_t st) {
+                   int nseg, bool x_bf16, cudaStream_t st, const TileSel* sel) {
   if (tokens < 0) return fail(-1, "b1_gemm: negative token count");
   if (tokens == 0) return 0;
   if (!x || !w.chunks) return fail(-1, "b1_gemm: null activation or weight");
@@ -507,7 +516,22 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
   p.n_ftiles = w.n_ftiles;
   p.n_ttiles = (tokens + gemm::BN - 1) / gemm::BN;
   p.k_blocks = w.k_blocks;
-  p.num_tiles = p.n_ftiles * p.n_ttiles;
+  if (sel) {
+    if (sel->groups < 1 || sel->groups > kMaxTileGroups || sel->count < 1)
+      return fail(-1, "b1_gemm: bad tile selection");
+    for (int g = 0; g < sel->groups; ++g)
+      if (sel->base[g] < 0 || sel->base[g] + sel->count > w.n_ftiles)
+        return fail(-1, "b1_gemm: tile selection outside the weight");
+    p.fgroups = sel->groups;
+    p.fcount = sel->count;
+    for (int g = 0; g < sel->groups; ++g) p.fbase[g] = sel->base[g];
+  } else {
+    p.fgroups = 1;
+    p.fcount = w.n_ftiles;
+    p.fbase[0] = 0;
+  }
+  p.nf = p.fgroups * p.fcount;
+  p.num_tiles = p.nf * p.n_ttiles;
   p.chunks = w.chunks;
   p.nseg = nseg;
   for (int i = 0; i < nseg; ++i) p.seg[i] = segs[i];
@@ -529,8 +553,10 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
     const double per = (m == EPI_F32) ? 4 : (m == EPI_RESID_F32) ? 8 : (m == EPI_SWIGLU_F16) ? 1 : 2;
     out_bytes += rows * tokens * per;
   }
-  ProfScope prof("b1_gemm", 2.0 * tokens * w.n_rows * (double)w.k_in,
-                 (double)tokens * w.k_in * 2 + (double)w.n_rows * w.k_in * 6 / 32 + out_bytes, st);
+  const double rows_done = sel ? std::min<double>(w.n_rows, 128.0 * p.nf) : (double)w.n_rows;
+  if (sel) out_bytes *= rows_done / std::max(1, w.n_rows);
+  ProfScope prof("b1_gemm", 2.0 * tokens * rows_done * (double)w.k_in,
+                 (double)tokens * w.k_in * 2 + rows_done * w.k_in * 6 / 32 + out_bytes, st);
   kern<<<grid, gemm::NUM_THREADS, gemm::SMEM_BYTES, st>>>(xmap, p);
   return launch_status("b1_gemm_kernel launch");
 }

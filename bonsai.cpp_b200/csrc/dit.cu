@@ -151,6 +151,10 @@ struct bonsai_dit {
   const void* graph_key[4] = {nullptr, nullptr, nullptr, nullptr};
   long long graph_kernels = 0;
   int forwards = 0;
+  // Multi-GPU partition (bonsai_dit_set_partition): this rank owns token
+  // rows [r0, r1) and heads [h0, h0 + hl).  world == 1: everything.
+  int rank = 0, world = 1;
+  int r0 = 0, r1 = 0, h0 = 0, hl = 24;
   // device copies of caller inputs for the host-buffer entry point
   float *in_img = nullptr, *in_txt = nullptr, *in_pooled = nullptr, *out_buf = nullptr;
 };
@@ -275,61 +279,139 @@ int compute_mods(bonsai_dit* m, cudaStream_t st) {
                            2 * c.H, false, st);
 }
 
-int run_double(bonsai_dit* m, int i, cudaStream_t st) {
+// Row ranges of this rank inside the text [0, Lt) and image [Lt, L) streams.
+struct Span {
+  int a, b;
+  int n() const { return b > a ? b - a : 0; }
+};
+Span own_txt(const bonsai_dit* m) { return {std::max(0, m->r0), std::min(m->c.txt, m->r1)}; }
+Span own_img(const bonsai_dit* m) { return {std::max(m->c.txt, m->r0), std::min(m->c.L, m->r1)}; }
+
+// QKV tiles of this rank's heads: q, k and v parts of the fused [3H] weight.
+TileSel head_tiles(const bonsai_dit* m) {
+  TileSel t;
+  t.groups = 3;
+  t.count = m->hl;
+  for (int g = 0; g < 3; ++g) t.base[g] = g * m->c.heads + m->h0;
+  return t;
+}
+
+// The three phases of a double block (src/diffuser_graph.cpp:341-466).
+// phase 0: LN-modulate (attention) of this rank's rows -> xm           (:347-352)
+// phase 1: Q/K/V of this rank's heads on every row, Q/K RMSNorm + RoPE,
+//          joint attention of those heads -> cat[:, heads]           (:354-416)
+// phase 2: out-projection + gate-residual, LN-modulate, MLP + gate-residual
+//          on this rank's rows (needs cat[own rows, all heads])      (:434-460)
+int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
   const Cfg& c = m->c;
   const DoubleW& w = m->dbl[i];
-  const int H = c.H, Lt = c.txt, Li = c.img, C = c.C();
+  const int H = c.H, Lt = c.txt, C = c.C();
   const float *mi, *mt;
   double_mods(m, i, &mi, &mt);
-  float* h_txt = m->hidden;
-  float* h_img = m->hidden + (size_t)Lt * H;
-  __half* x_txt = m->xm;
-  __half* x_img = m->xm + (size_t)Lt * H;
-  __half* a_txt = m->cat;
-  __half* a_img = m->cat + (size_t)Lt * C;
-  // attention sub-block: LN-modulate (:347-352), Q/K/V (:354-369) scattered head-major
-  RC(launch_ln_modulate_f16(h_txt, Lt, H, mt + 0 * H, mt + 1 * H, 1e-6f, x_txt, H, st));
-  RC(launch_ln_modulate_f16(h_img, Li, H, mi + 0 * H, mi + 1 * H, 1e-6f, x_img, H, st));
-  EpiSeg s = seg_qkv(c, 3 * H, m->qkv, 0);
-  RC(launch_b1_gemm(x_txt, H, Lt, w.txt_qkv, &s, 1, false, st));
-  s = seg_qkv(c, 3 * H, m->qkv, Lt);
-  RC(launch_b1_gemm(x_img, H, Li, w.img_qkv, &s, 1, false, st));
-  // rms_norm_qk (:371-374) + RoPE (:383-384), text rows use the added-stream weights
-  __half* q = m->qkv;
-  __half* k = m->qkv + (size_t)c.heads * c.L * c.hd;
-  __half* v = k + (size_t)c.heads * c.L * c.hd;
-  RC(launch_qk_norm_rope(q, k, c.heads, c.L, w.nq_txt, w.nq_img, w.nk_txt, w.nk_img, Lt, 1e-6f,
-                         m->cos_t, m->sin_t, st));
-  // joint attention over [txt; img] (:393-416)
-  RC(launch_attention(q, k, v, c.heads, c.L, c.hd, 1.0f / sqrtf((float)c.hd), m->cat, C, st));
-  // out projections + gate-residual (:434-442)
-  s = seg_of(EPI_RESID_F32, 0, H, h_txt, H, 0, mt + 2 * H);
-  RC(launch_b1_gemm(a_txt, C, Lt, w.txt_out, &s, 1, false, st));
-  s = seg_of(EPI_RESID_F32, 0, H, h_img, H, 0, mi + 2 * H);
-  RC(launch_b1_gemm(a_img, C, Li, w.img_out, &s, 1, false, st));
-  // MLP sub-block (:444-460): activation written into cat[:, H:H+mlp]
-  RC(launch_ln_modulate_f16(h_txt, Lt, H, mt + 3 * H, mt + 4 * H, 1e-6f, x_txt, H, st));
-  RC(launch_ln_modulate_f16(h_img, Li, H, mi + 3 * H, mi + 4 * H, 1e-6f, x_img, H, st));
+  const Span tx = own_txt(m), im = own_img(m);
+  if (phase == 0) {
+    RC(launch_ln_modulate_f16(m->hidden + (size_t)tx.a * H, tx.n(), H, mt + 0 * H, mt + 1 * H,
+                              1e-6f, m->xm + (size_t)tx.a * H, H, st));
+    RC(launch_ln_modulate_f16(m->hidden + (size_t)im.a * H, im.n(), H, mi + 0 * H, mi + 1 * H,
+                              1e-6f, m->xm + (size_t)im.a * H, H, st));
+    return 0;
+  }
+  if (phase == 1) {
+    const TileSel sel = head_tiles(m);
+    const TileSel* ps = m->world > 1 ? &sel : nullptr;
+    EpiSeg s = seg_qkv(c, 3 * H, m->qkv, 0);
+    RC(launch_b1_gemm(m->xm, H, Lt, w.txt_qkv, &s, 1, false, st, ps));
+    s = seg_qkv(c, 3 * H, m->qkv, Lt);
+    RC(launch_b1_gemm(m->xm + (size_t)Lt * H, H, c.img, w.img_qkv, &s, 1, false, st, ps));
+    const size_t hs = (size_t)c.L * c.hd;  // one head of one of q/k/v
+    __half* q = m->qkv + (size_t)m->h0 * hs;
+    __half* k = m->qkv + (size_t)(c.heads + m->h0) * hs;
+    __half* v = m->qkv + (size_t)(2 * c.heads + m->h0) * hs;
+    // rms_norm_qk (:371-374) + RoPE (:383-384); text rows use the added-stream weights
+    RC(launch_qk_norm_rope(q, k, m->hl, c.L, w.nq_txt, w.nq_img, w.nk_txt, w.nk_img, Lt, 1e-6f,
+                           m->cos_t, m->sin_t, st));
+    // joint attention over [txt; img] (:393-416)
+    return launch_attention(q, k, v, m->hl, c.L, c.hd, 1.0f / sqrtf((float)c.hd),
+                            m->cat + (size_t)m->h0 * c.hd, C, st);
+  }
+  // phase 2, per stream on this rank's rows
   const int act_mode = c.swiglu ? EPI_SWIGLU_F16 : EPI_GELU_F16;
-  s = seg_of(act_mode, 0, c.mlp_in_rows, a_txt, C, H, nullptr);
-  RC(launch_b1_gemm(x_txt, H, Lt, w.txt_mlp_in, &s, 1, false, st));
-  s = seg_of(act_mode, 0, c.mlp_in_rows, a_img, C, H, nullptr);
-  RC(launch_b1_gemm(x_img, H, Li, w.img_mlp_in, &s, 1, false, st));
-  s = seg_of(EPI_RESID_F32, 0, H, h_txt, H, 0, mt + 5 * H);
-  RC(launch_b1_gemm(a_txt + H, C, Lt, w.txt_mlp_out, &s, 1, false, st));
-  s = seg_of(EPI_RESID_F32, 0, H, h_img, H, 0, mi + 5 * H);
-  RC(launch_b1_gemm(a_img + H, C, Li, w.img_mlp_out, &s, 1, false, st));
+  for (int sidx = 0; sidx < 2; ++sidx) {
+    const Span sp = sidx == 0 ? tx : im;
+    if (sp.n() == 0) continue;
+    const float* md = sidx == 0 ? mt : mi;
+    const B1Weight& w_out = sidx == 0 ? w.txt_out : w.img_out;
+    const B1Weight& w_in = sidx == 0 ? w.txt_mlp_in : w.img_mlp_in;
+    const B1Weight& w_o2 = sidx == 0 ? w.txt_mlp_out : w.img_mlp_out;
+    float* h = m->hidden + (size_t)sp.a * H;
+    __half* x = m->xm + (size_t)sp.a * H;
+    __half* a = m->cat + (size_t)sp.a * C;
+    EpiSeg s = seg_of(EPI_RESID_F32, 0, H, h, H, 0, md + 2 * H);
+    RC(launch_b1_gemm(a, C, sp.n(), w_out, &s, 1, false, st));
+    RC(launch_ln_modulate_f16(h, sp.n(), H, md + 3 * H, md + 4 * H, 1e-6f, x, H, st));
+    s = seg_of(act_mode, 0, c.mlp_in_rows, a, C, H, nullptr);
+    RC(launch_b1_gemm(x, H, sp.n(), w_in, &s, 1, false, st));
+    s = seg_of(EPI_RESID_F32, 0, H, h, H, 0, md + 5 * H);
+    RC(launch_b1_gemm(a + H, C, sp.n(), w_o2, &s, 1, false, st));
+  }
   return 0;
 }
 
-int run_single(bonsai_dit* m, int i, cudaStream_t st) {
+// The three phases of a single block (src/diffuser_graph.cpp:476-542).
+// phase 0: LN-modulate of this rank's rows -> xm                      (:479-480)
+// phase 1: Q/K/V rows of to_qkv_mlp_proj for this rank's heads on every
+//          row, Q/K RMSNorm + RoPE, attention of those heads -> cat    (:482-519)
+// phase 2: MLP rows of to_qkv_mlp_proj + activation, then to_out and the
+//          gate-residual on this rank's rows                          (:533-538)
+int single_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
   const Cfg& c = m->c;
   const SingleW& w = m->sgl[i];
   const int H = c.H, L = c.L, C = c.C();
   const float* md = single_mods(m, i);
-  // LN-modulate (:479-480)
-  RC(launch_ln_modulate_f16(m->hidden, L, H, md, md + H, 1e-6f, m->xm, H, st));
-  // to_qkv_mlp_proj (:482-486): rows [0,3H) -> head-major Q/K/V, rest -> activation in cat
+  const int rows = m->r1 - m->r0;
+  if (phase == 0)
+    return launch_ln_modulate_f16(m->hidden + (size_t)m->r0 * H, rows, H, md, md + H, 1e-6f,
+                                  m->xm + (size_t)m->r0 * H, H, st);
+  if (phase == 1) {
+    TileSel sel = head_tiles(m);
+    EpiSeg s = seg_qkv(c, 3 * H, m->qkv, 0);
+    RC(launch_b1_gemm(m->xm, H, L, w.proj, &s, 1, false, st, &sel));
+    const size_t hs = (size_t)L * c.hd;
+    __half* q = m->qkv + (size_t)m->h0 * hs;
+    __half* k = m->qkv + (size_t)(c.heads + m->h0) * hs;
+    __half* v = m->qkv + (size_t)(2 * c.heads + m->h0) * hs;
+    RC(launch_qk_norm_rope(q, k, m->hl, L, w.nq, w.nq, w.nk, w.nk, L, 1e-6f, m->cos_t, m->sin_t, st));
+    return launch_attention(q, k, v, m->hl, L, c.hd, 1.0f / sqrtf((float)c.hd),
+                            m->cat + (size_t)m->h0 * c.hd, C, st);
+  }
+  // MLP part of to_qkv_mlp_proj (rows [3H, 3H + mlp_in_rows)) on this rank's rows
+  TileSel mlp;
+  mlp.groups = 1;
+  mlp.base[0] = 3 * H / 128;
+  mlp.count = (c.mlp_in_rows + 127) / 128;
+  EpiSeg s = seg_of(c.swiglu ? EPI_SWIGLU_F16 : EPI_GELU_F16, 3 * H, 3 * H + c.mlp_in_rows,
+                    m->cat + (size_t)m->r0 * C, C, H, nullptr);
+  RC(launch_b1_gemm(m->xm + (size_t)m->r0 * H, H, rows, w.proj, &s, 1, false, st, &mlp));
+  s = seg_of(EPI_RESID_F32, 0, H, m->hidden + (size_t)m->r0 * H, H, 0, md + 2 * H);
+  return launch_b1_gemm(m->cat + (size_t)m->r0 * C, C, rows, w.out, &s, 1, false, st);
+}
+
+int run_double(bonsai_dit* m, int i, cudaStream_t st) {
+  for (int ph = 0; ph < 3; ++ph) RC(double_phase(m, i, ph, st));
+  return 0;
+}
+
+int run_single(bonsai_dit* m, int i, cudaStream_t st) {
+  if (m->world > 1) {
+    for (int ph = 0; ph < 3; ++ph) RC(single_phase(m, i, ph, st));
+    return 0;
+  }
+  // One rank: the fused to_qkv_mlp_proj GEMM covers both segments in one launch.
+  const Cfg& c = m->c;
+  const SingleW& w = m->sgl[i];
+  const int H = c.H, L = c.L, C = c.C();
+  const float* md = single_mods(m, i);
+  RC(single_phase(m, i, 0, st));
   EpiSeg segs[2];
   segs[0] = seg_qkv(c, 3 * H, m->qkv, 0);
   segs[1] = seg_of(c.swiglu ? EPI_SWIGLU_F16 : EPI_GELU_F16, 3 * H, 3 * H + c.mlp_in_rows, m->cat,
@@ -338,10 +420,8 @@ int run_single(bonsai_dit* m, int i, cudaStream_t st) {
   __half* q = m->qkv;
   __half* k = m->qkv + (size_t)c.heads * L * c.hd;
   __half* v = k + (size_t)c.heads * L * c.hd;
-  // rms_norm_qk + RoPE (:490-499), attention (:501-519) into cat[:, 0:H]
   RC(launch_qk_norm_rope(q, k, c.heads, L, w.nq, w.nq, w.nk, w.nk, L, 1e-6f, m->cos_t, m->sin_t, st));
   RC(launch_attention(q, k, v, c.heads, L, c.hd, 1.0f / sqrtf((float)c.hd), m->cat, C, st));
-  // to_out on concat(attn, mlp_act) + gate-residual (:533-538)
   EpiSeg s = seg_of(EPI_RESID_F32, 0, H, m->hidden, H, 0, md + 2 * H);
   return launch_b1_gemm(m->cat, C, L, w.out, &s, 1, false, st);
 }
@@ -380,6 +460,10 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
   c.img = cfg->img_tokens;
   c.txt = cfg->txt_tokens;
   c.L = c.img + c.txt;
+  m->r0 = 0;
+  m->r1 = c.L;
+  m->h0 = 0;
+  m->hl = c.heads;
   c.grid_h = cfg->grid_h;
   c.grid_w = cfg->grid_w;
   c.seed = cfg->seed;
@@ -600,6 +684,9 @@ int bonsai_dit_forward(bonsai_dit_t m, const float* img, const float* txt, const
   if (!m || !img || !out || (m->c.txt > 0 && !txt)) return fail(BONSAI_ERR_ARG, "dit_forward: null argument");
   if (m->c.pooled > 0 && !pooled)
     return fail(BONSAI_ERR_ARG, "dit_forward: the Flux.1 preset needs the pooled vector");
+  if (m->world > 1)
+    return fail(BONSAI_ERR_ARG,
+                "dit_forward: a partitioned model is driven with bonsai_dit_begin/phase/end");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   RC(dit_upload_timestep(m, timestep, st));
   // The first call runs eagerly (it also performs one-time kernel set-up);
@@ -684,6 +771,85 @@ int bonsai_dit_double_block(bonsai_dit_t m, int i, void* stream) {
 int bonsai_dit_single_block(bonsai_dit_t m, int i, void* stream) {
   if (!m || i < 0 || i >= m->c.depth_single) return fail(BONSAI_ERR_ARG, "dit_single_block: bad block index");
   return run_single(m, i, static_cast<cudaStream_t>(stream));
+}
+
+int bonsai_dit_set_partition(bonsai_dit_t m, int rank, int world) {
+  if (!m || world < 1 || rank < 0 || rank >= world)
+    return fail(BONSAI_ERR_ARG, "dit_set_partition: need 0 <= rank < world");
+  const Cfg& c = m->c;
+  if (c.heads % world != 0 || c.L % world != 0)
+    return fail(BONSAI_ERR_ARG, "dit_set_partition: heads (" + std::to_string(c.heads) +
+                                    ") and tokens (" + std::to_string(c.L) +
+                                    ") must both divide by world");
+  m->rank = rank;
+  m->world = world;
+  const int rows = c.L / world;
+  m->r0 = rank * rows;
+  m->r1 = m->r0 + rows;
+  m->hl = c.heads / world;
+  m->h0 = rank * m->hl;
+  if (m->graph) {
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  return 0;
+}
+
+int bonsai_dit_buffer(bonsai_dit_t m, const char* name, void** ptr, long long* bytes) {
+  if (!m || !name || !ptr) return fail(BONSAI_ERR_ARG, "dit_buffer: null argument");
+  const Cfg& c = m->c;
+  const std::string n = name;
+  long long b = 0;
+  if (n == "hidden") { *ptr = m->hidden; b = (long long)c.L * c.H * 4; }
+  else if (n == "xm") { *ptr = m->xm; b = (long long)c.L * c.H * 2; }
+  else if (n == "cat") { *ptr = m->cat; b = (long long)c.L * c.C() * 2; }
+  else if (n == "qkv") { *ptr = m->qkv; b = 3LL * c.heads * c.L * c.hd * 2; }
+  else return fail(BONSAI_ERR_ARG, "dit_buffer: unknown buffer " + n);
+  if (bytes) *bytes = b;
+  return 0;
+}
+
+int bonsai_dit_begin(bonsai_dit_t m, const float* img, const float* txt, const float* pooled,
+                     float timestep, void* stream) {
+  if (!m || !img || (m->c.txt > 0 && !txt)) return fail(BONSAI_ERR_ARG, "dit_begin: null argument");
+  if (m->c.pooled > 0 && !pooled) return fail(BONSAI_ERR_ARG, "dit_begin: the Flux.1 preset needs the pooled vector");
+  const Cfg& c = m->c;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RC(dit_upload_timestep(m, timestep, st));
+  // input projections of this rank's rows (:283-286)
+  const Span tx = own_txt(m), im = own_img(m);
+  RC(launch_linear_f32(txt + (size_t)tx.a * c.ctx_dim, c.ctx_dim, tx.n(), c.ctx_dim, m->txt_in_w,
+                       m->txt_in_b, c.H, m->hidden + (size_t)tx.a * c.H, c.H, false, st, m->tmp32,
+                       (long long)c.img * c.H));
+  RC(launch_linear_f32(img + (size_t)(im.a - c.txt) * c.in_ch, c.in_ch, im.n(), c.in_ch,
+                       m->img_in_w, m->img_in_b, c.H, m->hidden + (size_t)im.a * c.H, c.H, false,
+                       st));
+  return dit_prepare_vec(m, pooled, st);
+}
+
+int bonsai_dit_phase(bonsai_dit_t m, int kind, int block, int phase, void* stream) {
+  if (!m || phase < 0 || phase > 2) return fail(BONSAI_ERR_ARG, "dit_phase: bad phase");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (kind == 0) {
+    if (block < 0 || block >= m->c.depth) return fail(BONSAI_ERR_ARG, "dit_phase: bad double block");
+    return double_phase(m, block, phase, st);
+  }
+  if (kind == 1) {
+    if (block < 0 || block >= m->c.depth_single) return fail(BONSAI_ERR_ARG, "dit_phase: bad single block");
+    return single_phase(m, block, phase, st);
+  }
+  return fail(BONSAI_ERR_ARG, "dit_phase: kind must be 0 (double) or 1 (single)");
+}
+
+int bonsai_dit_end(bonsai_dit_t m, float* out, void* stream) {
+  if (!m || !out) return fail(BONSAI_ERR_ARG, "dit_end: null argument");
+  const Cfg& c = m->c;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // output head (:544-556) on every image row (the caller has gathered them)
+  const float* h_img = m->hidden + (size_t)c.txt * c.H;
+  RC(launch_ln_modulate_f32(h_img, c.img, c.H, m->fin + c.H, m->fin, 1e-6f, m->tmp32, c.H, st));
+  return launch_linear_f32(m->tmp32, c.H, c.img, c.H, m->proj_out_w, m->proj_out_b, c.in_ch, out,
+                           c.in_ch, false, st);
 }
 
 long long bonsai_dit_weight(bonsai_dit_t m, const char* name, void* buf, long long cap) {

@@ -72,13 +72,24 @@ struct EpiSeg {
 };
 
 constexpr int kMaxSegs = 2;
+constexpr int kMaxTileGroups = 3;
+
+// Optional selection of 128-row weight tiles for a GEMM launch: the tiles
+// base[g] + i for g < groups, i < count (e.g. one rank's heads of the q, k
+// and v parts of a fused QKV weight).  Null = every tile.
+struct TileSel {
+  int groups = 1;
+  int count = 0;
+  int base[kMaxTileGroups] = {0, 0, 0};
+};
 
 // Launch the tcgen05 B1_0 GEMM: for every token t < tokens and weight row n,
 // acc[t][n] = sum_k x[t][k] * W[n][k]; acc is routed through the segment that
 // covers n.  x is f16 (or bf16 when x_bf16) row-major with leading dimension
 // ldx (elements); it must be 16-byte aligned with ldx % 8 == 0.
 int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w,
-                   const EpiSeg* segs, int nseg, bool x_bf16, cudaStream_t st);
+                   const EpiSeg* segs, int nseg, bool x_bf16, cudaStream_t st,
+                   const TileSel* sel = nullptr);
 
 // Retile packed reference bytes (device copy) into the chunked layout.
 int launch_b1_retile(const uint8_t* dev_packed, B1Weight& w, cudaStream_t st);

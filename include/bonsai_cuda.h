@@ -246,6 +246,33 @@ int bonsai_dit_get_state(bonsai_dit_t m, float* hidden, void* stream);
 int bonsai_dit_double_block(bonsai_dit_t m, int i, void* stream);
 int bonsai_dit_single_block(bonsai_dit_t m, int i, void* stream);
 
+/* ---- Multi-GPU: one long image split across GPUs (2048^2, 16896 tokens).
+ * Each of `world` ranks (one process per GPU, each with its own model holding
+ * the full weights) owns token rows [rank*L/world, (rank+1)*L/world) and
+ * heads [rank*24/world, (rank+1)*24/world).  A step is driven as
+ *   bonsai_dit_begin                       (edges of own rows, modulation)
+ *   for each double block i, then each single block i (kind 0 / 1):
+ *     bonsai_dit_phase(kind, i, 0)         LN-modulate own rows -> "xm"
+ *     all-gather the rows of "xm"          (caller: NCCL, in place)
+ *     bonsai_dit_phase(kind, i, 1)         Q/K/V of own heads on all rows,
+ *                                          Q/K norm + RoPE, attention -> "cat"
+ *     all-to-all of "cat" columns [0, 3072): own heads x all rows ->
+ *                                          all heads x own rows (caller)
+ *     bonsai_dit_phase(kind, i, 2)         out-proj / MLP / gate-residual, own rows
+ *   all-gather the rows of "hidden", then bonsai_dit_end -> out (every rank).
+ * No GEMM FLOP is repeated across ranks (Q/K/V weights are split by head,
+ * the rest by token rows).  With world == 1 the phases are exactly
+ * bonsai_dit_forward.  The reference has no multi-device path. */
+int bonsai_dit_set_partition(bonsai_dit_t m, int rank, int world);
+/* Device pointer and size of an engine buffer shared with the caller's
+ * collectives: "hidden" f32 [L][3072], "xm" f16 [L][3072],
+ * "cat" f16 [L][3072 + mlp], "qkv" f16 [3][24][L][128]. */
+int bonsai_dit_buffer(bonsai_dit_t m, const char* name, void** ptr, long long* bytes);
+int bonsai_dit_begin(bonsai_dit_t m, const float* img, const float* txt, const float* pooled,
+                     float timestep, void* stream);
+int bonsai_dit_phase(bonsai_dit_t m, int kind, int block, int phase, void* stream);
+int bonsai_dit_end(bonsai_dit_t m, float* out, void* stream);
+
 /* Export the seeded host weights of the model (packed B1_0 bytes and f32
  * tensors) by name, for the CPU oracle: returns the byte size when buf is
  * NULL.  Names follow the reference's safetensors keys
