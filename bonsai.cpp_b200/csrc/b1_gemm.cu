@@ -5,25 +5,37 @@
 // over the packed layout of src/diffuser_types.h:10-11 /
 // convert_to_b1_0_packed.py:21-43.
 //
-// Design (weights-as-A, tokens-as-B):
-//   * The MMA computes D[128 weight rows][128 tokens] += A * B^T with
-//     A = expanded weights held in TMEM and B = activation tile in SMEM.
-//   * Four expansion warps turn the retiled sign words + fp16 scales into
-//     exact f16 +-scale values in registers and write them straight into
-//     TMEM with tcgen05.st: the expanded weights never touch shared memory,
-//     so SMEM bandwidth is spent only on the activations.
-//   * A TMA warp streams activation tiles (128 tokens x 64 k, 128-byte
-//     swizzle) and the 1.5 KB weight chunk of each k-block.
-//   * One thread issues tcgen05.mma (A from TMEM, B from SMEM descriptor).
-//   * Four epilogue warps drain the double-buffered accumulator with
-//     tcgen05.ld and apply the fused epilogue (store, GELU, SwiGLU,
-//     gate-residual, head-major QKV scatter).
-//   * Persistent grid: one CTA per SM walks the tile list.
+// Two kernels share the retiled weight layout, the epilogues and the
+// warp-specialised structure (TMA warp, MMA warp, expansion warps, epilogue
+// warps, persistent tile loop, mbarrier rings with bounded waits):
+//
+// b1_gemm_pair_kernel (the main path): a cluster of two CTAs on the two SMs
+//   of a TPC computes a 256-weight-row x 256-token tile with
+//   tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16 per instruction).
+//   Each CTA's expansion warps turn the sign words + fp16 scales of its 128
+//   weight rows into exact f16 +-scale values and store them into its own
+//   shared memory in the 128-byte-swizzled K-major layout; its TMA warp loads
+//   its 128-token half of the activation tile.  The even CTA issues the MMAs;
+//   each CTA's TMEM receives its 128 rows x 256 tokens (two 256-column
+//   accumulators, so the epilogue of one tile overlaps the next tile's MMAs).
+//   Per SM and k-block of 64 this expands 8 K weights per 128x256x64 MMA
+//   block, half of what a 128x128 tile needs.
+//
+// b1_gemm_kernel (small grids): one CTA per 128x128 tile; the expanded
+//   weights go straight into TMEM with tcgen05.st (A from TMEM, B from SMEM).
+//   It has twice as many tiles as the pair kernel for the same problem, so it
+//   keeps more SMs busy when the pair kernel would run a single short wave
+//   (e.g. the 512-token text stream).
+//
+// launch_b1_gemm picks the kernel with the smaller estimated time (waves x
+// tile time); BONSAI_B1_KERNEL=pair|single forces one (used by the tests).
 #include "internal.cuh"
 #include "ptx.cuh"
 
 #include <cudaTypedefs.h>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace bonsai {
@@ -385,6 +397,327 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ------------------------------------------------- CTA-pair kernel (2 SMs)
+// A cluster of two CTAs computes a 256-row x 256-token tile with
+// tcgen05.mma.cta_group::2: each CTA expands its 128 weight rows into its
+// own shared memory (128-byte-swizzled K-major, the layout TMA writes) and
+// loads its 128-token half of the activation tile; the even CTA issues the
+// MMAs and each CTA's TMEM receives its 128 rows x 256 tokens.
+namespace pair {
+constexpr int BM = 128;                  // weight rows per CTA (MMA M = 256 per pair)
+constexpr int BN = 256;                  // tokens per pair tile (MMA N)
+constexpr int BNH = BN / 2;              // tokens loaded by each CTA
+constexpr int BK = 64;
+constexpr int STAGES = 6;
+constexpr int A_STAGE_BYTES = BM * BK * 2;    // 16 KB
+constexpr int X_STAGE_BYTES = BNH * BK * 2;   // 16 KB
+constexpr int RAW_STAGE_BYTES = kChunkWords * 4;
+constexpr int TMEM_COLS = 512;               // two 256-column accumulators
+constexpr int WARP_TMA = 0;
+constexpr int WARP_MMA = 1;
+constexpr int EXP_PER_G = 2;                 // expansion warps per 32-row group
+constexpr int EXP_WARPS = 4 * EXP_PER_G;
+constexpr int WARP_EXP0 = 2;
+constexpr int EPI_PER_Q = 2;
+constexpr int EPI_WARPS = 4 * EPI_PER_Q;
+constexpr int WARP_EPI0 = WARP_EXP0 + EXP_WARPS;
+constexpr int NUM_THREADS = (WARP_EPI0 + EPI_WARPS) * 32;
+constexpr int SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + X_STAGE_BYTES + RAW_STAGE_BYTES) + 256;
+
+struct Params {
+  int tokens;
+  int n_ttiles, k_blocks;
+  int npf;          // weight-tile pairs: selected tiles 2i and 2i+1
+  int num_tiles;    // npf * n_ttiles
+  int nf, fcount, fgroups;
+  int fbase[kMaxTileGroups];
+  const uint32_t* chunks;
+  int nseg;
+  EpiSeg seg[kMaxSegs];
+  int* err;
+};
+
+template <bool kBF16>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    b1_gemm_pair_kernel(const __grid_constant__ CUtensorMap xmap, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* as = smem;
+  uint8_t* xs = as + STAGES * A_STAGE_BYTES;
+  uint32_t* raw = reinterpret_cast<uint32_t*>(xs + STAGES * X_STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(raw + STAGES * kChunkWords);
+  uint64_t* rawfull = full + STAGES;
+  uint64_t* empty = rawfull + STAGES;
+  uint64_t* dfull = empty + STAGES;
+  uint64_t* dempty = dfull + 2;
+  uint64_t* drain = dempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();      // 0 = the CTA that issues the MMAs
+  const int cid = (int)cluster_id_x();
+  const int ncl = (int)cluster_count_x();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      // even CTA: its producer's expect_tx arrival + 4 expansion warps per CTA
+      bar_init(&full[s], 1 + 2 * 4);
+      bar_init(&rawfull[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(&dfull[b], 1);
+      bar_init(&dempty[b], 2 * EPI_WARPS);
+    }
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == WARP_MMA) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // barrier inits and TMEM of both CTAs visible to the pair
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int k_blocks = p.k_blocks;
+
+  if (warp == WARP_TMA) {
+    if (elect_one()) {
+      tma_prefetch_desc(&xmap);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = cid; tile < p.num_tiles && ok; tile += ncl) {
+        const int ttile = tile / p.npf;
+        const int pf = tile - ttile * p.npf;
+        const int fidx = min(2 * pf + (int)rank, p.nf - 1);
+        const int ftile = sel_ftile(fidx, p.fcount, p.fbase);
+        const uint32_t* wsrc = p.chunks + (size_t)ftile * k_blocks * kChunkWords;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!wait_bar(&empty[s], ph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          bar_arrive_expect_tx(&rawfull[s], RAW_STAGE_BYTES);
+          bulk_load(raw + s * kChunkWords, wsrc + (size_t)kb * kChunkWords, RAW_STAGE_BYTES,
+                    &rawfull[s]);
+          if (rank == 0) bar_arrive_expect_tx(&full[s], 2 * X_STAGE_BYTES);
+          tma_load_2d_pair(xs + s * X_STAGE_BYTES, &xmap, mapa_shared(smem_u32(&full[s]), 0),
+                           kb * BK, ttile * BN + (int)rank * BNH);
+        }
+      }
+      if (!ok) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 1000000ull) {
+        }
+      }
+    }
+  } else if (warp == WARP_MMA) {
+    if (elect_one()) {
+      if (rank == 0) {
+        constexpr uint32_t idesc = make_idesc_f16(2 * BM, BN, kBF16 ? 1 : 0, 0, 0);
+        uint32_t it = 0, lt = 0;
+        bool ok = true;
+        for (int tile = cid; tile < p.num_tiles && ok; tile += ncl, ++lt) {
+          const uint32_t b = lt & 1;
+          const uint32_t dph = (lt >> 1) & 1;
+          if (!wait_bar(&dempty[b], dph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem + b * BN;
+          for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+            const int s = it % STAGES;
+            const uint32_t ph = (it / STAGES) & 1;
+            if (!wait_bar(&full[s], ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t aaddr = smem_u32(as + s * A_STAGE_BYTES);
+            const uint32_t xaddr = smem_u32(xs + s * X_STAGE_BYTES);
+#pragma unroll
+            for (int k16 = 0; k16 < BK / 16; ++k16) {
+              const uint64_t adesc = make_smem_desc(aaddr + k16 * 32, 16, 1024);
+              const uint64_t bdesc = make_smem_desc(xaddr + k16 * 32, 16, 1024);
+              mma_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k16) != 0 ? 1u : 0u);
+            }
+            tc_commit_pair(&empty[s], 0x3);
+          }
+          if (!ok) break;
+          tc_commit_pair(&dfull[b], 0x3);
+        }
+        tc_commit_pair(drain, 0x3);
+      }
+      // Both CTAs: wait until every pair MMA has completed (the commit above
+      // arrives on the drain barrier of each CTA).
+      const uint32_t da = smem_u32(drain);
+      const unsigned long long t0 = globaltimer_ns();
+      while (!bar_try_wait(da, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          if (p.err) atomicCAS(p.err, 0, DEV_ERR_TIMEOUT_MMA);
+          break;
+        }
+      }
+    }
+  } else if (warp >= WARP_EXP0 && warp < WARP_EXP0 + EXP_WARPS) {
+    const int g = (warp - WARP_EXP0) & 3;   // 32-row group
+    const uint32_t slot = (uint32_t)((warp - WARP_EXP0) >> 2);
+    const int r = g * 32 + (int)lane;        // weight row within this CTA's 128
+    const uint32_t full0 = mapa_shared(smem_u32(&full[0]), 0);
+    const uint32_t row_off = (uint32_t)r * 128u;
+    const uint32_t sw = (uint32_t)(r & 7);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = cid; tile < p.num_tiles && ok; tile += ncl) {
+      for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        if (it % EXP_PER_G != slot) continue;
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        const bool good =
+            wait_bar(&rawfull[s], ph, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER) &&
+            wait_bar(&empty[s], ph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER);
+        if (!__all_sync(0xffffffffu, good)) {
+          ok = false;
+          break;
+        }
+        const uint32_t* rs = raw + s * kChunkWords;
+        const uint32_t p0 = rs[r];
+        const uint32_t p1 = rs[128 + r];
+        const uint32_t sc = rs[256 + r];
+        uint32_t v[32];
+        expand_group(p0, bf16_from_f16_scale<kBF16>(sc & 0xFFFFu), v);
+        expand_group(p1, bf16_from_f16_scale<kBF16>(sc >> 16), v + 16);
+        const uint32_t abase = smem_u32(as + s * A_STAGE_BYTES) + row_off;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          st_shared_v4(abase + (((uint32_t)c ^ sw) << 4), v[4 * c], v[4 * c + 1], v[4 * c + 2],
+                       v[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) bar_arrive_remote(full0 + (uint32_t)s * 8u);
+      }
+    }
+  } else if (warp >= WARP_EPI0 && warp < WARP_EPI0 + EPI_WARPS) {
+    const int q = warp & 3;
+    const int eh = (warp - WARP_EPI0) >> 2;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const uint32_t dempty0 = mapa_shared(smem_u32(&dempty[0]), 0);
+    uint32_t lt = 0;
+    for (int tile = cid; tile < p.num_tiles; tile += ncl, ++lt) {
+      const int ttile = tile / p.npf;
+      const int pf = tile - ttile * p.npf;
+      const int fidx = 2 * pf + (int)rank;
+      const uint32_t b = lt & 1;
+      const uint32_t dph = (lt >> 1) & 1;
+      const bool good = wait_bar(&dfull[b], dph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, good)) break;
+      tc_fence_after();
+
+      int si = -1;
+      int row = 0;
+      if (fidx < p.nf) {
+        row = sel_ftile(fidx, p.fcount, p.fbase) * BM + q * 32 + (int)lane;
+#pragma unroll
+        for (int i = 0; i < kMaxSegs; ++i)
+          if (i < p.nseg && row >= p.seg[i].row_begin && row < p.seg[i].row_end) si = i;
+      }
+      EpiSeg sg;
+      if (si >= 0) sg = p.seg[si];
+      const int mode = si >= 0 ? sg.mode : -1;
+      const int rr = row - sg.row_begin;
+      float gate = 1.0f;
+      if (mode == EPI_RESID_F32 && sg.gate) gate = sg.gate[rr];
+      size_t base = 0;
+      uint32_t stride = (uint32_t)sg.ld;
+      if (mode == EPI_QKV_F16) {
+        const int hd = sg.head_dim;
+        const int which = rr / (sg.heads * hd);
+        const int rem = rr - which * sg.heads * hd;
+        const int h = rem / hd;
+        const int d = rem - h * hd;
+        base = ((size_t)(which * sg.heads + h) * sg.seq_total + sg.tok_off) * hd + d;
+        stride = (uint32_t)hd;
+      } else if (mode == EPI_SWIGLU_F16) {
+        base = (size_t)sg.col_off + (rr >> 1);
+      } else if (mode >= 0) {
+        base = (size_t)sg.col_off + rr;
+      }
+      const bool warp_swiglu = __any_sync(0xffffffffu, mode == EPI_SWIGLU_F16);
+
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32 / EPI_PER_Q; ++cc) {
+        const int c = eh * (BN / 32 / EPI_PER_Q) + cc;
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + b * BN + c * 32, v);
+        tmem_wait_ld();
+        const int t0 = ttile * BN + c * 32;
+        const int nt = min(32, p.tokens - t0);
+        if (warp_swiglu) {
+          __half* dst = reinterpret_cast<__half*>(sg.dst) + base + (size_t)t0 * stride;
+          const bool own = mode == EPI_SWIGLU_F16 && (rr & 1) == 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float a = __uint_as_float(v[j]);
+            const float o = __shfl_xor_sync(0xffffffffu, a, 1);
+            if (own && j < nt) dst[j * stride] = __float2half_rn(silu(a) * o);
+          }
+          continue;
+        }
+        if (mode < 0 || nt <= 0) continue;
+        if (mode == EPI_F16 || mode == EPI_QKV_F16) {
+          __half* dst = reinterpret_cast<__half*>(sg.dst) + base + (size_t)t0 * stride;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nt) dst[j * stride] = __float2half_rn(__uint_as_float(v[j]));
+        } else if (mode == EPI_GELU_F16) {
+          __half* dst = reinterpret_cast<__half*>(sg.dst) + base + (size_t)t0 * stride;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nt) dst[j * stride] = __float2half_rn(gelu_tanh(__uint_as_float(v[j])));
+        } else if (mode == EPI_RESID_F32) {
+          float* dst = reinterpret_cast<float*>(sg.dst) + base + (size_t)t0 * stride;
+#pragma unroll
+          for (int h16 = 0; h16 < 32; h16 += 16) {
+            float old[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) old[j] = h16 + j < nt ? dst[(h16 + j) * stride] : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (h16 + j < nt) dst[(h16 + j) * stride] = fmaf(gate, __uint_as_float(v[h16 + j]), old[j]);
+          }
+        } else if (mode == EPI_F32) {
+          float* dst = reinterpret_cast<float*>(sg.dst) + base + (size_t)t0 * stride;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nt) dst[j * stride] = __uint_as_float(v[j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive_remote(dempty0 + b * 8u);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no pair MMA, remote arrive or TMEM access is left in either CTA
+  if (warp == WARP_MMA) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+}
+}  // namespace pair
+
 // ------------------------------------------------------------ retile kernel
 __device__ __forceinline__ uint32_t compress_even_bits(uint32_t x) {
   x &= 0x55555555u;
@@ -498,6 +831,53 @@ int launch_b1_retile(const uint8_t* dev_packed, B1Weight& w, cudaStream_t st) {
   return launch_status("b1_retile_kernel launch");
 }
 
+namespace {
+
+enum class B1Kernel { Auto, Single, Pair };
+
+B1Kernel forced_kernel() {
+  const char* e = getenv("BONSAI_B1_KERNEL");
+  if (!e) return B1Kernel::Auto;
+  if (strcmp(e, "pair") == 0) return B1Kernel::Pair;
+  if (strcmp(e, "single") == 0) return B1Kernel::Single;
+  return B1Kernel::Auto;
+}
+
+// Largest number of co-resident pair clusters (one per TPC when every SM
+// takes one CTA of the pair kernel); 0 if the query fails.
+int pair_cluster_slots(bool bf16) {
+  static int slots[2] = {-1, -1};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  int& n = slots[bf16 ? 1 : 0];
+  if (n >= 0) return n;
+  auto k2 = bf16 ? gemm::pair::b1_gemm_pair_kernel<true> : gemm::pair::b1_gemm_pair_kernel<false>;
+  n = 0;
+  if (cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           gemm::pair::SMEM_BYTES) != cudaSuccess)
+    return n;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * std::max(1, num_sms() / 2));
+  cfg.blockDim = dim3(gemm::pair::NUM_THREADS);
+  cfg.dynamicSmemBytes = gemm::pair::SMEM_BYTES;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int c = 0;
+  if (cudaOccupancyMaxActiveClusters(&c, k2, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return n;
+  }
+  n = c;
+  return n;
+}
+
+}  // namespace
+
 int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, const EpiSeg* segs,
                    int nseg, bool x_bf16, cudaStream_t st, const TileSel* sel) {
   if (tokens < 0) return fail(-1, "b1_gemm: negative token count");
@@ -506,38 +886,112 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
   if (nseg < 1 || nseg > kMaxSegs) return fail(-1, "b1_gemm: bad segment count");
   if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx % 8) != 0 || ldx < w.k_in)
     return fail(-1, "b1_gemm: activation must be 16-byte aligned with ld % 8 == 0 and ld >= K");
-  CUtensorMap xmap;
-  int rc = encode_tmap_2d_16b(&xmap, x, tokens, w.k_in, ldx, gemm::BK, gemm::BN, x_bf16);
-  if (rc) return rc;
 
-  gemm::Params p{};
-  p.tokens = tokens;
-  p.n_rows = w.n_rows;
-  p.n_ftiles = w.n_ftiles;
-  p.n_ttiles = (tokens + gemm::BN - 1) / gemm::BN;
-  p.k_blocks = w.k_blocks;
+  // Weight-tile selection: the nf = groups * count selected 128-row tiles
+  // are base[g] + i (g < groups, i < count).
+  int fgroups = 1, fcount = w.n_ftiles;
+  int fbase[kMaxTileGroups] = {0, 0, 0};
   if (sel) {
     if (sel->groups < 1 || sel->groups > kMaxTileGroups || sel->count < 1)
       return fail(-1, "b1_gemm: bad tile selection");
     for (int g = 0; g < sel->groups; ++g)
       if (sel->base[g] < 0 || sel->base[g] + sel->count > w.n_ftiles)
         return fail(-1, "b1_gemm: tile selection outside the weight");
-    p.fgroups = sel->groups;
-    p.fcount = sel->count;
-    for (int g = 0; g < sel->groups; ++g) p.fbase[g] = sel->base[g];
-  } else {
-    p.fgroups = 1;
-    p.fcount = w.n_ftiles;
-    p.fbase[0] = 0;
+    fgroups = sel->groups;
+    fcount = sel->count;
+    for (int g = 0; g < sel->groups; ++g) fbase[g] = sel->base[g];
   }
-  p.nf = p.fgroups * p.fcount;
-  p.num_tiles = p.nf * p.n_ttiles;
+  const int nf = fgroups * fcount;
+
+  // Kernel choice: estimated time = waves x tile time, with a 256x256 pair
+  // tile (two SMs) taking kPairTileCost 128x128-tile times of one SM (about
+  // 2 x 1255 / 1536 from isolated measurements of the two kernels).
+  const int slots = pair_cluster_slots(x_bf16);
+  const int n_tt1 = (tokens + gemm::BN - 1) / gemm::BN;
+  const int n_tt2 = (tokens + gemm::pair::BN - 1) / gemm::pair::BN;
+  const long long tiles1 = (long long)nf * n_tt1;
+  const long long tiles2 = (long long)((nf + 1) / 2) * n_tt2;
+  constexpr double kPairTileCost = 1.63;
+  bool use_pair = false;
+  const B1Kernel force = forced_kernel();
+  if (force == B1Kernel::Pair) {
+    if (slots < 1) return fail(-3, "b1_gemm: the pair kernel cannot be scheduled on this device");
+    use_pair = true;
+  } else if (force == B1Kernel::Auto && slots >= 1) {
+    const double t1 = (double)((tiles1 + num_sms() - 1) / num_sms());
+    const double t2 = kPairTileCost * (double)((tiles2 + slots - 1) / slots);
+    use_pair = t2 < t1;
+  }
+
+  double out_bytes = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const double rows = segs[i].row_end - segs[i].row_begin;
+    const int m = segs[i].mode;
+    const double per = (m == EPI_F32) ? 4 : (m == EPI_RESID_F32) ? 8 : (m == EPI_SWIGLU_F16) ? 1 : 2;
+    out_bytes += rows * tokens * per;
+  }
+  const double rows_done = sel ? std::min<double>(w.n_rows, 128.0 * nf) : (double)w.n_rows;
+  if (sel) out_bytes *= rows_done / std::max(1, w.n_rows);
+
+  if (use_pair) {
+    CUtensorMap xmap;
+    int rc = encode_tmap_2d_16b(&xmap, x, tokens, w.k_in, ldx, gemm::pair::BK, gemm::pair::BNH,
+                                x_bf16);
+    if (rc) return rc;
+    gemm::pair::Params q{};
+    q.tokens = tokens;
+    q.n_ttiles = n_tt2;
+    q.k_blocks = w.k_blocks;
+    q.nf = nf;
+    q.fcount = fcount;
+    q.fgroups = fgroups;
+    for (int g = 0; g < kMaxTileGroups; ++g) q.fbase[g] = fbase[g];
+    q.npf = (nf + 1) / 2;
+    q.num_tiles = (int)tiles2;
+    q.chunks = w.chunks;
+    q.nseg = nseg;
+    for (int i = 0; i < nseg; ++i) q.seg[i] = segs[i];
+    q.err = device_error_word();
+    auto k2 = x_bf16 ? gemm::pair::b1_gemm_pair_kernel<true> : gemm::pair::b1_gemm_pair_kernel<false>;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (unsigned)std::min<long long>(tiles2, slots));
+    cfg.blockDim = dim3(gemm::pair::NUM_THREADS);
+    cfg.dynamicSmemBytes = gemm::pair::SMEM_BYTES;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ProfScope prof("b1_gemm", 2.0 * tokens * rows_done * (double)w.k_in,
+                   (double)tokens * w.k_in * 2 + rows_done * w.k_in * 6 / 32 + out_bytes, st);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k2, xmap, q);
+    if (e != cudaSuccess) return cuda_status(e, "b1_gemm_pair_kernel launch");
+    return launch_status("b1_gemm_pair_kernel launch");
+  }
+
+  CUtensorMap xmap;
+  int rc = encode_tmap_2d_16b(&xmap, x, tokens, w.k_in, ldx, gemm::BK, gemm::BN, x_bf16);
+  if (rc) return rc;
+  gemm::Params p{};
+  p.tokens = tokens;
+  p.n_rows = w.n_rows;
+  p.n_ftiles = w.n_ftiles;
+  p.n_ttiles = n_tt1;
+  p.k_blocks = w.k_blocks;
+  p.fgroups = fgroups;
+  p.fcount = fcount;
+  for (int g = 0; g < kMaxTileGroups; ++g) p.fbase[g] = fbase[g];
+  p.nf = nf;
+  p.num_tiles = (int)tiles1;
   p.chunks = w.chunks;
   p.nseg = nseg;
   for (int i = 0; i < nseg; ++i) p.seg[i] = segs[i];
   p.err = device_error_word();
 
-  const int grid = std::min(p.num_tiles, num_sms());
+  const int grid = (int)std::min<long long>(tiles1, num_sms());
   auto kern = x_bf16 ? gemm::b1_gemm_kernel<true> : gemm::b1_gemm_kernel<false>;
   static bool attr_set[2] = {false, false};
   if (!attr_set[x_bf16 ? 1 : 0]) {
@@ -546,15 +1000,6 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
     if (e != cudaSuccess) return cuda_status(e, "b1_gemm set smem attribute");
     attr_set[x_bf16 ? 1 : 0] = true;
   }
-  double out_bytes = 0;
-  for (int i = 0; i < nseg; ++i) {
-    const double rows = segs[i].row_end - segs[i].row_begin;
-    const int m = segs[i].mode;
-    const double per = (m == EPI_F32) ? 4 : (m == EPI_RESID_F32) ? 8 : (m == EPI_SWIGLU_F16) ? 1 : 2;
-    out_bytes += rows * tokens * per;
-  }
-  const double rows_done = sel ? std::min<double>(w.n_rows, 128.0 * p.nf) : (double)w.n_rows;
-  if (sel) out_bytes *= rows_done / std::max(1, w.n_rows);
   ProfScope prof("b1_gemm", 2.0 * tokens * rows_done * (double)w.k_in,
                  (double)tokens * w.k_in * 2 + rows_done * w.k_in * 6 / 32 + out_bytes, st);
   kern<<<grid, gemm::NUM_THREADS, gemm::SMEM_BYTES, st>>>(xmap, p);

@@ -19,6 +19,15 @@ SWEEP_M = [1280, 4352, 8704]
 SWEEP_KN = [(3072, 9216), (3072, 3072), (3072, 12288), (12288, 3072), (3072, 21504), (15360, 3072)]
 
 
+@pytest.fixture(params=["single", "pair"])
+def kernel(request, monkeypatch):
+    """Run the test with each GEMM kernel forced (the launcher otherwise
+    picks by estimated time): 'single' = one CTA per 128x128 tile with the
+    weights in TMEM, 'pair' = a two-SM cluster per 256x256 tile."""
+    monkeypatch.setenv("BONSAI_B1_KERNEL", request.param)
+    return request.param
+
+
 def _cos(a, b):
     a = np.asarray(a, np.float64).ravel()
     b = np.asarray(b, np.float64).ravel()
@@ -40,7 +49,7 @@ def _case(M, K, N, seed):
     (129, 256, 384),
     (256, 512, 1000),
 ])
-def test_b1_linear_f32_small(gpu, M, K, N):
+def test_b1_linear_f32_small(gpu, kernel, M, K, N):
     import torch
     packed, x = _case(M, K, N, 1000 + M + K + N)
     w = bb.B1Weight(packed, N, K)
@@ -59,7 +68,7 @@ def test_b1_linear_f32_small(gpu, M, K, N):
     assert np.max(np.abs(got - ref32)) <= 1e-2 * np.sqrt(np.mean(ref32 ** 2))
 
 
-def test_b1_zero_tokens_is_noop(gpu):
+def test_b1_zero_tokens_is_noop(gpu, kernel):
     import torch
     packed, _ = _case(1, 64, 32, 5)
     w = bb.B1Weight(packed, 32, 64)
@@ -70,7 +79,7 @@ def test_b1_zero_tokens_is_noop(gpu):
 
 
 @pytest.mark.parametrize("K,N", SWEEP_KN)
-def test_b1_gemm_sweep_shapes(gpu, K, N):
+def test_b1_gemm_sweep_shapes(gpu, kernel, K, N):
     """Every (K,N) of the BASELINE GEMM sweep at every M, vs a torch fp32
     product of the dequantised weights and the same f16 activations."""
     import torch
@@ -92,7 +101,7 @@ def test_b1_gemm_sweep_shapes(gpu, K, N):
         assert err <= 1e-3 * rms, (M, K, N, err, rms)
 
 
-def test_b1_gemm_epilogues(gpu):
+def test_b1_gemm_epilogues(gpu, kernel):
     import torch
     M, K, N = 300, 1024, 512
     rng = np.random.default_rng(77)
