@@ -7,16 +7,22 @@
 // One CTA = one head x 256 queries, processed as two 128-query tiles that
 // ping-pong on the tensor core: while the softmax warps of one tile work,
 // the MMA thread runs the other tile's P*V and its next Q*K^T.
-//   warp 0      TMA: Q0/Q1 once, then K_j / V_j tiles (128 keys x 128 dims,
+//   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1: thread i
+//               owns query row i (TMEM lane i).  Online softmax in the log2
+//               domain with lazy rescaling: the running max only moves (and
+//               O_g in TMEM is rescaled) when a tile's max exceeds it by more
+//               than 8 (p <= 2^8 stays accurate in f16); the final 1/l is
+//               exact.  Scale/subtract and the row sum use packed f32x2 ops.
+//   warp 8      TMA: Q0/Q1 once, then K_j / V_j tiles (128 keys x 128 dims,
 //               two 64-dim halves, 128-byte swizzle) through 2-deep rings.
-//   warp 1      one thread issues tcgen05.mma:
+//   warp 9      one thread issues tcgen05.mma:
 //                 S_g  = Q_g K_j^T   (A, B from SMEM)          g = 0, 1
 //                 O_g += P_g V_j     (A = P_g from TMEM, B = V MN-major)
-//   warps 2-5   softmax of tile 0, warps 6-9 softmax of tile 1: thread i owns
-//               query row i (TMEM lane i).  Online softmax in the log2 domain
-//               with lazy rescaling: the running max only moves (and O_g in
-//               TMEM is rescaled) when a tile's max exceeds it by more than 8
-//               (p <= 2^8 stays accurate in f16); the final 1/l is exact.
+//   warps 10-11 idle (they complete the third warpgroup).
+// setmaxnreg gives the softmax warpgroups 224 registers per thread (the whole
+// S row stays in registers) and the TMA/MMA warpgroup 56; the three
+// warpgroups' code paths never rejoin, so each keeps its own budget, and the
+// MMA warp frees TMEM after every softmax warp has signalled it is done.
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // P_g (f16 pairs, 64 columns) overwrites the first half of S_g once the
 // softmax has read S_g; the next S_g is issued after P_g V_j in the same
@@ -36,7 +42,17 @@ constexpr int KS = 2;  // K ring depth
 constexpr int VS = 2;  // V ring depth
 constexpr int TILE_BYTES = BKV * HD * 2;  // 32 KB (two 16 KB halves)
 constexpr int HALF_BYTES = TILE_BYTES / 2;
-constexpr int NUM_THREADS = 320;
+// Warpgroup 0: softmax of query tile 0, warpgroup 1: tile 1 (one thread per
+// query row); warpgroup 2: TMA warp, MMA warp and two idle warps.  setmaxnreg
+// moves registers from warpgroup 2 to the softmax warpgroups.
+constexpr int NUM_THREADS = 384;
+constexpr int WARP_TMA = 8;
+constexpr int WARP_MMA = 9;
+constexpr int kLaunchRegs = 168;   // 65536 / 384, rounded down to 8
+constexpr int kSoftmaxRegs = 224;
+constexpr int kAuxRegs = 56;
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kAuxRegs <= NUM_THREADS * kLaunchRegs,
+              "register split exceeds the launch allocation");
 constexpr int TMEM_COLS = 512;
 constexpr int S_COL = 0, O_COL = 256;
 constexpr int SMEM_BYTES = 1024 + TILE_BYTES * (2 + KS + VS) + 256;
@@ -54,6 +70,47 @@ struct Params {
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Packed pairs of f32 in one 64-bit register (Blackwell f32x2 FMA pipe).
+__device__ __forceinline__ unsigned long long pack2(float a, float b) {
+  unsigned long long d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b,
+                                                   unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cvt_h2(float lo, float hi) {
+  uint32_t y;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(y) : "f"(hi), "f"(lo));
   return y;
 }
 
@@ -77,7 +134,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* p_ready = s_full + 2;    // [2]
   uint64_t* pv_done = p_ready + 2;   // [2]
   uint64_t* drain = pv_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* sm_done = drain + 1;     // softmax warps finished with TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -102,10 +160,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bar_init(&pv_done[g], 1);
     }
     bar_init(drain, 1);
+    bar_init(sm_done, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == WARP_MMA) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
@@ -114,7 +173,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp >= 8) {
+  regs_dec<kAuxRegs>();
+  if (warp == WARP_TMA) {
     if (elect_one()) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
@@ -149,7 +210,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == WARP_MMA) {
     if (elect_one()) {
       constexpr uint32_t idesc_s = make_idesc_f16(BQ, BKV, 0, 0, 0);   // K-major A and B
       constexpr uint32_t idesc_o = make_idesc_f16(BQ, HD, 0, 0, 1);    // B (V) MN-major
@@ -212,9 +273,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    __syncwarp();
+    // Free TMEM once every softmax warp has finished reading it (the roles
+    // never rejoin, so that each keeps its own register budget).
+    const uint32_t sd = smem_u32(sm_done);
+    const unsigned long long t1 = globaltimer_ns();
+    bool done = bar_try_wait(sd, 0);
+    while (!__all_sync(0xffffffffu, done)) {
+      if (globaltimer_ns() - t1 > kWaitLimitNs) {
+        if (p.err && lane == 0) atomicCAS(p.err, 0, DEV_ERR_TIMEOUT_MMA);
+        break;
+      }
+      done = bar_try_wait(sd, 0);
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
   } else {
-    // softmax warps: 2..5 -> query tile 0, 6..9 -> query tile 1
-    const int g = (warp - 2) >> 2;
+    regs_inc<kSoftmaxRegs>();
+    // softmax warps: 0..3 -> query tile 0, 4..7 -> query tile 1
+    const int g = warp >> 2;
     const int qd = warp & 3;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + S_COL + g * BKV;
@@ -231,13 +309,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       float s[BKV];
       {
-        uint32_t r[32];
+        // All four 32-column loads in flight before the one wait.
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(s_addr, r0);
+        tmem_ld32(s_addr + 32, r1);
+        tmem_ld32(s_addr + 64, r2);
+        tmem_ld32(s_addr + 96, r3);
+        tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(s_addr + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < 32; ++i) {
+          s[i] = __uint_as_float(r0[i]);
+          s[32 + i] = __uint_as_float(r1[i]);
+          s[64 + i] = __uint_as_float(r2[i]);
+          s[96 + i] = __uint_as_float(r3[i]);
         }
       }
       const int kbase = j * BKV;
@@ -246,9 +330,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int c = 0; c < BKV; ++c)
           if (kbase + c >= p.seq) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      // Row max as 8 independent chains, then a tree.
+      float m8[8];
 #pragma unroll
-      for (int c = 1; c < BKV; ++c) mx = fmaxf(mx, s[c]);
+      for (int i = 0; i < 8; ++i) m8[i] = fmaxf(s[i], s[8 + i]);
+#pragma unroll
+      for (int c = 16; c < BKV; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = max3f(m8[i], s[c + i], s[c + 8 + i]);
+      }
+      float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       mx *= p.scale_log2;
       float alpha = 1.0f;
       if (j == 0) {
@@ -257,21 +348,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         alpha = ex2(m - mx);
         m = mx;
       }
-      uint32_t pk[BKV / 2];
-      float rs = 0.0f;
-#pragma unroll
-      for (int c = 0; c < BKV / 2; ++c) {
-        const float a = ex2(fmaf(s[2 * c], p.scale_log2, -m));
-        const float b = ex2(fmaf(s[2 * c + 1], p.scale_log2, -m));
-        rs += a + b;
-        const __half2 h2 = __floats2half2_rn(a, b);
-        pk[c] = *reinterpret_cast<const uint32_t*>(&h2);
-      }
-      l = l * alpha + rs;
       if (j > 0) {
-        // P_g and O_g are free once the previous P_g V has completed.
-        good = wait_bar(&pv_done[g], (j - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
-        if (!__all_sync(0xffffffffu, good)) {
+        // P_g and O_g are free once the previous P_g V has completed (it
+        // precedes S_g of this step in the MMA stream, so this is immediate).
+        bool good2 = wait_bar(&pv_done[g], (j - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+        if (!__all_sync(0xffffffffu, good2)) {
           ok = false;
           break;
         }
@@ -288,15 +369,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
-      {
-        uint32_t r[32];
+      unsigned long long rs2[4] = {0ull, 0ull, 0ull, 0ull};
+      const unsigned long long sc2 = pack2(p.scale_log2, p.scale_log2);
+      const unsigned long long nm2 = pack2(-m, -m);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = pk[i];
-        tmem_st32(s_addr, r);
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = pk[32 + i];
-        tmem_st32(s_addr + 32, r);
+        for (int i = 0; i < 16; ++i) {
+          const int c = ch * 16 + i;
+          const unsigned long long x2 = fma2(pack2(s[2 * c], s[2 * c + 1]), sc2, nm2);
+          float x0, x1;
+          unpack2(x2, x0, x1);
+          const float a = ex2(x0);
+          const float b = ex2(x1);
+          rs2[c & 3] = add2(rs2[c & 3], pack2(a, b));
+          pk[i] = cvt_h2(a, b);
+        }
+        tmem_st16(s_addr + ch * 16, pk);
       }
+      float rsv[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) unpack2(rs2[i], rsv[2 * i], rsv[2 * i + 1]);
+      const float rs = ((rsv[0] + rsv[1]) + (rsv[2] + rsv[3])) + ((rsv[4] + rsv[5]) + (rsv[6] + rsv[7]));
+      l = l * alpha + rs;
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -331,12 +427,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
-  }
-
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) bar_arrive(sm_done);
   }
 }
 
@@ -367,9 +460,18 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
   p.err = device_error_word();
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn::attention_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         attn::SMEM_BYTES);
+    // setmaxnreg.inc waits until the block's launch allocation can supply
+    // the registers: refuse to launch unless the kernel was built with the
+    // per-thread count the split above assumes.
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, attn::attention_kernel);
+    if (e != cudaSuccess) return cuda_status(e, "attention function attributes");
+    if (fa.numRegs != attn::kLaunchRegs)
+      return fail(-2, "attention: kernel built with " + std::to_string(fa.numRegs) +
+                          " registers per thread, the register split needs " +
+                          std::to_string(attn::kLaunchRegs));
+    e = cudaFuncSetAttribute(attn::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             attn::SMEM_BYTES);
     if (e != cudaSuccess) return cuda_status(e, "attention set smem attribute");
     attr = true;
   }
