@@ -47,6 +47,13 @@ WORKLOAD_2048 = ("flux1-schnell DiT denoise step @2048^2: 19 double + 38 single 
                  "L = 512 text + 16384 image tokens, one image split across the GPUs")
 
 
+# DRAM traffic of the B1_0 GEMM (dram__bytes_read.sum + dram__bytes_write.sum),
+# summed over the 229 b1_gemm launches of one flux1 1024^2 step and divided by
+# 229: one ncu capture of this bench on one B200 (one pass per launch), kept in
+# profiles/b1_gemm_dram_flux1_1024.md.  It applies to the default workload only.
+GEMM_DRAM_BYTES_PER_LAUNCH = 116.53e6
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -90,15 +97,19 @@ class CpuSample:
 
     One double block and one single block at the full token count
     (L = 4608), with the reference's own b1_linear_f32_f32 (AVX2 build in
-    oracle/_ref, all host threads) on 1/ROW_FRAC of each linear's output
-    rows, attention for 1 of the 24 heads, and the remaining ops (LayerNorm-
-    modulate, Q/K RMSNorm + RoPE, GELU) in full through the CPU restatement
-    of the ggml built-ins.  Each part's time is scaled by the work it
-    skipped, then ms/step = 19 * double + 38 * single + edges.
+    oracle/_ref, all host threads) on 1/row_frac of each linear's output
+    rows, attention for `heads` of the 24 heads, and the remaining ops
+    (LayerNorm-modulate, Q/K RMSNorm + RoPE, GELU) in full through the CPU
+    restatement of the ggml built-ins.  Each part's time is scaled by the
+    work it skipped, then ms/step = 19 * double + 38 * single + edges.
+    The bench line's cpu_baseline uses every output row and 4 heads (about
+    10-20 s of CPU work on a 16-core host); the --impl reference arm times a
+    lighter sample per step so that its K + W steps finish in minutes.
     """
-    ROW_FRAC = 16
 
-    def __init__(self, threads: int):
+    def __init__(self, threads: int, row_frac: int = 1, heads: int = 4):
+        self.ROW_FRAC = row_frac
+        self.heads = heads
         import ctypes
         from oracle import pyoracle as O
         self.O = O
@@ -143,10 +154,10 @@ class CpuSample:
             self.w[key] = raw.reshape(rows, nb * 6)
         return self.w[key]
 
-    def _lin(self, tokens, K, N):
-        """Time the reference B1 kernel on N/ROW_FRAC rows; return the full-N estimate (s)."""
+    def _lin(self, tokens, K, N, row_frac=None):
+        """Time the reference B1 kernel on N/row_frac rows; return the full-N estimate (s)."""
         O = self.O
-        n = max(1, N // self.ROW_FRAC)
+        n = max(1, N // (row_frac or self.ROW_FRAC))
         w = self._packed(n, K)
         act = np.ascontiguousarray(self.x[:tokens, :K])
         out = np.zeros((tokens, n), np.float32)
@@ -173,10 +184,11 @@ class CpuSample:
             self.qkh.ctypes.data, 1, L, HD, self.nw.ctypes.data, self.nw.ctypes.data, TXT, 1e-6,
             self.cos.ctypes.data, self.sin.ctypes.data))
 
-    def _attn(self):  # 1 of 24 heads, scaled
-        return HEADS * self._timed(lambda: self.fast.orc_attention(
+    def _attn(self):  # `heads` of 24 heads, one at a time, scaled
+        t = sum(self._timed(lambda: self.fast.orc_attention(
             self.q1.ctypes.data, self.q1.ctypes.data, self.q1.ctypes.data, L, 1, HD,
-            float(HD ** -0.5), self.att.ctypes.data))
+            float(HD ** -0.5), self.att.ctypes.data)) for _ in range(self.heads))
+        return HEADS / self.heads * t
 
     def _gelu(self, rows):
         return self._timed(lambda: self.fast.orc_gelu(self.x.ctypes.data, rows, MLP,
@@ -191,16 +203,19 @@ class CpuSample:
                     + self._lin(tok, MLP, H))
         sgl = self._ln(L) + self._qk() + self._attn() + self._gelu(L)
         sgl += self._lin(L, H, 3 * H + MLP) + self._lin(L, H + MLP, H)
-        mods = self._lin(1, H, DEPTH * 12 * H + SINGLE * 3 * H)
+        # one token x 1.05 M modulation rows: sampled at 1/16 of the rows (a
+        # full-size packed copy would be 0.6 GB of host memory)
+        mods = self._lin(1, H, DEPTH * 12 * H + SINGLE * 3 * H, row_frac=max(16, self.ROW_FRAC))
         edges = self._lin(TXT, CTX, H)  # text embedder (dominant edge op), B1-rate proxy
         ms = 1000.0 * (DEPTH * dbl + SINGLE * sgl + mods + edges)
         return ms, time.perf_counter() - t_start
 
     def describe(self):
+        rows = "all" if self.ROW_FRAC == 1 else f"1/{self.ROW_FRAC}"
         return (f"1 double + 1 single block at L=4608 per sample: reference b1_linear_f32_f32 "
-                f"(AVX2, oracle/_ref) on 1/{self.ROW_FRAC} of each linear's output rows, attention "
-                f"on 1 of 24 heads, LayerNorm/RMSNorm/RoPE/GELU in full (CPU restatement of the "
-                f"ggml built-ins); scaled to 19 double + 38 single blocks + modulation + edges")
+                f"(AVX2, oracle/_ref) on {rows} of each linear's output rows, attention "
+                f"on {self.heads} of 24 heads, LayerNorm/RMSNorm/RoPE/GELU in full (CPU restatement "
+                f"of the ggml built-ins); scaled to 19 double + 38 single blocks + modulation + edges")
 
 
 def run_reference(args):
@@ -209,7 +224,7 @@ def run_reference(args):
         return 0
     threads = os.cpu_count() or 1
     with stdout_to_stderr():
-        cs = CpuSample(threads)
+        cs = CpuSample(threads, row_frac=16, heads=1)
         for _ in range(args.warmup):
             cs.run()
         vals = []
@@ -422,7 +437,10 @@ def run_bonsai(args):
                      "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
                      "frac": round(gemm_tf / pk["bf16_sustained"], 4),
                      "peak_kind": f"{pk['source']} sustained bf16 (dense GEMM under the power cap)",
-                     "frac_of_burst": round(gemm_tf / pk["bf16"], 4), "traffic": None,
+                     "frac_of_burst": round(gemm_tf / pk["bf16"], 4),
+                     "traffic": None if split else GEMM_DRAM_BYTES_PER_LAUNCH,
+                     "traffic_unit": "bytes per launch (mean over the step's launches, ncu)",
+                     "algorithmic_bytes": round(g["bytes"] / g["launches"]) if g else None,
                      "measured": "sum of 2*M*N*K over every b1_gemm launch / sum of their "
                                  "CUDA-event durations, over a second pass of the K steps"},
         "attention_roofline": {"bound": "tensor", "kernel": "attention",
@@ -441,9 +459,11 @@ def run_bonsai(args):
         threads = os.cpu_count() or 1
         with stdout_to_stderr():
             cs = CpuSample(threads)
-            cpu_ms, sample_s = cs.run()
+            runs = [cs.run() for _ in range(2)]  # two samples, ~10-20 s of CPU work in total
+            cpu_ms = statistics.mean(r[0] for r in runs)
+            sample_s = sum(r[1] for r in runs)
         line["cpu_baseline"] = {"value": round(cpu_ms, 1), "unit": "ms", "cores": threads,
-                                "kind": cs.kind, "sample": cs.describe(),
+                                "kind": cs.kind, "sample": "mean of 2 samples; each " + cs.describe(),
                                 "sample_seconds": round(sample_s, 2)}
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -181,6 +181,16 @@ def b1_gemm(x16, w: B1Weight, mode: int, out, gate=None, stream=None) -> None:
                                stream_ptr(stream)), "bonsai_b1_gemm")
 
 
+def joint_attention(q, k, v, out, scale=None, stream=None) -> None:
+    """softmax(Q K^T * scale) V per head: q/k/v f16 [H][L][128] head-major,
+    out f16 [L][ld >= H*128] token-major (head h at columns h*128)."""
+    H, L, D = q.shape
+    check(lib().bonsai_joint_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), H, L, D,
+                                       float(scale if scale is not None else D ** -0.5),
+                                       out.data_ptr(), out.stride(0), stream_ptr(stream)),
+          "bonsai_joint_attention")
+
+
 # ----------------------------------------------------------------- host side
 def random_b1_packed(out_dim: int, in_dim: int, rng: np.random.Generator,
                      scale_std: float = 0.02) -> np.ndarray:

@@ -1,0 +1,75 @@
+"""Time one kernel of the step in isolation (and give ncu a small, fixed case).
+
+    python -m bonsai_b200.kernel_bench gemm M K N [--kernel auto|pair|single] [--reps R]
+    python -m bonsai_b200.kernel_bench attention L [--heads H] [--reps R]
+
+gemm: B1_0 GEMM of M tokens x K inputs -> N outputs (f16 store epilogue) on
+seeded random weights/activations; attention: joint attention over L tokens,
+H heads of 128.  Prints one line: mean time per call over R calls after 3
+warm-up calls (CUDA events on the current stream) and the TFLOP/s.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+
+def _time(fn, reps: int) -> float:
+    import torch
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    sub = ap.add_subparsers(dest="op", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("M", type=int)
+    g.add_argument("K", type=int)
+    g.add_argument("N", type=int)
+    g.add_argument("--kernel", choices=["auto", "pair", "single"], default="auto")
+    g.add_argument("--reps", type=int, default=10)
+    a = sub.add_parser("attention")
+    a.add_argument("L", type=int)
+    a.add_argument("--heads", type=int, default=24)
+    a.add_argument("--reps", type=int, default=10)
+    args = ap.parse_args(argv)
+
+    import numpy as np
+    import torch
+    import bonsai_b200 as bb
+    torch.cuda.init()
+    bb.init(0)
+    if args.op == "gemm":
+        if args.kernel != "auto":
+            os.environ["BONSAI_B1_KERNEL"] = args.kernel
+        w = bb.B1Weight(bb.random_b1_packed(args.N, args.K, np.random.default_rng(1)), args.N, args.K)
+        x = torch.randn(args.M, args.K, device="cuda").half()
+        out = torch.empty(args.M, args.N, device="cuda", dtype=torch.float16)
+        ms = _time(lambda: bb.b1_gemm(x, w, bb.BONSAI_EPI_F16, out), args.reps)
+        flop = 2.0 * args.M * args.N * args.K
+        desc = f"gemm M={args.M} K={args.K} N={args.N} kernel={args.kernel}"
+    else:
+        H, L = args.heads, args.L
+        q, k, v = (torch.randn(H, L, 128, device="cuda").half() for _ in range(3))
+        out = torch.empty(L, H * 128, device="cuda", dtype=torch.float16)
+        ms = _time(lambda: bb.joint_attention(q, k, v, out), args.reps)
+        flop = 4.0 * L * L * 128 * H
+        desc = f"attention L={L} heads={H}"
+    err = bb.device_error()
+    print(f"{desc}: {ms * 1e3:.1f} us/call, {flop / (ms / 1e3) / 1e12:.1f} TFLOP/s, device_error={err}")
+    return 0 if err == 0 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
