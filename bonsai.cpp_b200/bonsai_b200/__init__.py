@@ -42,6 +42,8 @@ SIGNATURES = {
     "bonsai_last_error": (ctypes.c_char_p, []),
     "bonsai_init": (_c_int, [_c_int]),
     "bonsai_device_error": (_c_int, []),
+    "bonsai_shutdown": (_c_int, []),
+    "bonsai_count_nonfinite": (_c_int, [_vp, _c_ll, ctypes.POINTER(_c_ll), _vp]),
     "bonsai_launch_count": (_c_ll, []),
     "bonsai_profile_start": (_c_int, []),
     "bonsai_profile_stop": (_c_int, [ctypes.c_char_p, _c_int]),
@@ -67,6 +69,9 @@ SIGNATURES = {
     "bonsai_dit_double_block": (_c_int, [_vp, _c_int, _vp]),
     "bonsai_dit_single_block": (_c_int, [_vp, _c_int, _vp]),
     "bonsai_dit_weight": (_c_ll, [_vp, ctypes.c_char_p, _vp, _c_ll]),
+    "bonsai_dit_set_weight": (_c_int, [_vp, ctypes.c_char_p, _vp, _c_ll]),
+    "bonsai_dit_load_safetensors": (_c_int, [_vp, ctypes.c_char_p]),
+    "bonsai_dit_sample": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp]),
     "bonsai_dit_set_partition": (_c_int, [_vp, _c_int, _c_int]),
     "bonsai_dit_buffer": (_c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(_c_ll)]),
     "bonsai_dit_begin": (_c_int, [_vp, _vp, _vp, _vp, _fp, _vp]),
@@ -181,6 +186,18 @@ def b1_gemm(x16, w: B1Weight, mode: int, out, gate=None, stream=None) -> None:
                                stream_ptr(stream)), "bonsai_b1_gemm")
 
 
+def count_nonfinite(x, stream=None) -> int:
+    """Number of NaN / Inf values in a device f32 tensor."""
+    n = _c_ll()
+    check(lib().bonsai_count_nonfinite(x.data_ptr(), x.numel(), ctypes.byref(n), stream_ptr(stream)),
+          "bonsai_count_nonfinite")
+    return int(n.value)
+
+
+def shutdown() -> None:
+    check(lib().bonsai_shutdown(), "bonsai_shutdown")
+
+
 def joint_attention(q, k, v, out, scale=None, stream=None) -> None:
     """softmax(Q K^T * scale) V per head: q/k/v f16 [H][L][128] head-major,
     out f16 [L][ld >= H*128] token-major (head h at columns h*128)."""
@@ -268,6 +285,28 @@ class Dit:
         check(0 if lib().bonsai_dit_weight(self.handle, name.encode(), buf.ctypes.data, n) == n
               else -1, f"bonsai_dit_weight({name})")
         return buf
+
+    def set_weight(self, name: str, data: np.ndarray):
+        """Replace a weight from host bytes in the layout weight() returns."""
+        buf = np.ascontiguousarray(data)
+        check(lib().bonsai_dit_set_weight(self.handle, name.encode(), buf.ctypes.data, buf.nbytes),
+              f"bonsai_dit_set_weight({name})")
+
+    def load_safetensors(self, path):
+        """Load a checkpoint in the reference's packed safetensors layout (klein4b)."""
+        check(lib().bonsai_dit_load_safetensors(self.handle, str(path).encode()),
+              "bonsai_dit_load_safetensors")
+
+    def sample(self, latents, txt, pooled, n_steps: int, stream=None) -> np.ndarray:
+        """Whole Euler loop on the device (latents updated in place); returns the
+        per-step stats [n_steps][5] = NaN count, Inf count, min, max, mean."""
+        stats = np.zeros((n_steps, 5), np.float32)
+        check(lib().bonsai_dit_sample(self.handle, latents.data_ptr(),
+                                      txt.data_ptr() if txt is not None else None,
+                                      pooled.data_ptr() if pooled is not None else None,
+                                      n_steps, stats.ctypes.data, stream_ptr(stream)),
+              "bonsai_dit_sample")
+        return stats
 
     def weight_f32(self, name: str) -> np.ndarray:
         return self.weight(name).view(np.float32)

@@ -172,6 +172,28 @@ int bonsai_init(int device) {
   return 0;
 }
 
+int bonsai_shutdown(void) {
+  // Waits for the device, then releases what the library allocated lazily for
+  // this host thread on the current device (the f16 activation scratch of
+  // bonsai_b1_linear_f32) and any pending profiling events.  Weight handles
+  // and models stay valid until their own free/destroy calls.
+  int d = 0;
+  cudaGetDevice(&d);
+  const cudaError_t e = cudaDeviceSynchronize();
+  Scratch& sc = g_scratch[d & 63];
+  if (sc.ptr) {
+    cudaFree(sc.ptr);
+    sc = Scratch{};
+  }
+  for (auto& r : g_prof) {
+    cudaEventDestroy(r.e0);
+    cudaEventDestroy(r.e1);
+  }
+  g_prof.clear();
+  g_prof_on = false;
+  return cuda_status(e, "bonsai_shutdown: device synchronize");
+}
+
 int bonsai_profile_start(void) {
   for (auto& r : g_prof) {
     cudaEventDestroy(r.e0);

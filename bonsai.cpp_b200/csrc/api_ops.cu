@@ -26,6 +26,26 @@ static cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
 
 extern "C" {
 
+int bonsai_count_nonfinite(const float* x, long long n, long long* count, void* stream) {
+  if (!count || n < 0 || (n > 0 && !x)) return fail(BONSAI_ERR_ARG, "count_nonfinite: bad argument");
+  *count = 0;
+  if (n == 0) return 0;
+  cudaStream_t st = S(stream);
+  unsigned long long* d = nullptr;
+  int rc = cuda_status(cudaMallocAsync(reinterpret_cast<void**>(&d), sizeof(*d), st),
+                       "count_nonfinite: allocation");
+  if (rc) return rc;
+  unsigned long long h = 0;
+  rc = cuda_status(cudaMemsetAsync(d, 0, sizeof(*d), st), "count_nonfinite: memset");
+  if (!rc) rc = launch_count_nonfinite(x, n, d, st);
+  if (!rc) rc = cuda_status(cudaMemcpyAsync(&h, d, sizeof(h), cudaMemcpyDeviceToHost, st),
+                            "count_nonfinite: copy");
+  cudaFreeAsync(d, st);
+  if (!rc) rc = cuda_status(cudaStreamSynchronize(st), "count_nonfinite: synchronize");
+  if (!rc) *count = (long long)h;
+  return rc;
+}
+
 int bonsai_rope_2d_f32(const float* x, const float* cos_t, const float* sin_t, int head_dim,
                        int n_heads, int seq, float* out, void* stream) {
   if (seq == 0 || n_heads == 0) return 0;

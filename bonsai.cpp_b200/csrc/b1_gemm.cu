@@ -771,6 +771,47 @@ __global__ void b1_retile_kernel(const uint8_t* __restrict__ src, uint32_t* __re
   }
 }
 
+// Inverse of compress_even_bits: bit j of x (j < 16) -> bit 2j.
+__device__ __forceinline__ uint32_t spread_even_bits(uint32_t x) {
+  x &= 0x0000FFFFu;
+  x = (x | (x << 8)) & 0x00FF00FFu;
+  x = (x | (x << 4)) & 0x0F0F0F0Fu;
+  x = (x | (x << 2)) & 0x33333333u;
+  x = (x | (x << 1)) & 0x55555555u;
+  return x;
+}
+
+// Packed row srow, group grp <- device chunks (the exact inverse of
+// b1_retile_kernel, including the SwiGLU row interleave).
+__global__ void b1_unretile_kernel(const uint32_t* __restrict__ chunks, uint8_t* __restrict__ dst,
+                                   int N, int K, int k_blocks, int swiglu_from) {
+  const int groups = K / 32;
+  const long long total = (long long)N * groups;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int srow = (int)(i / groups);
+    const int grp = (int)(i - (long long)srow * groups);
+    int n = srow;
+    if (swiglu_from >= 0 && srow >= swiglu_from) {
+      const int half = (N - swiglu_from) / 2;
+      const int j = srow - swiglu_from;
+      n = swiglu_from + (j < half ? 2 * j : 2 * (j - half) + 1);
+    }
+    const int ftile = n / 128, r = n % 128, kb = grp / 2, g = grp & 1;
+    const uint32_t* c = chunks + ((size_t)ftile * k_blocks + kb) * kChunkWords;
+    const uint32_t word = c[g * 128 + r];
+    const uint32_t sc = (c[256 + r] >> (16 * g)) & 0xFFFFu;
+    const uint32_t bits = spread_even_bits(word) | (spread_even_bits(word >> 16) << 1);
+    uint8_t* o = dst + ((size_t)srow * groups + grp) * 6;
+    o[0] = (uint8_t)(sc & 0xFF);
+    o[1] = (uint8_t)(sc >> 8);
+    o[2] = (uint8_t)(bits & 0xFF);
+    o[3] = (uint8_t)((bits >> 8) & 0xFF);
+    o[4] = (uint8_t)((bits >> 16) & 0xFF);
+    o[5] = (uint8_t)(bits >> 24);
+  }
+}
+
 // -------------------------------------------------------------- tensor maps
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -877,6 +918,17 @@ int pair_cluster_slots(bool bf16) {
 }
 
 }  // namespace
+
+int launch_b1_unretile(const B1Weight& w, uint8_t* dev_packed, cudaStream_t st) {
+  const long long total = (long long)w.n_rows * (w.k_in / 32);
+  if (total <= 0) return 0;
+  const int threads = 256;
+  const long long blocks = std::min<long long>((total + threads - 1) / threads, 65535LL * 8);
+  gemm::b1_unretile_kernel<<<(unsigned)blocks, threads, 0, st>>>(w.chunks, dev_packed, w.n_rows,
+                                                                 w.k_in, w.k_blocks,
+                                                                 w.swiglu_from);
+  return launch_status("b1_unretile_kernel launch");
+}
 
 int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, const EpiSeg* segs,
                    int nseg, bool x_bf16, cudaStream_t st, const TileSel* sel) {

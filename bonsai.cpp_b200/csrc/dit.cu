@@ -96,6 +96,11 @@ struct TensorInfo {
   long long rows, cols;  // B1: out_dim, in_dim; F32: numel in rows*cols
   uint64_t tid;
   float mean, stdv;
+  // Where the tensor lives on the device: B1 rows [row_off, row_off + rows)
+  // of *b1 (row_off is a multiple of 128), or f32 values at f32.
+  B1Weight* b1 = nullptr;
+  long long row_off = 0;
+  float* f32 = nullptr;
 };
 
 struct DoubleW {
@@ -188,6 +193,7 @@ int gen_f32_into(const Cfg& c, const TensorInfo& ti, float* dst, cudaStream_t st
 int make_b1(bonsai_dit* m, const std::string& name, long long rows, long long cols,
             int swiglu_from, B1Weight& w, uint8_t* staging) {
   TensorInfo ti{KIND_B1, rows, cols, (uint64_t)m->reg.size() + 1, 0.f, 0.02f};
+  ti.b1 = &w;
   m->reg[name] = ti;
   int rc = gen_b1_into(m->c, ti, staging, 0);
   if (rc) return rc;
@@ -207,10 +213,28 @@ int make_b1(bonsai_dit* m, const std::string& name, long long rows, long long co
 int make_f32(bonsai_dit* m, const std::string& name, long long rows, long long cols, float mean,
              float stdv, float** out) {
   TensorInfo ti{KIND_F32, rows, cols, (uint64_t)m->reg.size() + 1, mean, stdv};
-  m->reg[name] = ti;
   int rc = dev_alloc(m, reinterpret_cast<void**>(out), (size_t)rows * cols * 4);
   if (rc) return rc;
+  ti.f32 = *out;
+  m->reg[name] = ti;
   return gen_f32_into(m->c, ti, *out, 0);
+}
+
+long long tensor_bytes(const TensorInfo& ti) {
+  return ti.kind == KIND_B1 ? ti.rows * (ti.cols / 32) * 6 : ti.rows * ti.cols * 4;
+}
+
+// The device B1_0 weight a registered tensor occupies: the whole weight, or
+// whole 128-row tiles of a stacked one (the per-block modulation linears).
+B1Weight b1_view(const TensorInfo& ti) {
+  const B1Weight& w = *ti.b1;
+  if (ti.row_off == 0 && ti.rows == w.n_rows) return w;
+  B1Weight v = w;
+  v.n_rows = (int)ti.rows;
+  v.n_ftiles = (int)((ti.rows + 127) / 128);
+  v.swiglu_from = -1;
+  v.chunks = w.chunks + (size_t)(ti.row_off / 128) * w.k_blocks * kChunkWords;
+  return v;
 }
 
 EpiSeg seg_of(int mode, int row_begin, int row_end, void* dst, long long ld, int col_off,
@@ -518,12 +542,16 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
     for (int i = 0; i < c.depth; ++i)
       for (const char* s : {"img_mod", "txt_mod"}) {
         TensorInfo ti{KIND_B1, 6LL * H, H, (uint64_t)m->reg.size() + 1, 0.f, 0.02f};
+        ti.b1 = &m->mod_all;
+        ti.row_off = row;
         m->reg["double." + std::to_string(i) + "." + s] = ti;
         RC(gen_b1_into(c, ti, staging + row * (H / 32) * 6, st));
         row += 6LL * H;
       }
     for (int i = 0; i < c.depth_single; ++i) {
       TensorInfo ti{KIND_B1, 3LL * H, H, (uint64_t)m->reg.size() + 1, 0.f, 0.02f};
+      ti.b1 = &m->mod_all;
+      ti.row_off = row;
       m->reg["single." + std::to_string(i) + ".mod"] = ti;
       RC(gen_b1_into(c, ti, staging + row * (H / 32) * 6, st));
       row += 3LL * H;
@@ -857,16 +885,154 @@ long long bonsai_dit_weight(bonsai_dit_t m, const char* name, void* buf, long lo
   auto it = m->reg.find(name);
   if (it == m->reg.end()) return fail(BONSAI_ERR_ARG, std::string("dit_weight: unknown tensor ") + name);
   const TensorInfo& ti = it->second;
-  const long long bytes = ti.kind == KIND_B1 ? ti.rows * (ti.cols / 32) * 6 : ti.rows * ti.cols * 4;
+  const long long bytes = tensor_bytes(ti);
   if (!buf) return bytes;
   if (cap < bytes) return fail(BONSAI_ERR_ARG, "dit_weight: buffer too small");
+  RC(cuda_status(cudaDeviceSynchronize(), "dit_weight: synchronize"));
+  if (ti.kind == KIND_F32)
+    return cuda_status(cudaMemcpy(buf, ti.f32, bytes, cudaMemcpyDeviceToHost), "dit_weight copy") ? BONSAI_ERR_CUDA : bytes;
+  // B1_0: the device copy, turned back into the packed file layout.
   void* tmp = nullptr;
   if (cudaMalloc(&tmp, bytes) != cudaSuccess) return fail(BONSAI_ERR_NOMEM, "dit_weight: staging allocation failed");
-  int rc = ti.kind == KIND_B1 ? gen_b1_into(m->c, ti, static_cast<uint8_t*>(tmp), 0)
-                              : gen_f32_into(m->c, ti, static_cast<float*>(tmp), 0);
+  int rc = launch_b1_unretile(b1_view(ti), static_cast<uint8_t*>(tmp), 0);
   if (!rc) rc = cuda_status(cudaMemcpy(buf, tmp, bytes, cudaMemcpyDeviceToHost), "dit_weight copy");
   cudaFree(tmp);
   return rc ? rc : bytes;
+}
+
+int bonsai_dit_set_weight(bonsai_dit_t m, const char* name, const void* host, long long bytes) {
+  if (!m || !name || !host) return fail(BONSAI_ERR_ARG, "dit_set_weight: null argument");
+  auto it = m->reg.find(name);
+  if (it == m->reg.end())
+    return fail(BONSAI_ERR_ARG, std::string("dit_set_weight: unknown tensor ") + name);
+  const TensorInfo& ti = it->second;
+  if (bytes != tensor_bytes(ti))
+    return fail(BONSAI_ERR_ARG, std::string("dit_set_weight: ") + name + " takes " +
+                                    std::to_string(tensor_bytes(ti)) + " bytes, got " +
+                                    std::to_string(bytes));
+  // No forward of this model may be running while its weights change.
+  RC(cuda_status(cudaDeviceSynchronize(), "dit_set_weight: synchronize"));
+  if (ti.kind == KIND_F32)
+    return cuda_status(cudaMemcpy(ti.f32, host, bytes, cudaMemcpyHostToDevice), "dit_set_weight copy");
+  void* tmp = nullptr;
+  if (cudaMalloc(&tmp, bytes) != cudaSuccess) return fail(BONSAI_ERR_NOMEM, "dit_set_weight: staging allocation failed");
+  int rc = cuda_status(cudaMemcpy(tmp, host, bytes, cudaMemcpyHostToDevice), "dit_set_weight copy");
+  B1Weight v = b1_view(ti);
+  if (!rc) rc = launch_b1_retile(static_cast<const uint8_t*>(tmp), v, 0);
+  if (!rc) rc = cuda_status(cudaDeviceSynchronize(), "dit_set_weight: retile");
+  cudaFree(tmp);
+  return rc;
+}
+
+int bonsai_dit_load_safetensors(bonsai_dit_t m, const char* path) {
+  if (!m || !path) return fail(BONSAI_ERR_ARG, "dit_load_safetensors: null argument");
+  if (m->c.preset != BONSAI_PRESET_KLEIN4B)
+    return fail(BONSAI_ERR_UNSUPPORTED,
+                "dit_load_safetensors: the reference's checkpoint layout (src/diffuser.cpp:88-186) "
+                "exists for the klein4b preset only");
+  StFile f;
+  RC(st_open(path, f));
+  // Our tensor <- the reference's tensors, stacked by rows in this order.
+  std::vector<std::pair<std::string, std::vector<std::string>>> map = {
+      {"img_in.w", {"x_embedder.weight"}},
+      {"txt_in.w", {"context_embedder.weight"}},
+      {"time.w1", {"time_guidance_embed.timestep_embedder.linear_1.weight"}},
+      {"time.w2", {"time_guidance_embed.timestep_embedder.linear_2.weight"}},
+      {"mod_img.w", {"double_stream_modulation_img.linear.weight"}},
+      {"mod_txt.w", {"double_stream_modulation_txt.linear.weight"}},
+      {"mod_single.w", {"single_stream_modulation.linear.weight"}},
+      {"norm_out.w", {"norm_out.linear.weight"}},
+      {"proj_out.w", {"proj_out.weight"}},
+  };
+  for (int d = 0; d < m->c.depth; ++d) {
+    const std::string o = "double." + std::to_string(d) + ".";
+    const std::string r = "transformer_blocks." + std::to_string(d) + ".";
+    map.push_back({o + "img_qkv", {r + "attn.to_q.weight", r + "attn.to_k.weight", r + "attn.to_v.weight"}});
+    map.push_back({o + "txt_qkv", {r + "attn.add_q_proj.weight", r + "attn.add_k_proj.weight",
+                                   r + "attn.add_v_proj.weight"}});
+    map.push_back({o + "img_out", {r + "attn.to_out.0.weight"}});
+    map.push_back({o + "txt_out", {r + "attn.to_add_out.weight"}});
+    map.push_back({o + "img_norm_q", {r + "attn.norm_q.weight"}});
+    map.push_back({o + "img_norm_k", {r + "attn.norm_k.weight"}});
+    map.push_back({o + "txt_norm_q", {r + "attn.norm_added_q.weight"}});
+    map.push_back({o + "txt_norm_k", {r + "attn.norm_added_k.weight"}});
+    map.push_back({o + "img_mlp_in", {r + "ff.linear_in.weight"}});
+    map.push_back({o + "img_mlp_out", {r + "ff.linear_out.weight"}});
+    map.push_back({o + "txt_mlp_in", {r + "ff_context.linear_in.weight"}});
+    map.push_back({o + "txt_mlp_out", {r + "ff_context.linear_out.weight"}});
+  }
+  for (int s = 0; s < m->c.depth_single; ++s) {
+    const std::string o = "single." + std::to_string(s) + ".";
+    const std::string r = "single_transformer_blocks." + std::to_string(s) + ".attn.";
+    map.push_back({o + "proj", {r + "to_qkv_mlp_proj.weight"}});
+    map.push_back({o + "out", {r + "to_out.weight"}});
+    map.push_back({o + "norm_q", {r + "norm_q.weight"}});
+    map.push_back({o + "norm_k", {r + "norm_k.weight"}});
+  }
+  std::vector<uint8_t> buf;
+  for (const auto& e : map) {
+    auto it = m->reg.find(e.first);
+    if (it == m->reg.end()) return fail(BONSAI_ERR_ARG, "dit_load_safetensors: model lacks " + e.first);
+    const TensorInfo& ti = it->second;
+    const long long want = tensor_bytes(ti);
+    buf.resize((size_t)want);
+    long long off = 0, rows = 0;
+    for (const std::string& src : e.second) {
+      auto ts = f.tensors.find(src);
+      if (ts == f.tensors.end())
+        return fail(BONSAI_ERR_ARG, "dit_load_safetensors: tensor '" + src + "' not found in " + path);
+      const StTensor& t = ts->second;
+      const long long n = t.end - t.begin;
+      if (ti.kind == KIND_B1) {
+        // packed [out][in/32*6] bytes (convert_to_b1_0_packed.py:21-43)
+        if ((t.dtype != "U8" && t.dtype != "I8") || t.shape.size() != 2 ||
+            t.shape[1] != (ti.cols / 32) * 6 || n != t.shape[0] * t.shape[1])
+          return fail(BONSAI_ERR_ARG, "dit_load_safetensors: '" + src + "' is not a packed B1_0 [" +
+                                          "rows][" + std::to_string((ti.cols / 32) * 6) + "] U8 tensor");
+        rows += t.shape[0];
+      } else if (t.dtype != "F32") {
+        return fail(BONSAI_ERR_ARG, "dit_load_safetensors: '" + src + "' must be F32, found " + t.dtype);
+      }
+      if (off + n > want)
+        return fail(BONSAI_ERR_ARG, "dit_load_safetensors: '" + src + "' is larger than " + e.first);
+      RC(st_read(f, t, buf.data() + off, n));
+      off += n;
+    }
+    if (off != want || (ti.kind == KIND_B1 && rows != ti.rows))
+      return fail(BONSAI_ERR_ARG, "dit_load_safetensors: the tensors for " + e.first + " hold " +
+                                      std::to_string(off) + " bytes, the model needs " +
+                                      std::to_string(want));
+    RC(bonsai_dit_set_weight(m, e.first.c_str(), buf.data(), want));
+  }
+  return 0;
+}
+
+int bonsai_dit_sample(bonsai_dit_t m, float* latents, const float* txt, const float* pooled,
+                      int n_steps, float* stats, void* stream) {
+  if (!m || !latents || n_steps < 1) return fail(BONSAI_ERR_ARG, "dit_sample: bad argument");
+  if (m->world > 1)
+    return fail(BONSAI_ERR_ARG, "dit_sample: a partitioned model is driven with bonsai_dit_begin/phase/end");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long n = (long long)m->c.img * m->c.in_ch;
+  float* dstats = nullptr;
+  RC(cuda_status(cudaMallocAsync(reinterpret_cast<void**>(&dstats), (size_t)n_steps * 5 * 4, st),
+                 "dit_sample: stats allocation"));
+  int rc = 0;
+  // Timesteps and step sizes exactly as the reference's loop computes them
+  // (src/diffuser.cpp:251-255, :258-259), in float.
+  for (int step = 0; step < n_steps && !rc; ++step) {
+    const float t = 1.0f - (float)step / n_steps;
+    const float t_next = 1.0f - (float)(step + 1) / n_steps;
+    const float dt = (step < n_steps - 1) ? t - t_next : t;
+    rc = bonsai_dit_forward(m, latents, txt, pooled, t * 1000.0f, m->out_buf, stream);
+    if (!rc) rc = launch_euler_stats(latents, m->out_buf, n, dt, dstats + 5LL * step, st);
+  }
+  if (!rc && stats)
+    rc = cuda_status(cudaMemcpyAsync(stats, dstats, (size_t)n_steps * 5 * 4, cudaMemcpyDeviceToHost, st),
+                     "dit_sample: stats copy");
+  cudaFreeAsync(dstats, st);
+  if (!rc && stats) rc = cuda_status(cudaStreamSynchronize(st), "dit_sample: synchronize");
+  return rc;
 }
 
 }  // extern "C"

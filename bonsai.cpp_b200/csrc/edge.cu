@@ -186,6 +186,72 @@ __global__ void add_kernel(const float* __restrict__ a, const float* __restrict_
     y[i] = a[i] + b[i];
 }
 
+// Non-finite values (NaN or +-Inf) in x, one atomic per warp.
+__global__ void count_nonfinite_kernel(const float* __restrict__ x, long long n,
+                                       unsigned long long* __restrict__ count) {
+  unsigned int mine = 0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    mine += isfinite(x[i]) ? 0u : 1u;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+  if ((threadIdx.x & 31) == 0 && mine) atomicAdd(count, (unsigned long long)mine);
+}
+
+// One Euler step of the reference's sampler (src/diffuser.cpp:290-291):
+// lat += dt * pred, plus the per-step diagnostics it prints (:276-288):
+// stats = {NaN count, Inf count, min, max, mean} of pred, min/max over the
+// non-NaN values.  One CTA of kEulerThreads; deterministic reduction order.
+constexpr int kEulerThreads = 1024;
+__global__ void __launch_bounds__(kEulerThreads)
+    euler_stats_kernel(float* __restrict__ lat, const float* __restrict__ pred, long long n,
+                       float dt, float* __restrict__ stats) {
+  __shared__ float s_min[kEulerThreads / 32], s_max[kEulerThreads / 32], s_sum[kEulerThreads / 32];
+  __shared__ unsigned int s_nan[kEulerThreads / 32], s_inf[kEulerThreads / 32];
+  unsigned int nan_c = 0, inf_c = 0;
+  float mn = INFINITY, mx = -INFINITY, sum = 0.0f;
+  for (long long i = threadIdx.x; i < n; i += kEulerThreads) {
+    const float v = pred[i];
+    if (isnan(v)) ++nan_c;
+    else if (isinf(v)) ++inf_c;
+    mn = fminf(mn, v);
+    mx = fmaxf(mx, v);
+    sum += v;
+    lat[i] = __fadd_rn(lat[i], __fmul_rn(dt, v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    nan_c += __shfl_xor_sync(0xffffffffu, nan_c, o);
+    inf_c += __shfl_xor_sync(0xffffffffu, inf_c, o);
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  const int w = threadIdx.x / 32;
+  if ((threadIdx.x & 31) == 0) {
+    s_nan[w] = nan_c;
+    s_inf[w] = inf_c;
+    s_min[w] = mn;
+    s_max[w] = mx;
+    s_sum[w] = sum;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < kEulerThreads / 32; ++k) {
+      nan_c += s_nan[k];
+      inf_c += s_inf[k];
+      mn = fminf(mn, s_min[k]);
+      mx = fmaxf(mx, s_max[k]);
+      sum += s_sum[k];
+    }
+    stats[0] = (float)nan_c;
+    stats[1] = (float)inf_c;
+    stats[2] = mn;
+    stats[3] = mx;
+    stats[4] = n > 0 ? sum / (float)n : 0.0f;
+  }
+}
+
 }  // namespace edge
 
 int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* W, const float* b,
@@ -240,6 +306,20 @@ int launch_add_f32(const float* a, const float* b, long long n, float* y, cudaSt
   const long long blocks = std::min<long long>((n + 255) / 256, 4096);
   edge::add_kernel<<<(unsigned)blocks, 256, 0, st>>>(a, b, n, y);
   return launch_status("add launch");
+}
+
+int launch_count_nonfinite(const float* x, long long n, unsigned long long* dev_count,
+                           cudaStream_t st) {
+  if (n <= 0) return 0;
+  const long long blocks = std::min<long long>((n + 255) / 256, (long long)num_sms() * 8);
+  edge::count_nonfinite_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, n, dev_count);
+  return launch_status("count_nonfinite launch");
+}
+
+int launch_euler_stats(float* lat, const float* pred, long long n, float dt, float* stats,
+                       cudaStream_t st) {
+  edge::euler_stats_kernel<<<1, edge::kEulerThreads, 0, st>>>(lat, pred, n, dt, stats);
+  return launch_status("euler_stats launch");
 }
 
 }  // namespace bonsai

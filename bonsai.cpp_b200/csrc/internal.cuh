@@ -6,7 +6,10 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <cstdio>
+#include <map>
 #include <string>
+#include <vector>
 
 namespace bonsai {
 
@@ -93,6 +96,27 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w,
 
 // Retile packed reference bytes (device copy) into the chunked layout.
 int launch_b1_retile(const uint8_t* dev_packed, B1Weight& w, cudaStream_t st);
+// Inverse of launch_b1_retile: device chunks of w back to the packed
+// [n_rows][k_in/32][6] bytes (dev_packed, device memory).
+int launch_b1_unretile(const B1Weight& w, uint8_t* dev_packed, cudaStream_t st);
+
+// ------------------------------------------------------------ safetensors
+// Index of a .safetensors file: 8-byte little-endian header length, JSON
+// header {name: {"dtype", "shape", "data_offsets": [begin, end]}}, then the
+// tensor bytes (offsets relative to the end of the header).
+struct StTensor {
+  std::string dtype;
+  std::vector<long long> shape;
+  long long begin = 0, end = 0;
+};
+struct StFile {
+  FILE* f = nullptr;
+  long long data_start = 0, file_size = 0;
+  std::map<std::string, StTensor> tensors;
+  ~StFile();
+};
+int st_open(const char* path, StFile& out);                     // 0 or a BONSAI_ERR_* code
+int st_read(StFile& f, const StTensor& t, void* dst, long long bytes);
 
 // ------------------------------------------------------------- attention
 // q, k, v: f16 [n_heads][seq][128]; out: f16 [seq][ld_out], head h at columns h*128.
@@ -130,6 +154,12 @@ int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* 
                       float* workspace = nullptr, long long workspace_elems = 0);
 int launch_silu_f32(const float* x, long long n, float* y, cudaStream_t st);
 int launch_add_f32(const float* a, const float* b, long long n, float* y, cudaStream_t st);
+// *dev_count += number of NaN / Inf values in x[0, n).
+int launch_count_nonfinite(const float* x, long long n, unsigned long long* dev_count,
+                           cudaStream_t st);
+// lat += dt * pred and stats[0..4] = {NaN count, Inf count, min, max, mean} of pred.
+int launch_euler_stats(float* lat, const float* pred, long long n, float dt, float* stats,
+                       cudaStream_t st);
 
 }  // namespace bonsai
 

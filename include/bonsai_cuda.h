@@ -66,6 +66,17 @@ int bonsai_init(int device);
  * Synchronises the device. */
 int bonsai_device_error(void);
 
+/* Wait for the current device and release what the library allocated
+ * lazily for the calling thread on it (bonsai_b1_linear_f32's activation
+ * scratch, pending profiling events).  Weight handles and models stay valid.
+ * The counterpart of ggml_backend_free (src/diffuser.cpp:310). */
+int bonsai_shutdown(void);
+
+/* *count = number of NaN / Inf values in the device array x[0, n);
+ * synchronises the stream.  Replaces the reference's NaN/Inf abort() checks
+ * (src/b1_0_kernel.h:45-69, :195-198) with a value the caller can test. */
+int bonsai_count_nonfinite(const float* x, long long n, long long* count, void* stream);
+
 /* Number of kernel launches this library has issued on the current thread
  * since the last call (launch accounting for benchmarks); resets to 0. */
 long long bonsai_launch_count(void);
@@ -273,11 +284,41 @@ int bonsai_dit_begin(bonsai_dit_t m, const float* img, const float* txt, const f
 int bonsai_dit_phase(bonsai_dit_t m, int kind, int block, int phase, void* stream);
 int bonsai_dit_end(bonsai_dit_t m, float* out, void* stream);
 
-/* Export the seeded host weights of the model (packed B1_0 bytes and f32
- * tensors) by name, for the CPU oracle: returns the byte size when buf is
- * NULL.  Names follow the reference's safetensors keys
- * (src/diffuser.cpp:107-183). */
+/* Export one weight of the model as it is on the device, by the engine's
+ * name ("double.<i>.img_qkv", "single.<i>.proj", "mod_img.w", "img_in.w",
+ * ...): packed B1_0 bytes [out][in/32][6] (the layout of
+ * convert_to_b1_0_packed.py:21-43) or f32 values [out][in].  Returns the byte
+ * size when buf is NULL.  Synchronises the device.  Used by the CPU oracle
+ * to run on identical weights. */
 long long bonsai_dit_weight(bonsai_dit_t m, const char* name, void* buf, long long cap);
+
+/* Replace one weight from host bytes in the layout bonsai_dit_weight
+ * exports (B1_0 weights are retiled on the device).  bytes must match the
+ * tensor.  Synchronises the device; no forward of this model may be running.
+ * The per-tensor form of load_b1 / load_f32_2d (src/diffuser.cpp:27-50). */
+int bonsai_dit_set_weight(bonsai_dit_t m, const char* name, const void* host, long long bytes);
+
+/* Load a packed checkpoint in the reference's safetensors layout: the
+ * tensor names, dtypes and shapes that src/diffuser.cpp:88-186 reads
+ * (x_embedder.weight, transformer_blocks.<d>.attn.to_q.weight, ...;
+ * B1_0 tensors U8 [out][in/32*6], the rest F32 [out][in]).  Q/K/V are
+ * stacked into the engine's fused weights; blocks beyond the model's depth
+ * are ignored (the reference's --max-depth / --max-single).  klein4b preset
+ * only (BONSAI_ERR_UNSUPPORTED otherwise).  Missing tensors or wrong shapes
+ * return BONSAI_ERR_ARG instead of the reference's abort()
+ * (src/diffuser.cpp:52-56); tensors are set in order, so after an error the
+ * model may hold a mix of old and new weights. */
+int bonsai_dit_load_safetensors(bonsai_dit_t m, const char* path);
+
+/* The reference's whole diffusion loop (src/diffuser.cpp:251-294) on the
+ * device: for step s < n_steps, t = 1 - s/n_steps, pred = forward(latents,
+ * t*1000), latents += dt*pred with dt = t - t_next (the last step: dt = t).
+ * latents: device f32 [img_tokens][in_ch], updated in place.  stats (host,
+ * optional): 5 floats per step = the reference's per-step printout {NaN
+ * count, Inf count, min, max, mean} of pred (:276-288); when given, the call
+ * synchronises the stream. */
+int bonsai_dit_sample(bonsai_dit_t m, float* latents, const float* txt, const float* pooled,
+                      int n_steps, float* stats, void* stream);
 
 #ifdef __cplusplus
 }

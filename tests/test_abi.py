@@ -40,3 +40,8 @@ def test_no_gpu_error_paths():
     assert rc == -1 and b"multiple of 32" in L.bonsai_last_error()
     assert L.bonsai_b1_gemm(None, 64, 4, None, 0, None, 32, None, None) == -1
     assert L.bonsai_joint_attention(None, None, None, 24, 128, 64, 0.1, None, 3072, None) == -2
+    assert L.bonsai_dit_set_weight(None, b"img_in.w", None, 0) == -1
+    assert L.bonsai_dit_load_safetensors(None, b"/nonexistent.safetensors") == -1
+    assert L.bonsai_dit_sample(None, None, None, None, 4, None, None) == -1
+    assert L.bonsai_count_nonfinite(None, 5, None, None) == -1
+    assert b"count_nonfinite" in L.bonsai_last_error()
