@@ -152,6 +152,10 @@ struct bonsai_dit {
   // by the caller's buffer pointers; captured on a private stream, replayed
   // on the caller's stream.
   cudaStream_t cap_stream = nullptr;
+  // The double blocks run their text-stream chain on `aux`, forked from and
+  // joined back into the caller's stream inside each phase.
+  cudaStream_t aux = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   cudaGraphExec_t graph = nullptr;
   const void* graph_key[4] = {nullptr, nullptr, nullptr, nullptr};
   long long graph_kernels = 0;
@@ -326,6 +330,23 @@ TileSel head_tiles(const bonsai_dit* m) {
 //          joint attention of those heads -> cat[:, heads]           (:354-416)
 // phase 2: out-projection + gate-residual, LN-modulate, MLP + gate-residual
 //          on this rank's rows (needs cat[own rows, all heads])      (:434-460)
+// The stream of the double blocks' text-stream chain: m->aux, or st itself
+// while per-launch profiling is on (concurrent kernels would stretch each
+// other's event-timed durations).
+cudaStream_t txt_stream(bonsai_dit* m, cudaStream_t st) { return profiling_active() ? st : m->aux; }
+// The text stream starts after everything issued so far on st ...
+int fork_aux(bonsai_dit* m, cudaStream_t st) {
+  if (txt_stream(m, st) == st) return 0;
+  RC(cuda_status(cudaEventRecord(m->ev_fork, st), "fork record"));
+  return cuda_status(cudaStreamWaitEvent(m->aux, m->ev_fork, 0), "fork wait");
+}
+// ... and st continues only after everything issued on it.
+int join_aux(bonsai_dit* m, cudaStream_t st) {
+  if (txt_stream(m, st) == st) return 0;
+  RC(cuda_status(cudaEventRecord(m->ev_join, m->aux), "join record"));
+  return cuda_status(cudaStreamWaitEvent(st, m->ev_join, 0), "join wait");
+}
+
 int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
   const Cfg& c = m->c;
   const DoubleW& w = m->dbl[i];
@@ -333,20 +354,28 @@ int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
   const float *mi, *mt;
   double_mods(m, i, &mi, &mt);
   const Span tx = own_txt(m), im = own_img(m);
+  const cudaStream_t ts = txt_stream(m, st);
+  // The text and image streams touch disjoint rows of hidden / xm / cat and
+  // disjoint tokens of qkv until the joint attention: the text chain runs on
+  // its own stream, concurrently with the image chain, and is joined back
+  // into st before anything that reads both (and at the end of every phase).
   if (phase == 0) {
+    RC(fork_aux(m, st));
     RC(launch_ln_modulate_f16(m->hidden + (size_t)tx.a * H, tx.n(), H, mt + 0 * H, mt + 1 * H,
-                              1e-6f, m->xm + (size_t)tx.a * H, H, st));
+                              1e-6f, m->xm + (size_t)tx.a * H, H, ts));
     RC(launch_ln_modulate_f16(m->hidden + (size_t)im.a * H, im.n(), H, mi + 0 * H, mi + 1 * H,
                               1e-6f, m->xm + (size_t)im.a * H, H, st));
-    return 0;
+    return join_aux(m, st);
   }
   if (phase == 1) {
     const TileSel sel = head_tiles(m);
     const TileSel* ps = m->world > 1 ? &sel : nullptr;
+    RC(fork_aux(m, st));
     EpiSeg s = seg_qkv(c, 3 * H, m->qkv, 0);
-    RC(launch_b1_gemm(m->xm, H, Lt, w.txt_qkv, &s, 1, false, st, ps));
+    RC(launch_b1_gemm(m->xm, H, Lt, w.txt_qkv, &s, 1, false, ts, ps));
     s = seg_qkv(c, 3 * H, m->qkv, Lt);
     RC(launch_b1_gemm(m->xm + (size_t)Lt * H, H, c.img, w.img_qkv, &s, 1, false, st, ps));
+    RC(join_aux(m, st));
     const size_t hs = (size_t)c.L * c.hd;  // one head of one of q/k/v
     __half* q = m->qkv + (size_t)m->h0 * hs;
     __half* k = m->qkv + (size_t)(c.heads + m->h0) * hs;
@@ -358,11 +387,13 @@ int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
     return launch_attention(q, k, v, m->hl, c.L, c.hd, 1.0f / sqrtf((float)c.hd),
                             m->cat + (size_t)m->h0 * c.hd, C, st);
   }
-  // phase 2, per stream on this rank's rows
+  // phase 2, per stream on this rank's rows (text on its own stream)
   const int act_mode = c.swiglu ? EPI_SWIGLU_F16 : EPI_GELU_F16;
+  RC(fork_aux(m, st));
   for (int sidx = 0; sidx < 2; ++sidx) {
     const Span sp = sidx == 0 ? tx : im;
     if (sp.n() == 0) continue;
+    const cudaStream_t ss = sidx == 0 ? ts : st;
     const float* md = sidx == 0 ? mt : mi;
     const B1Weight& w_out = sidx == 0 ? w.txt_out : w.img_out;
     const B1Weight& w_in = sidx == 0 ? w.txt_mlp_in : w.img_mlp_in;
@@ -371,14 +402,14 @@ int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
     __half* x = m->xm + (size_t)sp.a * H;
     __half* a = m->cat + (size_t)sp.a * C;
     EpiSeg s = seg_of(EPI_RESID_F32, 0, H, h, H, 0, md + 2 * H);
-    RC(launch_b1_gemm(a, C, sp.n(), w_out, &s, 1, false, st));
-    RC(launch_ln_modulate_f16(h, sp.n(), H, md + 3 * H, md + 4 * H, 1e-6f, x, H, st));
+    RC(launch_b1_gemm(a, C, sp.n(), w_out, &s, 1, false, ss));
+    RC(launch_ln_modulate_f16(h, sp.n(), H, md + 3 * H, md + 4 * H, 1e-6f, x, H, ss));
     s = seg_of(act_mode, 0, c.mlp_in_rows, a, C, H, nullptr);
-    RC(launch_b1_gemm(x, H, sp.n(), w_in, &s, 1, false, st));
+    RC(launch_b1_gemm(x, H, sp.n(), w_in, &s, 1, false, ss));
     s = seg_of(EPI_RESID_F32, 0, H, h, H, 0, md + 5 * H);
-    RC(launch_b1_gemm(a + H, C, sp.n(), w_o2, &s, 1, false, st));
+    RC(launch_b1_gemm(a + H, C, sp.n(), w_o2, &s, 1, false, ss));
   }
-  return 0;
+  return join_aux(m, st);
 }
 
 // The three phases of a single block (src/diffuser_graph.cpp:476-542).
@@ -615,6 +646,9 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->in_pooled), (size_t)std::max(c.pooled, 1) * 4));
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->out_buf), (size_t)c.img * c.in_ch * 4));
   RC(cuda_status(cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking), "capture stream"));
+  RC(cuda_status(cudaStreamCreateWithFlags(&m->aux, cudaStreamNonBlocking), "aux stream"));
+  RC(cuda_status(cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming), "fork event"));
+  RC(cuda_status(cudaEventCreateWithFlags(&m->ev_join, cudaEventDisableTiming), "join event"));
   cudaMemset(m->vec_silu16, 0, (size_t)8 * H * 2);
 
   // RoPE ids (src/diffuser.cpp:240-249): text rows 0, image rows (.., y, x)
@@ -653,6 +687,9 @@ int bonsai_dit_destroy(bonsai_dit_t m) {
   cudaDeviceSynchronize();
   if (m->graph) cudaGraphExecDestroy(m->graph);
   if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
+  if (m->aux) cudaStreamDestroy(m->aux);
+  if (m->ev_fork) cudaEventDestroy(m->ev_fork);
+  if (m->ev_join) cudaEventDestroy(m->ev_join);
   for (void* p : m->allocs) cudaFree(p);
   delete m;
   return 0;
