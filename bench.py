@@ -473,6 +473,139 @@ def run_bonsai(args):
     return 0
 
 
+def _cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_configs(args):
+    """--configs: BASELINE configs 1-3 timed on the GPU and with the
+    reference CPU path on all host cores, one JSON line each.
+
+    C1 one Flux double block, 256 text + 1024 image tokens (32x32 grid);
+    C2 joint attention only, 24 heads x 128, L = 4352;
+    C3 the 18-shape B1_0 GEMM sweep (M in 1280/4352/8704 x six (K, N)).
+    CPU: the reference's own b1_linear_f32_f32 (AVX2, oracle/_ref) for
+    every B1_0 linear, the vectorised CPU restatement of the ggml built-ins
+    for the rest (flash attention with f16 K/V, norms, RoPE).  GPU: the C ABI
+    (CUDA events, mean of `steps` calls after `warmup`).  Speedups are
+    GPU vs CPU on the same seeded inputs; not a parity check (the tests are).
+    """
+    import ctypes
+    import torch
+    import bonsai_b200 as bb
+    from oracle import pyoracle as O
+    torch.cuda.init()
+    bb.init(0)
+    threads = os.cpu_count() or 1
+    info = {"cpu_threads": threads, "cpu_model": _cpu_model(), "device": torch.cuda.get_device_name(0)}
+    R = O.ref()
+    if R is None:
+        print(json.dumps({"configs": "unavailable", "why": "oracle/_ref (the reference's b1 kernel) is not built"}))
+        return 0
+    fast = ctypes.CDLL(str(ROOT / "oracle/_build/libbonsai_oracle_fast.so"))
+    vp, ci, cf = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    fast.orc_set_threads.argtypes = [ci]
+    fast.orc_set_threads(threads)
+    fast.orc_use_reference_b1.argtypes = [vp, ci]
+    fast.orc_set_attention_f16.argtypes = [ci]
+    fast.orc_attention.argtypes = [vp, vp, vp, ci, ci, ci, cf, vp]
+    fast.orc_double_block.argtypes = [ctypes.POINTER(O.Dims), ci, ci, vp] + [vp] * 16
+    K_steps, W = args.steps, args.warmup
+
+    def gpu_time(fn):
+        for _ in range(W):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K_steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / K_steps
+
+    def emit(name, flop, gms, cms, extra=None):
+        d = {"config": name, "gpu_ms": round(gms, 4), "cpu_ms": round(cms, 1),
+             "speedup": round(cms / gms, 1), "gpu_tflops": round(flop / gms / 1e9, 1),
+             "cpu_gflops": round(flop / cms / 1e6, 1), **info}
+        if extra:
+            d.update(extra)
+        print(json.dumps(d), flush=True)
+
+    rng = np.random.default_rng(1234)
+    # ---- C1: one double block
+    m = bb.Dit(bb.PRESET_FLUX1, 1024, 256, 32, 32, depth=1, depth_single=1, seed=1234)
+    hidden = rng.standard_normal((m.L, H)).astype(np.float32)
+    vec = rng.standard_normal(H).astype(np.float32)
+    hd, vd = torch.from_numpy(hidden).cuda(), torch.from_numpy(vec).cuda()
+    m.set_state(hd, vd)
+    gms = gpu_time(lambda: m.double_block(0))
+    mods, _ = O.modulations(m, vec)
+    cos_t, sin_t = O.rope_cos_sin(m.rope_ids(), m.axes, m.theta)
+    p = "double.0."
+    w = {n: m.weight(p + n) for n in ("img_qkv", "txt_qkv", "img_out", "txt_out", "img_mlp_in",
+                                      "img_mlp_out", "txt_mlp_in", "txt_mlp_out")}
+    nrm = {n: m.weight_f32(p + n) for n in ("img_norm_q", "img_norm_k", "txt_norm_q", "txt_norm_k")}
+    D = O.dims(m.swiglu, m.mlp)
+    fast.orc_use_reference_b1(ctypes.cast(R.ref_b1_linear, vp), threads)
+    fast.orc_set_attention_f16(1)
+    h = hidden.copy()
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    mi, mt, ct, st = f(mods["double"][0][0]), f(mods["double"][0][1]), f(cos_t), f(sin_t)
+    with stdout_to_stderr():
+        t0 = time.perf_counter()
+        fast.orc_double_block(ctypes.byref(D), m.txt, m.img, O.P(h), O.P(mi), O.P(mt),
+                              O.P(w["img_qkv"]), O.P(w["txt_qkv"]), O.P(w["img_out"]), O.P(w["txt_out"]),
+                              O.P(w["img_mlp_in"]), O.P(w["img_mlp_out"]), O.P(w["txt_mlp_in"]),
+                              O.P(w["txt_mlp_out"]), O.P(nrm["img_norm_q"]), O.P(nrm["img_norm_k"]),
+                              O.P(nrm["txt_norm_q"]), O.P(nrm["txt_norm_k"]), O.P(ct), O.P(st))
+        cms = 1000 * (time.perf_counter() - t0)
+    fast.orc_use_reference_b1(None, 1)
+    L1 = m.L
+    flop = 2.0 * L1 * H * (3 * H + H + MLP + MLP) + 4.0 * L1 * L1 * HD * HEADS
+    emit("C1 double block, 256 txt + 1024 img tokens (flux1 dims)", flop, gms, cms)
+    m.close()
+
+    # ---- C2: attention, L = 4352
+    L2 = 4352
+    q, k, v = (torch.randn(HEADS, L2, HD, device="cuda").half() for _ in range(3))
+    out = torch.empty(L2, HEADS * HD, device="cuda", dtype=torch.float16)
+    gms = gpu_time(lambda: bb.joint_attention(q, k, v, out))
+    qc, kc, vc = (np.ascontiguousarray(t.float().permute(1, 0, 2).cpu().numpy()) for t in (q, k, v))
+    oc = np.zeros((L2, HEADS, HD), np.float32)
+    with stdout_to_stderr():
+        t0 = time.perf_counter()
+        fast.orc_attention(qc.ctypes.data, kc.ctypes.data, vc.ctypes.data, L2, HEADS, HD,
+                           float(HD ** -0.5), oc.ctypes.data)
+        cms = 1000 * (time.perf_counter() - t0)
+    emit("C2 joint attention, 24 heads x 128, L = 4352", 4.0 * L2 * L2 * HD * HEADS, gms, cms)
+
+    # ---- C3: GEMM sweep
+    for (Kd, N) in [(3072, 9216), (3072, 3072), (3072, 12288), (12288, 3072), (3072, 21504), (15360, 3072)]:
+        packed = bb.random_b1_packed(N, Kd, rng)
+        wgt = bb.B1Weight(packed, N, Kd)
+        for M in (1280, 4352, 8704):
+            x = torch.randn(M, Kd, device="cuda")
+            x16 = x.half()
+            o16 = torch.empty(M, N, device="cuda", dtype=torch.float16)
+            gms = gpu_time(lambda: bb.b1_gemm(x16, wgt, bb.BONSAI_EPI_F16, o16))
+            xc = np.ascontiguousarray(x.cpu().numpy())
+            oc = np.zeros((M, N), np.float32)
+            with stdout_to_stderr():
+                t0 = time.perf_counter()
+                R.ref_b1_linear(xc.ctypes.data, M, Kd, packed.ctypes.data, N, oc.ctypes.data, threads)
+                cms = 1000 * (time.perf_counter() - t0)
+            emit(f"C3 GEMM M={M} K={Kd} N={N}", 2.0 * M * N * Kd, gms, cms)
+        wgt.free()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -483,9 +616,14 @@ def main():
     ap.add_argument("--workload", choices=["1024", "2048"], default="1024",
                     help="1024: config 4, one image per GPU (data parallel, default); "
                          "2048: config 5(b), one 2048^2 image split by heads/rows across the GPUs")
+    ap.add_argument("--configs", action="store_true",
+                    help="instead of the step: BASELINE configs 1-3, GPU vs the reference CPU "
+                         "path, one JSON line per config")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.configs:
+        return run_configs(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_bonsai(args)

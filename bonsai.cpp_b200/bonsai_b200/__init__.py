@@ -56,6 +56,7 @@ SIGNATURES = {
     "bonsai_rope_2d_f32": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp]),
     "bonsai_rope_tables": (_c_int, [_vp, _c_int, _c_int, _vp, _fp, _vp, _vp, _vp]),
     "bonsai_rms_norm_f32": (_c_int, [_vp, _vp, _c_int, _c_int, _fp, _vp, _vp]),
+    "bonsai_linear_f32": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _c_int, _vp, _vp]),
     "bonsai_ln_modulate": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _fp, _vp, _c_ll, _vp]),
     "bonsai_ln_modulate_f32": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _fp, _vp, _vp]),
     "bonsai_joint_attention": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _fp, _vp, _c_ll, _vp]),
@@ -184,6 +185,16 @@ def b1_gemm(x16, w: B1Weight, mode: int, out, gate=None, stream=None) -> None:
                                out.data_ptr(), out.stride(0),
                                gate.data_ptr() if gate is not None else None,
                                stream_ptr(stream)), "bonsai_b1_gemm")
+
+
+def linear_f32(x, W, bias, out, stream=None) -> None:
+    """f32 edge linear: out[t][o] = x[t] . W[o] (+ bias[o]); device tensors."""
+    T, K = x.shape
+    N = W.shape[0]
+    assert x.is_contiguous() and W.is_contiguous() and out.is_contiguous()
+    check(lib().bonsai_linear_f32(x.data_ptr(), T, K, W.data_ptr(),
+                                  bias.data_ptr() if bias is not None else None, N,
+                                  out.data_ptr(), stream_ptr(stream)), "bonsai_linear_f32")
 
 
 def count_nonfinite(x, stream=None) -> int:

@@ -85,6 +85,24 @@ int bonsai_rope_tables(const float* ids, int seq, int n_axes, const int* host_ax
   return rc;
 }
 
+int bonsai_linear_f32(const float* x, int tokens, int in_dim, const float* W, const float* bias,
+                      int out_dim, float* y, void* stream) {
+  if (tokens < 0 || in_dim <= 0 || out_dim < 0) return fail(BONSAI_ERR_ARG, "linear_f32: bad shape");
+  if (tokens == 0 || out_dim == 0) return 0;
+  if (!x || !W || !y) return fail(BONSAI_ERR_ARG, "linear_f32: null tensor");
+  cudaStream_t st = S(stream);
+  // Up to 8 partial sums of the output (the split-K limit of the kernel).
+  const long long ws_elems = 8LL * tokens * out_dim;
+  float* ws = nullptr;
+  int rc = cuda_status(cudaMallocAsync(reinterpret_cast<void**>(&ws), (size_t)ws_elems * 4, st),
+                       "linear_f32: workspace");
+  if (rc) return rc;
+  rc = launch_linear_f32(x, in_dim, tokens, in_dim, W, bias, out_dim, y, out_dim, false, st, ws,
+                         ws_elems);
+  cudaFreeAsync(ws, st);
+  return rc;
+}
+
 int bonsai_rms_norm_f32(const float* x, const float* w, int rows, int head_dim, float eps,
                         float* out, void* stream) {
   if (rows == 0) return 0;

@@ -740,8 +740,10 @@ static int dit_forward_body(bonsai_dit* m, const float* img, const float* txt, c
   // output head (:544-556): norm_out modulation is (scale, shift)
   const float* h_img = m->hidden + (size_t)c.txt * c.H;
   RC(launch_ln_modulate_f32(h_img, c.img, c.H, m->fin + c.H, m->fin, 1e-6f, m->tmp32, c.H, st));
+  // cat (free by now) holds the split-K partial sums of the narrow projection
   return launch_linear_f32(m->tmp32, c.H, c.img, c.H, m->proj_out_w, m->proj_out_b, c.in_ch, out,
-                           c.in_ch, false, st);
+                           c.in_ch, false, st, reinterpret_cast<float*>(m->cat),
+                           (long long)c.L * c.C() / 2);
 }
 
 int bonsai_dit_forward(bonsai_dit_t m, const float* img, const float* txt, const float* pooled,
@@ -913,8 +915,10 @@ int bonsai_dit_end(bonsai_dit_t m, float* out, void* stream) {
   // output head (:544-556) on every image row (the caller has gathered them)
   const float* h_img = m->hidden + (size_t)c.txt * c.H;
   RC(launch_ln_modulate_f32(h_img, c.img, c.H, m->fin + c.H, m->fin, 1e-6f, m->tmp32, c.H, st));
+  // cat (free by now) holds the split-K partial sums of the narrow projection
   return launch_linear_f32(m->tmp32, c.H, c.img, c.H, m->proj_out_w, m->proj_out_b, c.in_ch, out,
-                           c.in_ch, false, st);
+                           c.in_ch, false, st, reinterpret_cast<float*>(m->cat),
+                           (long long)c.L * c.C() / 2);
 }
 
 long long bonsai_dit_weight(bonsai_dit_t m, const char* name, void* buf, long long cap) {

@@ -113,24 +113,38 @@ __global__ void __launch_bounds__(256) linear128_kernel(const float* __restrict_
   const int t0 = blockIdx.y * LB, o0 = blockIdx.x * LB;
   // loader mapping: thread -> (row = tid / 2, k4 = (tid % 2) * 4)
   const int lr = tid >> 1, lk = (tid & 1) * 4;
-  auto load = [&](int buf, int k0) {
+  const int Kfull = K;  // row stride of W
+  const int kb = blockIdx.z * kspan;
+  K = min(K, kb + kspan);  // this block's slice is [kb, K)
+  y += blockIdx.z * zstride;
+  // The next k-tile is fetched into registers before the current one is
+  // multiplied and stored to shared memory after it, so the global-load
+  // latency overlaps the FMAs.
+  float rx[4], rw[4];
+  auto fetch = [&](int k0) {
     const int t = t0 + lr, o = o0 + lr;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int kk = k0 + lk + u;
-      xs[buf][lk + u][lr] = (t < T && kk < K) ? x[(size_t)t * ldx + kk] : 0.f;
-      ws[buf][lk + u][lr] = (o < N && kk < K) ? W[(size_t)o * K + kk] : 0.f;
+      rx[u] = (t < T && kk < K) ? x[(size_t)t * ldx + kk] : 0.f;
+      rw[u] = (o < N && kk < K) ? W[(size_t)o * Kfull + kk] : 0.f;
     }
   };
-  const int kb = blockIdx.z * kspan;
-  K = min(K, kb + kspan);  // this block's slice is [kb, K)
-  y += blockIdx.z * zstride;
+  auto stash = [&](int buf) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      xs[buf][lk + u][lr] = rx[u];
+      ws[buf][lk + u][lr] = rw[u];
+    }
+  };
   float acc[8][8] = {};
-  load(0, kb);
+  fetch(kb);
+  stash(0);
   __syncthreads();
   int buf = 0;
   for (int k0 = kb; k0 < K; k0 += LK) {
-    if (k0 + LK < K) load(buf ^ 1, k0 + LK);
+    const bool more = k0 + LK < K;
+    if (more) fetch(k0 + LK);
 #pragma unroll
     for (int c = 0; c < LK; ++c) {
       const float4 a0 = *reinterpret_cast<const float4*>(&xs[buf][c][ty * 8]);
@@ -144,6 +158,7 @@ __global__ void __launch_bounds__(256) linear128_kernel(const float* __restrict_
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
+    if (more) stash(buf ^ 1);
     __syncthreads();
     buf ^= 1;
   }
@@ -265,7 +280,9 @@ int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* 
   }
   if (silu_in) return fail(-2, "linear_f32: silu input only supported for T == 1");
   ProfScope prof("linear_f32", 2.0 * T * N * (double)K, 4.0 * ((double)T * K + (double)N * K + (double)T * N), st);
-  if ((long long)T * N >= 64LL * 128 * 128) {
+  // 128x128 tiles for large outputs, and for small ones whenever a split-K
+  // workspace lets the grid grow (e.g. the 64-wide output projection).
+  if ((long long)T * N >= 64LL * 128 * 128 || workspace) {
     dim3 grid((N + edge::LB - 1) / edge::LB, (T + edge::LB - 1) / edge::LB);
     // Split K so that the grid covers the GPU twice, when a workspace for the
     // partial sums is available (deterministic reduction afterwards).

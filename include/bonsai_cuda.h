@@ -169,6 +169,16 @@ int bonsai_rope_2d_f32(const float* x, const float* cos_t, const float* sin_t, i
 int bonsai_rope_tables(const float* ids, int seq, int n_axes, const int* host_axes_dim,
                        float theta, float* cos_out, float* sin_out, void* stream);
 
+/* f32 linear y[t][o] = sum_k x[t][k] * W[o][k] (+ bias[o]), the ggml_mul_mat
+ * of the reference's f32 edge projections (x_embedder / context_embedder /
+ * proj_out, src/diffuser_graph.cpp:283-286, :544-556) in f32 arithmetic.
+ * x: f32 [tokens][in_dim]; W: f32 [out_dim][in_dim] (PyTorch layout);
+ * bias: f32 [out_dim] or NULL; y: f32 [tokens][out_dim].  Narrow or short
+ * problems split the K sum (partials in a stream-ordered allocation,
+ * reduced in a fixed order: deterministic). */
+int bonsai_linear_f32(const float* x, int tokens, int in_dim, const float* W, const float* bias,
+                      int out_dim, float* y, void* stream);
+
 /* Q/K RMSNorm of rms_norm_qk (src/diffuser_graph.cpp:71-79): for each row
  * of head_dim values, y = x / sqrt(mean(x^2) + eps) * w.
  * x, out: f32 [rows][head_dim]; w: f32 [head_dim]. */

@@ -112,3 +112,26 @@ def test_forward_depth2(gpu, preset):
     m.forward_host(img, txt, pooled, t, host_out)
     np.testing.assert_array_equal(host_out, got)
     m.close()
+
+
+def test_forward_long_text_split_k_edges(gpu):
+    """384 text tokens: the context embedder (384 x 4096 -> 3072) and the
+    output projection take the split-K path of the f32 edge linear inside the
+    engine; the whole step must still match the oracle."""
+    import torch
+    m = _model(bb.PRESET_FLUX1, 384, 4, 4, depth=1, single=1, seed=23)
+    rng = np.random.default_rng(6)
+    img = rng.standard_normal((m.img, m.in_ch)).astype(np.float32)
+    txt = rng.standard_normal((m.txt, m.ctx_dim)).astype(np.float32)
+    pooled = rng.standard_normal(m.pooled).astype(np.float32)
+    out = torch.empty(m.img, m.in_ch, device="cuda")
+    m.forward(torch.from_numpy(img).cuda(), torch.from_numpy(txt).cuda(),
+              torch.from_numpy(pooled).cuda(), 600.0, out)
+    got = out.cpu().numpy()
+    O.use_reference_b1(True, nthreads=16)
+    try:
+        ref = O.dit_forward(m, img, txt, pooled, 600.0)
+    finally:
+        O.use_reference_b1(False)
+    _check(got, ref, "forward with 384 text tokens")
+    m.close()

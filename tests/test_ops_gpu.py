@@ -171,3 +171,27 @@ def test_rms_norm_vs_oracle(gpu):
                                           bb.stream_ptr()))
     torch.cuda.synchronize()
     np.testing.assert_allclose(y.cpu().numpy(), O.rms_norm(x, w), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("T,K,N", [
+    (512, 4096, 3072),   # context_embedder at 1024^2: split-K over 4 slices
+    (4096, 3072, 64),    # proj_out (flux1): narrow output, split-K over 8 slices
+    (4096, 64, 3072),    # x_embedder (flux1): K = 64, no split
+    (7, 40, 33),         # ragged, K % 8 != 0
+    (300, 1000, 130),    # ragged split-K slices
+    (1, 3072, 1000),     # one token (GEMV path)
+])
+def test_linear_f32_edges(gpu, T, K, N):
+    """The f32 edge projections (ggml_mul_mat f32, src/diffuser_graph.cpp:283-286,
+    :544-556) against float64 numpy, including every split-K slice."""
+    import torch
+    rng = np.random.default_rng(T * 7 + K + N)
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    W = (0.05 * rng.standard_normal((N, K))).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    out = torch.empty(T, N, device="cuda")
+    bb.linear_f32(torch.from_numpy(x).cuda(), torch.from_numpy(W).cuda(), torch.from_numpy(b).cuda(), out)
+    ref = x.astype(np.float64) @ W.astype(np.float64).T + b
+    got = out.cpu().numpy()
+    err = np.max(np.abs(got - ref)) / (np.sqrt(np.mean(ref ** 2)) + 1e-30)
+    assert err <= 2e-6 * np.sqrt(K), (T, K, N, err)
