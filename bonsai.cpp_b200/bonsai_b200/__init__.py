@@ -72,6 +72,7 @@ SIGNATURES = {
     "bonsai_dit_weight": (_c_ll, [_vp, ctypes.c_char_p, _vp, _c_ll]),
     "bonsai_dit_set_weight": (_c_int, [_vp, ctypes.c_char_p, _vp, _c_ll]),
     "bonsai_dit_load_safetensors": (_c_int, [_vp, ctypes.c_char_p]),
+    "bonsai_safetensors_list": (_c_int, [ctypes.c_char_p, ctypes.c_char_p, _c_int]),
     "bonsai_dit_sample": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _vp, _vp]),
     "bonsai_dit_set_partition": (_c_int, [_vp, _c_int, _c_int]),
     "bonsai_dit_buffer": (_c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(_c_ll)]),
@@ -203,6 +204,21 @@ def count_nonfinite(x, stream=None) -> int:
     check(lib().bonsai_count_nonfinite(x.data_ptr(), x.numel(), ctypes.byref(n), stream_ptr(stream)),
           "bonsai_count_nonfinite")
     return int(n.value)
+
+
+def safetensors_list(path) -> list:
+    """[(name, dtype, shape tuple, begin, end)] of a .safetensors file (host only)."""
+    p = str(path).encode()
+    n = lib().bonsai_safetensors_list(p, None, 0)
+    if n < 0:
+        check(n, "bonsai_safetensors_list")
+    buf = ctypes.create_string_buffer(n + 1)
+    check(0 if lib().bonsai_safetensors_list(p, buf, n + 1) == n else -1, "bonsai_safetensors_list")
+    out = []
+    for line in buf.value.decode().splitlines():
+        name, dtype, shape, b, e = line.split("\t")
+        out.append((name, dtype, tuple(int(d) for d in shape.split(",") if d), int(b), int(e)))
+    return out
 
 
 def shutdown() -> None:

@@ -209,3 +209,22 @@ int st_read(StFile& f, const StTensor& t, void* dst, long long bytes) {
 }
 
 }  // namespace bonsai
+
+extern "C" int bonsai_safetensors_list(const char* path, char* out, int cap) {
+  bonsai::StFile f;
+  const int rc = bonsai::st_open(path, f);
+  if (rc) return rc;
+  std::string txt;
+  for (const auto& kv : f.tensors) {
+    txt += kv.first + "\t" + kv.second.dtype + "\t";
+    for (size_t i = 0; i < kv.second.shape.size(); ++i)
+      txt += (i ? "," : "") + std::to_string(kv.second.shape[i]);
+    txt += "\t" + std::to_string(kv.second.begin) + "\t" + std::to_string(kv.second.end) + "\n";
+  }
+  if (out && cap > 0) {
+    const size_t n = std::min<size_t>(txt.size(), (size_t)cap - 1);
+    memcpy(out, txt.data(), n);
+    out[n] = 0;
+  }
+  return (int)std::min<size_t>(txt.size(), 0x7fffffff);
+}

@@ -320,6 +320,14 @@ int bonsai_dit_set_weight(bonsai_dit_t m, const char* name, const void* host, lo
  * model may hold a mix of old and new weights. */
 int bonsai_dit_load_safetensors(bonsai_dit_t m, const char* path);
 
+/* The tensor index of a .safetensors file (src/safetensors.h reads the
+ * same container): one line per tensor, sorted by name,
+ * "name<TAB>dtype<TAB>d0,d1,...<TAB>begin<TAB>end\n" (data offsets relative to
+ * the end of the header).  Host only, no device work.  Returns the full text
+ * length (out may be NULL to size it; at most cap-1 bytes are written) or a
+ * negative BONSAI_ERR_* code for an unreadable or malformed file. */
+int bonsai_safetensors_list(const char* path, char* out, int cap);
+
 /* The reference's whole diffusion loop (src/diffuser.cpp:251-294) on the
  * device: for step s < n_steps, t = 1 - s/n_steps, pred = forward(latents,
  * t*1000), latents += dt*pred with dt = t - t_next (the last step: dt = t).

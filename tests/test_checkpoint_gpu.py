@@ -12,13 +12,13 @@ reference's sampling loop run on the device.
 * bonsai_dit_sample equals the reference's loop (src/diffuser.cpp:251-294)
   driven from the host: forward, then lat += dt * pred in f32.
 """
-import json
 import struct
 
 import numpy as np
 import pytest
 
 import bonsai_b200 as bb
+from st_writer import write_safetensors
 
 pytestmark = pytest.mark.gpu
 
@@ -28,24 +28,6 @@ TXT = 32
 
 def _klein(seed, depth=1, single=1):
     return bb.Dit(bb.PRESET_KLEIN4B, GH * GW, TXT, GH, GW, depth=depth, depth_single=single, seed=seed)
-
-
-def write_safetensors(path, tensors):
-    """Minimal safetensors writer: 8-byte LE header length, JSON header, data."""
-    header, blobs, off = {"__metadata__": {"format": "pt"}}, [], 0
-    for name, arr in tensors.items():
-        arr = np.ascontiguousarray(arr)
-        dtype = {np.dtype(np.uint8): "U8", np.dtype(np.float32): "F32"}[arr.dtype]
-        header[name] = {"dtype": dtype, "shape": list(arr.shape), "data_offsets": [off, off + arr.nbytes]}
-        blobs.append(arr.tobytes())
-        off += arr.nbytes
-    h = json.dumps(header).encode()
-    h += b" " * (-len(h) % 8)
-    with open(path, "wb") as f:
-        f.write(struct.pack("<Q", len(h)))
-        f.write(h)
-        for b in blobs:
-            f.write(b)
 
 
 def reference_checkpoint(m):
