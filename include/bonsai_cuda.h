@@ -313,7 +313,8 @@ int bonsai_dit_set_weight(bonsai_dit_t m, const char* name, const void* host, lo
  * (x_embedder.weight, transformer_blocks.<d>.attn.to_q.weight, ...;
  * B1_0 tensors U8 [out][in/32*6], the rest F32 [out][in]).  Q/K/V are
  * stacked into the engine's fused weights; blocks beyond the model's depth
- * are ignored (the reference's --max-depth / --max-single).  klein4b preset
+ * are ignored (the reference's --max-depth / --max-single).  The same
+ * tensors in a GGUF file (convert_to_b1_0.py) load too.  klein4b preset
  * only (BONSAI_ERR_UNSUPPORTED otherwise).  Missing tensors or wrong shapes
  * return BONSAI_ERR_ARG instead of the reference's abort()
  * (src/diffuser.cpp:52-56); tensors are set in order, so after an error the
@@ -321,7 +322,9 @@ int bonsai_dit_set_weight(bonsai_dit_t m, const char* name, const void* host, lo
 int bonsai_dit_load_safetensors(bonsai_dit_t m, const char* path);
 
 /* The tensor index of a .safetensors file (src/safetensors.h reads the
- * same container): one line per tensor, sorted by name,
+ * same container) or of a GGUF file (recognised by its magic; B1_0 is tensor
+ * type 100 as convert_to_b1_0.py writes it, listed as U8 [out][in/32*6]
+ * under the reference's safetensors names): one line per tensor, sorted by name,
  * "name<TAB>dtype<TAB>d0,d1,...<TAB>begin<TAB>end\n" (data offsets relative to
  * the end of the header).  Host only, no device work.  Returns the full text
  * length (out may be NULL to size it; at most cap-1 bytes are written) or a

@@ -224,3 +224,28 @@ def test_count_nonfinite(gpu):
     x[12] = float("-inf")
     assert bb.count_nonfinite(x) == 6
     assert bb.count_nonfinite(x[:0]) == 0
+
+
+def test_load_gguf_container(gpu, tmp_path):
+    """The same checkpoint in the GGUF container (B1_0 = type 100, the
+    reference converter's renaming) loads to the same weights."""
+    from gguf_writer import write_gguf
+    src = _klein(seed=15)
+    dst = _klein(seed=16)
+    try:
+        ckpt = reference_checkpoint(src)
+        gg = {}
+        for name, arr in ckpt.items():
+            if arr.dtype == np.uint8:
+                gg[name] = (arr, arr.shape[1] // 6 * 32)
+            else:
+                gg[name] = arr
+        path = tmp_path / "klein_1bit.gguf"
+        write_gguf(path, gg)
+        dst.load_safetensors(path)
+        for name in ("double.0.img_qkv", "double.0.txt_mlp_out", "single.0.proj", "mod_img.w",
+                     "time.w1", "single.0.norm_q"):
+            assert np.array_equal(dst.weight(name), src.weight(name)), name
+    finally:
+        src.close()
+        dst.close()
