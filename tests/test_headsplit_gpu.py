@@ -20,7 +20,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+SMALL = dict(img=256, txt=64, grid=16, depth=2, single=2)
+# BASELINE config 5(b) at full size: 2048^2 (128 x 128 latent tokens) + 512
+# text tokens, all 19 + 38 blocks.
+FULL = dict(img=16384, txt=512, grid=128, depth=19, single=38)
+
+
+def _worker(rank, world, port, q, shape):
     import datetime
     import sys
     from pathlib import Path
@@ -37,7 +43,9 @@ def _worker(rank, world, port, q):
                             device_id=torch.device("cuda", rank))
     try:
         bb.init(rank)
-        m = bb.Dit(bb.PRESET_FLUX1, 256, 64, 16, 16, depth=2, depth_single=2, seed=11)
+        c = shape
+        m = bb.Dit(bb.PRESET_FLUX1, c["img"], c["txt"], c["grid"], c["grid"], depth=c["depth"],
+                   depth_single=c["single"], seed=11)
         m.set_partition(rank, world)
         rng = np.random.default_rng(3)
         img = torch.from_numpy(rng.standard_normal((m.img, m.in_ch)).astype(np.float32)).cuda()
@@ -48,7 +56,8 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         res = None
         if rank == 0:
-            ref_m = bb.Dit(bb.PRESET_FLUX1, 256, 64, 16, 16, depth=2, depth_single=2, seed=11)
+            ref_m = bb.Dit(bb.PRESET_FLUX1, c["img"], c["txt"], c["grid"], c["grid"],
+                           depth=c["depth"], depth_single=c["single"], seed=11)
             ref = torch.empty_like(out)
             ref_m.forward(img, txt, pooled, 600.0, ref)
             torch.cuda.synchronize()
@@ -64,7 +73,8 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_headsplit_two_gpus_matches_single():
+@pytest.mark.parametrize("shape", [SMALL, FULL], ids=["small", "2048sq_full_depth"])
+def test_headsplit_two_gpus_matches_single(shape):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -72,7 +82,7 @@ def test_headsplit_two_gpus_matches_single():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, shape)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict((r, (res, err)) for r, res, err in (q.get(timeout=600) for _ in range(2)))
