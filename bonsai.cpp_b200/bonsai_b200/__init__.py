@@ -79,6 +79,15 @@ SIGNATURES = {
     "bonsai_dit_begin": (_c_int, [_vp, _vp, _vp, _vp, _fp, _vp]),
     "bonsai_dit_phase": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp]),
     "bonsai_dit_end": (_c_int, [_vp, _vp, _vp]),
+    "bonsai_vae_create": (_c_int, [_c_int, _c_int, ctypes.c_ulonglong, ctypes.POINTER(_vp)]),
+    "bonsai_vae_destroy": (_c_int, [_vp]),
+    "bonsai_vae_load_safetensors": (_c_int, [_vp, ctypes.c_char_p]),
+    "bonsai_vae_decode": (_c_int, [_vp, _vp, _vp, _vp]),
+    "bonsai_vae_decode_host": (_c_int, [_vp, _vp, _vp, _vp]),
+    "bonsai_vae_rgb8": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
+    "bonsai_vae_info": (_c_int, [_vp, ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
+    "bonsai_conv2d_nhwc": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp,
+                                    _vp, _vp]),
 }
 
 
@@ -401,6 +410,70 @@ class Dit:
 
     def single_block(self, i: int, stream=None):
         check(lib().bonsai_dit_single_block(self.handle, i, stream_ptr(stream)), "single_block")
+
+
+class Vae:
+    """The Flux VAE decoder on the device (bonsai_vae_* entry points), the
+    reference's bonsai_vae program (src/vae_decoder.cpp) for one encoded
+    latent size: latent f32 [128][h][w] -> raw image f32 [3][16h][16w]."""
+
+    def __init__(self, latent_h: int, latent_w: int, seed: int = 0):
+        h = _vp()
+        check(lib().bonsai_vae_create(latent_h, latent_w, seed, ctypes.byref(h)), "bonsai_vae_create")
+        self.handle = h
+        self.latent_h, self.latent_w = latent_h, latent_w
+        self.image_h, self.image_w = 16 * latent_h, 16 * latent_w
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().bonsai_vae_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_safetensors(self, path) -> None:
+        check(lib().bonsai_vae_load_safetensors(self.handle, str(path).encode()),
+              "bonsai_vae_load_safetensors")
+
+    def decode(self, latent, image, stream=None) -> None:
+        """latent: cuda f32 [128][h][w]; image: cuda f32 [3][16h][16w]."""
+        assert latent.is_contiguous() and image.is_contiguous()
+        assert latent.numel() == 128 * self.latent_h * self.latent_w
+        assert image.numel() == 3 * self.image_h * self.image_w
+        check(lib().bonsai_vae_decode(self.handle, latent.data_ptr(), image.data_ptr(),
+                                      stream_ptr(stream)), "bonsai_vae_decode")
+
+    def decode_host(self, latent: np.ndarray, stream=None) -> np.ndarray:
+        lat = np.ascontiguousarray(latent, dtype=np.float32)
+        assert lat.size == 128 * self.latent_h * self.latent_w
+        out = np.empty((3, self.image_h, self.image_w), np.float32)
+        check(lib().bonsai_vae_decode_host(self.handle, lat.ctypes.data, out.ctypes.data,
+                                           stream_ptr(stream)), "bonsai_vae_decode_host")
+        return out
+
+
+def conv2d_nhwc(x, w, bias, out, resid=None, stream=None) -> None:
+    """x: cuda f16/bf16 NHWC [H][W][cin]; w: cuda f32 [cout][cin][k][k];
+    bias: cuda f32 [cout] or None; out (and resid): cuda f32 NHWC [H][W][cout]."""
+    import torch
+    hh, ww, cin = x.shape
+    cout, _, k, _ = w.shape
+    assert x.is_contiguous() and w.is_contiguous() and out.is_contiguous()
+    check(lib().bonsai_conv2d_nhwc(x.data_ptr(), hh, ww, cin, int(x.dtype == torch.bfloat16),
+                                   w.data_ptr(), cout, k, bias.data_ptr() if bias is not None else None,
+                                   resid.data_ptr() if resid is not None else None, out.data_ptr(),
+                                   stream_ptr(stream)), "bonsai_conv2d_nhwc")
+
+
+def vae_rgb8(image, rgb, stream=None) -> None:
+    """image: cuda f32 [3][H][W]; rgb: cuda u8 [H][W][3] (sigmoid, x255, clamp)."""
+    _, hh, ww = image.shape
+    check(lib().bonsai_vae_rgb8(image.data_ptr(), hh, ww, rgb.data_ptr(), stream_ptr(stream)),
+          "bonsai_vae_rgb8")
 
 
 def _wrap_device(ptr: int, nbytes: int, dtype, shape):

@@ -2,10 +2,15 @@
 
     python -m bonsai_b200.kernel_bench gemm M K N [--kernel auto|pair|single] [--reps R]
     python -m bonsai_b200.kernel_bench attention L [--heads H] [--reps R]
+    python -m bonsai_b200.kernel_bench conv H W CIN COUT [--k 3] [--bf16] [--reps R]
+    python -m bonsai_b200.kernel_bench vae LATENT_H LATENT_W [--reps R]
 
 gemm: B1_0 GEMM of M tokens x K inputs -> N outputs (f16 store epilogue) on
 seeded random weights/activations; attention: joint attention over L tokens,
-H heads of 128.  Prints one line: mean time per call over R calls after 3
+H heads of 128; conv: one VAE decoder convolution (NHWC f16/bf16 in, f32
+out, bias) on the implicit-GEMM kernel; vae: one whole decode of a
+latent_h x latent_w latent (synthetic weights) with the per-kernel time
+split.  Prints one line: mean time per call over R calls after 3
 warm-up calls (CUDA events on the current stream) and the TFLOP/s.
 """
 from __future__ import annotations
@@ -43,6 +48,18 @@ def main(argv=None) -> int:
     a.add_argument("L", type=int)
     a.add_argument("--heads", type=int, default=24)
     a.add_argument("--reps", type=int, default=10)
+    c = sub.add_parser("conv")
+    c.add_argument("H", type=int)
+    c.add_argument("W", type=int)
+    c.add_argument("cin", type=int)
+    c.add_argument("cout", type=int)
+    c.add_argument("--k", type=int, default=3)
+    c.add_argument("--bf16", action="store_true")
+    c.add_argument("--reps", type=int, default=10)
+    vae = sub.add_parser("vae")
+    vae.add_argument("lh", type=int)
+    vae.add_argument("lw", type=int)
+    vae.add_argument("--reps", type=int, default=5)
     args = ap.parse_args(argv)
 
     import numpy as np
@@ -59,6 +76,34 @@ def main(argv=None) -> int:
         ms = _time(lambda: bb.b1_gemm(x, w, bb.BONSAI_EPI_F16, out), args.reps)
         flop = 2.0 * args.M * args.N * args.K
         desc = f"gemm M={args.M} K={args.K} N={args.N} kernel={args.kernel}"
+    elif args.op == "conv":
+        td = torch.bfloat16 if args.bf16 else torch.float16
+        x = torch.randn(args.H, args.W, args.cin, device="cuda").to(td)
+        w = torch.randn(args.cout, args.cin, args.k, args.k, device="cuda") * 0.02
+        b = torch.randn(args.cout, device="cuda")
+        out = torch.empty(args.H, args.W, args.cout, device="cuda")
+        ms = _time(lambda: bb.conv2d_nhwc(x, w, b, out), args.reps)
+        flop = 2.0 * args.H * args.W * args.cin * args.cout * args.k * args.k
+        desc = f"conv {args.H}x{args.W} {args.cin}->{args.cout} k={args.k} {'bf16' if args.bf16 else 'f16'}"
+    elif args.op == "vae":
+        import json
+        v = bb.Vae(args.lh, args.lw, seed=1)
+        lat = torch.rand(128, args.lh, args.lw, device="cuda") * 2 - 1
+        img = torch.empty(3, 16 * args.lh, 16 * args.lw, device="cuda")
+        ms = _time(lambda: v.decode(lat, img), args.reps)
+        bb.profile_start()
+        v.decode(lat, img)
+        prof = bb.profile_stop()
+        v.close()
+        tot = sum(e["ms"] for e in prof.values())
+        for name, e in sorted(prof.items(), key=lambda kv: -kv[1]["ms"]):
+            tf = e["flop"] / (e["ms"] / 1e3) / 1e12 if e["ms"] > 0 else 0.0
+            gbs = e["bytes"] / (e["ms"] / 1e3) / 1e9 if e["ms"] > 0 else 0.0
+            print(json.dumps({"kernel": name, "launches": e["launches"], "ms": round(e["ms"], 3),
+                              "share": round(e["ms"] / tot, 3), "tflops": round(tf, 1),
+                              "gbs": round(gbs, 1)}))
+        flop = sum(e["flop"] for e in prof.values())
+        desc = f"vae decode latent {args.lh}x{args.lw} -> {16 * args.lh}x{16 * args.lw}"
     else:
         H, L = args.heads, args.L
         q, k, v = (torch.randn(H, L, 128, device="cuda").half() for _ in range(3))

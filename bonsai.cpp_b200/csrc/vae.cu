@@ -1,0 +1,529 @@
+// Flux VAE decoder engine on the device (C ABI bonsai_vae_*).
+//
+// Replaces the reference's bonsai_vae pipeline (src/vae_decoder.cpp:281-547):
+// the latent preprocessing (:353-421), the decoder graph
+// build_decoder_graph (src/vae_graph.cpp:174-212) computed by ggml on the
+// CPU in f32 NCHW, and the sigmoid / u8 conversion of chw_f32_to_hwc_u8
+// (:262-281).
+//
+// Layout: activations are NHWC.  The residual stream h is f32; every
+// convolution / linear reads 16-bit operands that the preceding memory-bound
+// kernel writes: GroupNorm + SiLU outputs (bounded by the normalisation) in
+// f16, the raw stream fed to the upsampler convs and the 1x1 shortcuts in
+// bf16 (its range is not bounded).  Accumulation is f32 in TMEM.
+// Convolutions, linears and the two attention products run on the tcgen05
+// implicit-GEMM kernel (vae_conv.cu); the attention is unfused (scores f32,
+// softmax numerators f16, 1/rowsum applied in the P.V epilogue) and walks the
+// queries in chunks so the score matrix stays bounded at large images.
+#include "internal.cuh"
+#include "vae.cuh"
+#include "bonsai_cuda.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace bonsai {
+namespace vae {
+
+struct Conv {
+  int cin = 0, cout = 0, taps = 1, cin_pad = 0, rows = 0;
+  bool bf16 = false;
+  void* w = nullptr;   // 16-bit [rows][taps][cin_pad]
+  float* b = nullptr;  // [rows], zero beyond cout
+};
+struct Norm {
+  int c = 0;
+  float* g = nullptr;
+  float* b = nullptr;
+};
+struct Res {
+  Norm n1, n2;
+  Conv c1, c2;
+  bool has_sc = false;
+  Conv sc;
+};
+
+enum Kind { K_CONV_W, K_CONV_B, K_VEC, K_BN_MEAN, K_BN_VAR };
+struct Entry {
+  std::string name;
+  Kind kind;
+  std::vector<long long> shape;
+  Conv* conv = nullptr;
+  float* vec = nullptr;
+  float init_mean = 0.f, init_std = 0.f;
+};
+
+constexpr int kUpIn[4] = {512, 512, 512, 256};
+constexpr int kUpOut[4] = {512, 512, 256, 128};
+constexpr float kGnEps = 1e-6f;
+constexpr long long kMaxScoreRows = 16384;  // query rows per attention chunk
+
+}  // namespace vae
+}  // namespace bonsai
+
+using namespace bonsai;
+using namespace bonsai::vae;
+
+struct bonsai_vae {
+  int lat_h = 0, lat_w = 0, H0 = 0, W0 = 0;
+  std::vector<void*> allocs;
+  std::vector<Entry> reg;
+  float* bn_mean = nullptr;  // [128]
+  float* bn_std = nullptr;   // [128] sqrt(var + 1e-4)
+  Conv post_quant, conv_in, to_q, to_k, to_v, to_out, upconv[3], conv_out;
+  Res mid[2], up[4][3];
+  Norm attn_norm, norm_out;
+  // activations
+  float* hbuf[2] = {nullptr, nullptr};
+  float* t = nullptr;
+  void* a16 = nullptr;
+  void* u16 = nullptr;
+  __half *q = nullptr, *k = nullptr, *vt = nullptr, *o = nullptr, *P = nullptr;
+  float* S = nullptr;
+  float* rowinv = nullptr;
+  long long qchunk = 0, ldS = 0, ldP = 0, ldV = 0;
+  double* gn_part = nullptr;
+  float* gn_stat = nullptr;
+  float* staging = nullptr;  // f32 upload / generation scratch
+  long long staging_elems = 0;
+  float *in_lat = nullptr, *out_img = nullptr;  // device copies for decode_host
+};
+
+namespace {
+
+#define RC(x)            \
+  do {                   \
+    int _rc = (x);       \
+    if (_rc) return _rc; \
+  } while (0)
+
+int valloc(bonsai_vae* v, void** p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e != cudaSuccess)
+    return fail(BONSAI_ERR_NOMEM, "vae: cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+  v->allocs.push_back(*p);
+  return 0;
+}
+
+long long round_up(long long x, long long m) { return (x + m - 1) / m * m; }
+
+// A convolution weight [cout][cin][k][k] (or, linear = true, an nn.Linear
+// weight [cout][cin]) and its bias [cout].
+int make_conv(bonsai_vae* v, const std::string& name, Conv& c, int cin, int cout, int k,
+              bool bf16, int rows = 0, bool linear = false) {
+  c.cin = cin;
+  c.cout = cout;
+  c.taps = k * k;
+  c.cin_pad = (int)round_up(cin, 64);
+  c.rows = rows > 0 ? rows : cout;
+  c.bf16 = bf16;
+  RC(valloc(v, &c.w, (size_t)c.rows * c.taps * c.cin_pad * 2));
+  RC(valloc(v, reinterpret_cast<void**>(&c.b), (size_t)c.rows * 4));
+  RC(cuda_status(cudaMemset(c.b, 0, (size_t)c.rows * 4), "vae: bias clear"));
+  const float stdv = 1.0f / std::sqrt((float)cin * c.taps);
+  Entry w{name + ".weight", K_CONV_W, {cout, cin, k, k}, &c, nullptr, 0.f, stdv};
+  if (linear) w.shape = {cout, cin};
+  v->reg.push_back(w);
+  v->reg.push_back(Entry{name + ".bias", K_CONV_B, {cout}, &c, nullptr, 0.f, 0.05f});
+  return 0;
+}
+
+int make_norm(bonsai_vae* v, const std::string& name, Norm& n, int c) {
+  n.c = c;
+  RC(valloc(v, reinterpret_cast<void**>(&n.g), (size_t)c * 4));
+  RC(valloc(v, reinterpret_cast<void**>(&n.b), (size_t)c * 4));
+  v->reg.push_back(Entry{name + ".weight", K_VEC, {c}, nullptr, n.g, 1.f, 0.1f});
+  v->reg.push_back(Entry{name + ".bias", K_VEC, {c}, nullptr, n.b, 0.f, 0.05f});
+  return 0;
+}
+
+int make_res(bonsai_vae* v, const std::string& p, Res& r, int cin, int cout) {
+  RC(make_norm(v, p + ".norm1", r.n1, cin));
+  RC(make_conv(v, p + ".conv1", r.c1, cin, cout, 3, false));
+  RC(make_norm(v, p + ".norm2", r.n2, cout));
+  RC(make_conv(v, p + ".conv2", r.c2, cout, cout, 3, false));
+  r.has_sc = cin != cout;
+  if (r.has_sc) RC(make_conv(v, p + ".conv_shortcut", r.sc, cin, cout, 1, true));
+  return 0;
+}
+
+// Upload f32 values of one registered tensor (from the staging buffer) into
+// its device form.
+int commit_entry(bonsai_vae* v, const Entry& e, const float* dev_src, cudaStream_t st) {
+  switch (e.kind) {
+    case K_CONV_W:
+      return launch_vae_pack_weight(dev_src, e.conv->cout, e.conv->cin, e.conv->taps, e.conv->rows,
+                                    e.conv->cin_pad, e.conv->w, e.conv->bf16, st);
+    case K_CONV_B:
+      return cuda_status(cudaMemcpyAsync(e.conv->b, dev_src, (size_t)e.conv->cout * 4,
+                                         cudaMemcpyDeviceToDevice, st),
+                         "vae: bias copy");
+    case K_VEC:
+      return cuda_status(cudaMemcpyAsync(e.vec, dev_src, (size_t)e.shape[0] * 4,
+                                         cudaMemcpyDeviceToDevice, st),
+                         "vae: vector copy");
+    default: {
+      // BatchNorm statistics: mean as is, std = sqrt(var + 1e-4) computed on
+      // the host in f32 as src/vae_decoder.cpp:368-372 does.
+      float host[128];
+      RC(cuda_status(cudaStreamSynchronize(st), "vae: bn sync"));
+      RC(cuda_status(cudaMemcpy(host, dev_src, sizeof(host), cudaMemcpyDeviceToHost), "vae: bn copy"));
+      if (e.kind == K_BN_VAR)
+        for (float& x : host) x = std::sqrt(x + 1e-4f);
+      float* dst = e.kind == K_BN_MEAN ? v->bn_mean : v->bn_std;
+      return cuda_status(cudaMemcpy(dst, host, sizeof(host), cudaMemcpyHostToDevice), "vae: bn upload");
+    }
+  }
+}
+
+long long numel(const std::vector<long long>& s) {
+  long long n = 1;
+  for (long long d : s) n *= d;
+  return n;
+}
+
+int conv(bonsai_vae* v, const Conv& c, const void* in, long long ld_in, int H, int W, void* out,
+         long long ld_out, int mode, cudaStream_t st, const float* resid = nullptr,
+         long long ld_resid = 0, int n_out = 0) {
+  VaeConvArgs a;
+  a.in = in;
+  a.ld_in = ld_in;
+  a.H = H;
+  a.W = W;
+  a.cin = c.cin_pad;
+  a.bf16 = c.bf16;
+  a.taps = c.taps;
+  a.w = c.w;
+  a.w_ld = (long long)c.taps * c.cin_pad;
+  a.k_per_tap = c.cin_pad;
+  a.N = n_out > 0 ? n_out : c.cout;
+  a.w_rows = c.rows;
+  a.bias = c.b;
+  a.resid = resid;
+  a.ld_resid = ld_resid;
+  a.out = out;
+  a.ld_out = ld_out;
+  a.out_mode = mode;
+  (void)v;
+  return launch_vae_conv(a, st);
+}
+
+int group_norm(bonsai_vae* v, const float* x, long long P, const Norm& n, bool silu, void* y,
+               bool bf16, cudaStream_t st) {
+  RC(launch_vae_gn_stats(x, P, n.c, v->gn_part, v->gn_stat, kGnEps, st));
+  return launch_vae_gn_apply(x, P, n.c, v->gn_stat, n.g, n.b, silu, y, bf16, st);
+}
+
+// build_resnet (src/vae_graph.cpp:44-76) on the stream buffer hbuf[cur].
+int resnet(bonsai_vae* v, const Res& r, int& cur, int H, int W, cudaStream_t st) {
+  const long long P = (long long)H * W;
+  float* x = v->hbuf[cur];
+  const int ci = r.c1.cin, co = r.c1.cout;
+  RC(group_norm(v, x, P, r.n1, true, v->a16, false, st));
+  RC(conv(v, r.c1, v->a16, ci, H, W, v->t, co, VOUT_F32, st));
+  RC(group_norm(v, v->t, P, r.n2, true, v->a16, false, st));
+  if (r.has_sc) {
+    RC(launch_vae_cast(x, P * ci, v->u16, true, st));
+    RC(conv(v, r.sc, v->u16, ci, H, W, v->t, co, VOUT_F32, st));
+    RC(conv(v, r.c2, v->a16, co, H, W, v->hbuf[cur ^ 1], co, VOUT_F32, st, v->t, co));
+    cur ^= 1;
+    return 0;
+  }
+  return conv(v, r.c2, v->a16, co, H, W, x, co, VOUT_F32, st, x, co);
+}
+
+// build_attention (src/vae_graph.cpp:97-166): one head over all H*W pixels.
+int attention(bonsai_vae* v, int cur, int H, int W, cudaStream_t st) {
+  const long long P = (long long)H * W;
+  constexpr int C = 512;
+  float* x = v->hbuf[cur];
+  RC(group_norm(v, x, P, v->attn_norm, false, v->a16, false, st));
+  RC(conv(v, v->to_q, v->a16, C, H, W, v->q, C, VOUT_F16, st));
+  RC(conv(v, v->to_k, v->a16, C, H, W, v->k, C, VOUT_F16, st));
+  RC(conv(v, v->to_v, v->a16, C, H, W, v->vt, v->ldV, VOUT_F16_T, st));
+  const float scale = 1.0f / std::sqrt((float)C);
+  for (long long r0 = 0; r0 < P; r0 += v->qchunk) {
+    const int rows = (int)std::min<long long>(v->qchunk, P - r0);
+    VaeConvArgs s;
+    s.in = v->q + r0 * C;
+    s.ld_in = C;
+    s.H = 1;
+    s.W = rows;
+    s.cin = C;
+    s.taps = 1;
+    s.w = v->k;
+    s.w_ld = C;
+    s.N = (int)P;
+    s.out = v->S;
+    s.ld_out = v->ldS;
+    s.out_mode = VOUT_F32;
+    RC(launch_vae_conv(s, st));
+    RC(launch_vae_softmax(v->S, v->ldS, rows, (int)P, scale, v->P, v->ldP, v->rowinv, st));
+    VaeConvArgs pv;
+    pv.in = v->P;
+    pv.ld_in = v->ldP;
+    pv.H = 1;
+    pv.W = rows;
+    pv.cin = (int)P;
+    pv.taps = 1;
+    pv.w = v->vt;
+    pv.w_ld = v->ldV;
+    pv.N = C;
+    pv.row_scale = v->rowinv;
+    pv.out = v->o + r0 * C;
+    pv.ld_out = C;
+    pv.out_mode = VOUT_F16;
+    RC(launch_vae_conv(pv, st));
+  }
+  return conv(v, v->to_out, v->o, C, H, W, x, C, VOUT_F32, st, x, C);
+}
+
+int decode(bonsai_vae* v, const float* latent, float* image, cudaStream_t st) {
+  int H = v->H0, W = v->W0;
+  RC(launch_vae_preprocess(latent, v->lat_h, v->lat_w, v->bn_mean, v->bn_std,
+                           static_cast<__half*>(v->a16), st));
+  // post_quant_conv writes all 64 padded channels (rows 32..63 are zero).
+  RC(conv(v, v->post_quant, v->a16, 64, H, W, v->u16, 64, VOUT_F16, st, nullptr, 0, 64));
+  int cur = 0;
+  RC(conv(v, v->conv_in, v->u16, 64, H, W, v->hbuf[0], 512, VOUT_F32, st));
+  RC(resnet(v, v->mid[0], cur, H, W, st));
+  RC(attention(v, cur, H, W, st));
+  RC(resnet(v, v->mid[1], cur, H, W, st));
+  for (int i = 0; i < 4; ++i) {
+    for (int j = 0; j < 3; ++j) RC(resnet(v, v->up[i][j], cur, H, W, st));
+    if (i < 3) {
+      const int C = kUpOut[i];
+      RC(launch_vae_upsample2(v->hbuf[cur], H, W, C, v->u16, true, st));
+      H *= 2;
+      W *= 2;
+      RC(conv(v, v->upconv[i], v->u16, C, H, W, v->hbuf[cur ^ 1], C, VOUT_F32, st));
+      cur ^= 1;
+    }
+  }
+  RC(group_norm(v, v->hbuf[cur], (long long)H * W, v->norm_out, true, v->a16, false, st));
+  return conv(v, v->conv_out, v->a16, 128, H, W, image, 0, VOUT_F32_NCHW, st);
+}
+
+__global__ void rgb8_kernel(const float* __restrict__ img, long long plane,
+                            uint8_t* __restrict__ rgb) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < plane;
+       i += (long long)gridDim.x * blockDim.x) {
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const float r = img[c * plane + i];
+      const float s = 1.0f / (1.0f + expf(-r));
+      rgb[i * 3 + c] = (uint8_t)min(255, max(0, (int)(s * 255.0f)));
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int bonsai_vae_create(int latent_h, int latent_w, unsigned long long seed, bonsai_vae_t* out) {
+  if (!out) return fail(BONSAI_ERR_ARG, "vae_create: null argument");
+  *out = nullptr;
+  if (latent_h < 1 || latent_w < 1 || (long long)latent_h * latent_w > (1LL << 20))
+    return fail(BONSAI_ERR_ARG, "vae_create: latent size out of range");
+  std::unique_ptr<bonsai_vae> v(new bonsai_vae());
+  v->lat_h = latent_h;
+  v->lat_w = latent_w;
+  v->H0 = 2 * latent_h;
+  v->W0 = 2 * latent_w;
+  bonsai_vae* m = v.get();
+
+  RC(valloc(m, reinterpret_cast<void**>(&m->bn_mean), 128 * 4));
+  RC(valloc(m, reinterpret_cast<void**>(&m->bn_std), 128 * 4));
+  // The reference's loading order (src/vae_decoder.cpp:214-250), 32-channel
+  // tensors padded to 64 channels.
+  RC(make_conv(m, "post_quant_conv", m->post_quant, 32, 32, 1, false, 64));
+  RC(make_conv(m, "decoder.conv_in", m->conv_in, 32, 512, 3, false));
+  RC(make_res(m, "decoder.mid_block.resnets.0", m->mid[0], 512, 512));
+  RC(make_norm(m, "decoder.mid_block.attentions.0.group_norm", m->attn_norm, 512));
+  RC(make_conv(m, "decoder.mid_block.attentions.0.to_q", m->to_q, 512, 512, 1, false, 0, true));
+  RC(make_conv(m, "decoder.mid_block.attentions.0.to_k", m->to_k, 512, 512, 1, false, 0, true));
+  RC(make_conv(m, "decoder.mid_block.attentions.0.to_v", m->to_v, 512, 512, 1, false, 0, true));
+  RC(make_conv(m, "decoder.mid_block.attentions.0.to_out.0", m->to_out, 512, 512, 1, false, 0, true));
+  RC(make_res(m, "decoder.mid_block.resnets.1", m->mid[1], 512, 512));
+  for (int i = 0; i < 4; ++i) {
+    for (int j = 0; j < 3; ++j)
+      RC(make_res(m, "decoder.up_blocks." + std::to_string(i) + ".resnets." + std::to_string(j),
+                  m->up[i][j], j == 0 ? kUpIn[i] : kUpOut[i], kUpOut[i]));
+    if (i < 3)
+      RC(make_conv(m, "decoder.up_blocks." + std::to_string(i) + ".upsamplers.0.conv",
+                   m->upconv[i], kUpOut[i], kUpOut[i], 3, true));
+  }
+  RC(make_norm(m, "decoder.conv_norm_out", m->norm_out, 128));
+  RC(make_conv(m, "decoder.conv_out", m->conv_out, 128, 3, 3, false, 16));
+  m->reg.push_back(Entry{"bn.running_mean", K_BN_MEAN, {128}, nullptr, nullptr, 0.f, 0.5f});
+  m->reg.push_back(Entry{"bn.running_var", K_BN_VAR, {128}, nullptr, nullptr, 0.25f, 3.75f});
+
+  // Activations (sizes: the largest tensor of each role over the schedule).
+  const long long P0 = (long long)m->H0 * m->W0;
+  RC(valloc(m, reinterpret_cast<void**>(&m->hbuf[0]), (size_t)P0 * 16384 * 4));
+  RC(valloc(m, reinterpret_cast<void**>(&m->hbuf[1]), (size_t)P0 * 16384 * 4));
+  RC(valloc(m, reinterpret_cast<void**>(&m->t), (size_t)P0 * 8192 * 4));
+  RC(valloc(m, &m->a16, (size_t)P0 * 16384 * 2));
+  RC(valloc(m, &m->u16, (size_t)P0 * 16384 * 2));
+  RC(valloc(m, reinterpret_cast<void**>(&m->q), (size_t)P0 * 512 * 2));
+  RC(valloc(m, reinterpret_cast<void**>(&m->k), (size_t)P0 * 512 * 2));
+  RC(valloc(m, reinterpret_cast<void**>(&m->o), (size_t)P0 * 512 * 2));
+  m->ldV = round_up(P0, 64);
+  RC(valloc(m, reinterpret_cast<void**>(&m->vt), (size_t)512 * m->ldV * 2));
+  m->qchunk = std::min<long long>(P0, kMaxScoreRows);
+  m->ldS = round_up(P0, 4);
+  m->ldP = round_up(P0, 64);
+  RC(valloc(m, reinterpret_cast<void**>(&m->S), (size_t)m->qchunk * m->ldS * 4));
+  RC(valloc(m, reinterpret_cast<void**>(&m->P), (size_t)m->qchunk * m->ldP * 2));
+  RC(valloc(m, reinterpret_cast<void**>(&m->rowinv), (size_t)m->qchunk * 4));
+  RC(valloc(m, reinterpret_cast<void**>(&m->gn_part), (size_t)kGnMaxBlocks * 64 * 8));
+  RC(valloc(m, reinterpret_cast<void**>(&m->gn_stat), 64 * 4));
+  long long most = 0;
+  for (const Entry& e : m->reg) most = std::max(most, numel(e.shape));
+  m->staging_elems = most;
+  RC(valloc(m, reinterpret_cast<void**>(&m->staging), (size_t)most * 4));
+  RC(valloc(m, reinterpret_cast<void**>(&m->in_lat), (size_t)128 * latent_h * latent_w * 4));
+  RC(valloc(m, reinterpret_cast<void**>(&m->out_img), (size_t)3 * 64 * P0 * 4));
+
+  // Seeded synthetic weights, through the same packing path as a checkpoint.
+  for (size_t i = 0; i < m->reg.size(); ++i) {
+    const Entry& e = m->reg[i];
+    const bool uni = e.kind == K_BN_VAR;
+    RC(launch_vae_fill(m->staging, numel(e.shape), seed * 1000003ull + i, e.init_mean, e.init_std,
+                       uni, 0));
+    RC(commit_entry(m, e, m->staging, 0));
+  }
+  RC(cuda_status(cudaDeviceSynchronize(), "vae_create: initialisation"));
+  *out = v.release();
+  return 0;
+}
+
+int bonsai_vae_destroy(bonsai_vae_t v) {
+  if (!v) return 0;
+  cudaDeviceSynchronize();
+  for (void* p : v->allocs) cudaFree(p);
+  delete v;
+  return 0;
+}
+
+int bonsai_vae_load_safetensors(bonsai_vae_t v, const char* path) {
+  if (!v || !path) return fail(BONSAI_ERR_ARG, "vae_load_safetensors: null argument");
+  StFile f;
+  RC(st_open(path, f));
+  std::vector<float> host;
+  std::vector<uint16_t> raw16;
+  for (const Entry& e : v->reg) {
+    auto it = f.tensors.find(e.name);
+    if (it == f.tensors.end())
+      return fail(BONSAI_ERR_ARG, "vae_load_safetensors: tensor '" + e.name + "' not found in " + path);
+    const StTensor& t = it->second;
+    bool shape_ok = t.shape.size() == e.shape.size();
+    for (size_t d = 0; shape_ok && d < e.shape.size(); ++d) shape_ok = t.shape[d] == e.shape[d];
+    if (!shape_ok) {
+      std::string want;
+      for (long long d : e.shape) want += (want.empty() ? "" : ",") + std::to_string(d);
+      return fail(BONSAI_ERR_ARG, "vae_load_safetensors: '" + e.name + "' must have shape [" + want + "]");
+    }
+    const long long n = numel(e.shape);
+    host.resize((size_t)n);
+    if (t.dtype == "F32") {
+      RC(st_read(f, t, host.data(), n * 4));
+    } else if (t.dtype == "F16" || t.dtype == "BF16") {
+      raw16.resize((size_t)n);
+      RC(st_read(f, t, raw16.data(), n * 2));
+      for (long long i = 0; i < n; ++i) {
+        if (t.dtype == "BF16") {
+          const uint32_t b = (uint32_t)raw16[i] << 16;
+          std::memcpy(&host[i], &b, 4);
+        } else {
+          host[i] = __half2float(__ushort_as_half(raw16[i]));
+        }
+      }
+    } else {
+      return fail(BONSAI_ERR_ARG, "vae_load_safetensors: '" + e.name + "' must be F32, F16 or BF16, found " + t.dtype);
+    }
+    RC(cuda_status(cudaMemcpy(v->staging, host.data(), (size_t)n * 4, cudaMemcpyHostToDevice),
+                   "vae_load_safetensors: upload"));
+    RC(commit_entry(v, e, v->staging, 0));
+    RC(cuda_status(cudaDeviceSynchronize(), "vae_load_safetensors: pack"));
+  }
+  return 0;
+}
+
+int bonsai_vae_decode(bonsai_vae_t v, const float* latent, float* image, void* stream) {
+  if (!v || !latent || !image) return fail(BONSAI_ERR_ARG, "vae_decode: null argument");
+  return decode(v, latent, image, static_cast<cudaStream_t>(stream));
+}
+
+int bonsai_vae_decode_host(bonsai_vae_t v, const float* host_latent, float* host_image,
+                           void* stream) {
+  if (!v || !host_latent || !host_image) return fail(BONSAI_ERR_ARG, "vae_decode_host: null argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t in_bytes = (size_t)128 * v->lat_h * v->lat_w * 4;
+  const size_t out_bytes = (size_t)3 * 64 * v->H0 * v->W0 * 4;
+  RC(cuda_status(cudaMemcpyAsync(v->in_lat, host_latent, in_bytes, cudaMemcpyHostToDevice, st),
+                 "vae_decode_host: latent copy"));
+  RC(decode(v, v->in_lat, v->out_img, st));
+  RC(cuda_status(cudaMemcpyAsync(host_image, v->out_img, out_bytes, cudaMemcpyDeviceToHost, st),
+                 "vae_decode_host: image copy"));
+  return cuda_status(cudaStreamSynchronize(st), "vae_decode_host: synchronize");
+}
+
+int bonsai_vae_rgb8(const float* image, int height, int width, unsigned char* rgb, void* stream) {
+  if (!image || !rgb || height < 1 || width < 1) return fail(BONSAI_ERR_ARG, "vae_rgb8: bad argument");
+  const long long plane = (long long)height * width;
+  const int grid = (int)std::min<long long>((plane + 255) / 256, (long long)num_sms() * 8);
+  rgb8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(image, plane, rgb);
+  return launch_status("vae rgb8_kernel launch");
+}
+
+int bonsai_conv2d_nhwc(const void* x, int H, int W, int cin, int x_bf16, const float* w, int cout,
+                       int k, const float* bias, const float* resid, float* y, void* stream) {
+  if (!x || !w || !y || H < 1 || W < 1 || cin < 1 || cout < 1 || (k != 1 && k != 3))
+    return fail(BONSAI_ERR_ARG, "conv2d_nhwc: bad argument");
+  if (cin % 8 != 0) return fail(BONSAI_ERR_ARG, "conv2d_nhwc: cin must be a multiple of 8");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int taps = k * k;
+  const int cin_pad = k == 1 ? cin : (int)round_up(cin, 64);
+  void* packed = nullptr;
+  RC(cuda_status(cudaMallocAsync(&packed, (size_t)cout * taps * cin_pad * 2, st),
+                 "conv2d_nhwc: weight scratch"));
+  int rc = launch_vae_pack_weight(w, cout, cin, taps, cout, cin_pad, packed, x_bf16 != 0, st);
+  if (!rc) {
+    VaeConvArgs a;
+    a.in = x;
+    a.ld_in = cin;
+    a.H = H;
+    a.W = W;
+    a.cin = cin;
+    a.bf16 = x_bf16 != 0;
+    a.taps = taps;
+    a.w = packed;
+    a.w_ld = (long long)taps * cin_pad;
+    a.k_per_tap = cin_pad;
+    a.N = cout;
+    a.bias = bias;
+    a.resid = resid;
+    a.ld_resid = cout;
+    a.out = y;
+    a.ld_out = cout;
+    a.out_mode = VOUT_F32;
+    rc = launch_vae_conv(a, st);
+  }
+  cudaFreeAsync(packed, st);
+  return rc;
+}
+
+int bonsai_vae_info(bonsai_vae_t v, int* image_h, int* image_w) {
+  if (!v) return fail(BONSAI_ERR_ARG, "vae_info: null argument");
+  if (image_h) *image_h = 8 * v->H0;
+  if (image_w) *image_w = 8 * v->W0;
+  return 0;
+}
+
+}  // extern "C"

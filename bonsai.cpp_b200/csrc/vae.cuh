@@ -1,0 +1,81 @@
+// Internal declarations of the Flux VAE decoder kernels (vae_conv.cu,
+// vae_ops.cu) used by the decoder engine (vae.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace bonsai {
+
+// Output layouts of the implicit-GEMM epilogue.
+enum VaeOut : int {
+  VOUT_F32 = 0,       // f32 [pix][ld_out] + n
+  VOUT_F16 = 1,       // f16 [pix][ld_out] + n
+  VOUT_BF16 = 2,      // bf16 [pix][ld_out] + n
+  VOUT_F16_T = 3,     // f16 [n][ld_out] + pix (transposed)
+  VOUT_F32_NCHW = 4,  // f32 [n][H*W] + pix (planar image)
+};
+
+// out[pix][n] = row_scale[pix] * sum_{tap, c} in[pix + off(tap)][c] * w[n][tap*k_per_tap + c]
+//               + bias[n] + resid[pix][n]
+// in: NHWC 16-bit [H][W][ld_in] (channels 0..cin-1 used), zero outside the
+// image (taps = 9: 3x3 'same' convolution; taps = 1: pointwise / plain GEMM).
+// w: 16-bit [w_rows][w_ld] (same type as in); for taps = 9, k_per_tap >= cin
+// rounded up to 64 and the padding columns hold zeros.  bias, row_scale and
+// resid are optional.  in, w, resid and out must be 16-byte aligned.
+struct VaeConvArgs {
+  const void* in = nullptr;
+  long long ld_in = 0;
+  int H = 0, W = 0, cin = 0;
+  bool bf16 = false;
+  int taps = 1;
+  const void* w = nullptr;
+  long long w_ld = 0;
+  int k_per_tap = 0;
+  int N = 0;
+  int w_rows = 0;  // weight rows in memory (>= N); 0 = N
+  const float* bias = nullptr;
+  const float* row_scale = nullptr;
+  const float* resid = nullptr;
+  long long ld_resid = 0;
+  void* out = nullptr;
+  long long ld_out = 0;
+  int out_mode = VOUT_F32;
+  int bn = 0;  // output-channel tile (0 = automatic)
+};
+int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st);
+
+// GroupNorm(32) statistics of an f32 NHWC tensor [pixels][C] (C in {128,
+// 256, 512, 1024}): per-block f64 partial sums into partials[nblk][32][2],
+// then mean_rstd[32][2] = {mean, 1/sqrt(var + eps)}.  nblk <= kGnMaxBlocks.
+constexpr int kGnMaxBlocks = 1184;
+int launch_vae_gn_stats(const float* x, long long pixels, int C, double* partials,
+                        float* mean_rstd, float eps, cudaStream_t st);
+// y = [silu]((x - mean_g) * rstd_g * gamma_c + beta_c), f32 -> f16 / bf16.
+int launch_vae_gn_apply(const float* x, long long pixels, int C, const float* mean_rstd,
+                        const float* gamma, const float* beta, bool silu, void* y, bool y_bf16,
+                        cudaStream_t st);
+// Nearest 2x upsample of f32 NHWC [H][W][C] into 16-bit [2H][2W][C].
+int launch_vae_upsample2(const float* x, int H, int W, int C, void* y, bool y_bf16,
+                         cudaStream_t st);
+// f32 -> 16-bit copy of n elements (n % 4 == 0).
+int launch_vae_cast(const float* x, long long n, void* y, bool y_bf16, cudaStream_t st);
+// Encoded latent f32 [128][h][w] -> f16 NHWC [2h][2w][64]: channel c < 32 of
+// pixel (2i + di, 2j + dj) = latent[4c + 2di + dj][i][j] * bn_std + bn_mean,
+// channels 32..63 zero.
+int launch_vae_preprocess(const float* latent, int h, int w, const float* bn_mean,
+                          const float* bn_std, __half* y, cudaStream_t st);
+// Row softmax numerators: P[r][c] = exp(scale * (S[r][c] - max_c S[r][c])) as
+// f16, rowinv[r] = 1 / sum_c P[r][c] (f32 sum of the unrounded values).
+int launch_vae_softmax(const float* S, long long ld_s, int rows, int cols, float scale,
+                       __half* P, long long ld_p, float* rowinv, cudaStream_t st);
+// PyTorch-layout f32 weight [cout][cin][taps] -> 16-bit [rows][taps][cin_pad]
+// (zero rows >= cout and columns >= cin).
+int launch_vae_pack_weight(const float* src, int cout, int cin, int taps, int rows, int cin_pad,
+                           void* dst, bool bf16, cudaStream_t st);
+// Seeded synthetic values: dst[i] = mean + std * N(0,1) (uniform = false) or
+// mean + std * U[0,1) (uniform = true), from a counter-based hash of (seed, i).
+int launch_vae_fill(float* dst, long long n, unsigned long long seed, float mean, float std,
+                    bool uniform, cudaStream_t st);
+
+}  // namespace bonsai

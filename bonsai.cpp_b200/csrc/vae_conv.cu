@@ -1,0 +1,453 @@
+// Implicit-GEMM convolution / dense GEMM on tcgen05 for the Flux VAE decoder.
+//
+// Replaces the ggml_conv_2d_direct and ggml_mul_mat nodes of the reference's
+// decoder graph (src/vae_graph.cpp:44-212).  Activations are NHWC (channels
+// innermost) f16 or bf16; a stride-1 convolution with 'same' zero padding
+// (3x3 or 1x1) is a GEMM with M = pixels, N = output channels and
+// K = taps x input channels:
+//
+//   out[pix][n] = sum_tap sum_c in[pix + offset(tap)][c] * w[n][tap][c]
+//
+// One CTA (persistent, one per SM) computes 128 pixels x BN output channels
+// per tile with tcgen05.mma.cta_group::1.kind::f16 (M = 128, N = BN <= 256,
+// f32 accumulators in TMEM, two of them so the epilogue of one tile overlaps
+// the next tile's MMAs).  The 128 pixels are a bw x bh rectangle of the
+// image; for each tap the TMA warp loads the rectangle shifted by the tap's
+// offset as one 3-D box {64 channels, bw, bh} of the NHWC tensor.  Pixels
+// outside the image come back as zeros from the TMA's out-of-bounds fill,
+// which is exactly the convolution's zero padding; the box lands in shared
+// memory as 128 rows of 128 bytes in the 128-byte-swizzled K-major layout
+// the MMA reads.  The weight tile {64, BN} of w[n][tap*Cin + c] comes by a
+// 2-D TMA load.  A plain GEMM is the 1x1 case over a 1-row "image".
+//
+// The epilogue (8 warps) reads the accumulators with tcgen05.ld (one pixel
+// per thread), optionally scales by a per-pixel factor, adds the bias and an
+// f32 residual, and writes f32 / f16 / bf16 NHWC, an f16 transposed
+// [n][pixel] tensor, or f32 NCHW (the decoder's final image).
+#include "internal.cuh"
+#include "ptx.cuh"
+#include "vae.cuh"
+#include "bonsai_cuda.h"
+
+#include <cudaTypedefs.h>
+#include <algorithm>
+
+namespace bonsai {
+namespace gemm {
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn();
+}
+
+namespace vconv {
+
+constexpr int BM = 128;       // pixels per tile (MMA M)
+constexpr int BN_MAX = 256;   // output channels per tile (MMA N)
+constexpr int BK = 64;        // input channels per pipeline stage
+constexpr int STAGES = 4;
+constexpr int A_STAGE = BM * BK * 2;      // 16 KB
+constexpr int B_STAGE = BN_MAX * BK * 2;  // 32 KB
+constexpr int TMEM_COLS = 2 * BN_MAX;
+constexpr int WARP_TMA = 0;
+constexpr int WARP_MMA = 1;
+constexpr int WARP_EPI0 = 2;
+constexpr int EPI_WARPS = 8;
+constexpr int NUM_THREADS = (WARP_EPI0 + EPI_WARPS) * 32;
+constexpr int SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + 256;
+
+struct Params {
+  int H, W;                // image (output pixels H*W; the input has the same size)
+  int bw, bh, tiles_x;     // pixel tile bw x bh = 128
+  int n_ntiles, num_tiles;
+  int BN;                  // output channels per tile (multiple of 16, <= 256)
+  int taps;                // 1 or 9
+  int cin_blocks;          // 64-channel blocks per tap
+  int k_per_tap;           // weight K offset between taps
+  int N;                   // output channels
+  const float* bias;
+  const float* row_scale;
+  const float* resid;
+  long long ld_resid;
+  void* out;
+  long long ld_out;
+  int out_mode;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    conv_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+                const Params p, const uint32_t idesc) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* as = smem;
+  uint8_t* bs = smem + STAGES * A_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bs + STAGES * B_STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* dfull = empty + STAGES;
+  uint64_t* dempty = dfull + 2;
+  uint64_t* drain = dempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(&dfull[b], 1);
+      bar_init(&dempty[b], EPI_WARPS);
+    }
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == WARP_MMA) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int ksteps = p.taps * p.cin_blocks;
+
+  if (warp == WARP_TMA) {
+    if (elect_one()) {
+      tma_prefetch_desc(&amap);
+      tma_prefetch_desc(&bmap);
+      const uint32_t stage_bytes = (uint32_t)(A_STAGE + p.BN * BK * 2);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int m = tile / p.n_ntiles;
+        const int n0 = (tile - m * p.n_ntiles) * p.BN;
+        const int ty = m / p.tiles_x;
+        const int x0 = (m - ty * p.tiles_x) * p.bw;
+        const int y0 = ty * p.bh;
+        for (int t = 0; t < p.taps && ok; ++t) {
+          const int dy = p.taps == 9 ? t / 3 - 1 : 0;
+          const int dx = p.taps == 9 ? t % 3 - 1 : 0;
+          for (int cb = 0; cb < p.cin_blocks; ++cb, ++it) {
+            const int s = it % STAGES;
+            const uint32_t ph = (it / STAGES) & 1;
+            if (!wait_bar(&empty[s], ph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
+              ok = false;
+              break;
+            }
+            bar_arrive_expect_tx(&full[s], stage_bytes);
+            tma_load_3d(as + s * A_STAGE, &amap, &full[s], cb * BK, x0 + dx, y0 + dy);
+            tma_load_2d(bs + s * B_STAGE, &bmap, &full[s], t * p.k_per_tap + cb * BK, n0);
+          }
+        }
+      }
+      if (!ok) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 1000000ull) {
+        }
+      }
+    }
+  } else if (warp == WARP_MMA) {
+    if (elect_one()) {
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++lt) {
+        const uint32_t b = lt & 1;
+        const uint32_t dph = (lt >> 1) & 1;
+        if (!wait_bar(&dempty[b], dph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + b * BN_MAX;
+        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!wait_bar(&full[s], ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aaddr = smem_u32(as + s * A_STAGE);
+          const uint32_t baddr = smem_u32(bs + s * B_STAGE);
+#pragma unroll
+          for (int k16 = 0; k16 < BK / 16; ++k16) {
+            const uint64_t adesc = make_smem_desc(aaddr + k16 * 32, 16, 1024);
+            const uint64_t bdesc = make_smem_desc(baddr + k16 * 32, 16, 1024);
+            mma_ss(d_tmem, adesc, bdesc, idesc, (ks | k16) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&dfull[b]);
+      }
+      tc_commit(drain);
+      const uint32_t da = smem_u32(drain);
+      const unsigned long long t0 = globaltimer_ns();
+      while (!bar_try_wait(da, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          if (p.err) atomicCAS(p.err, 0, DEV_ERR_TIMEOUT_MMA);
+          break;
+        }
+      }
+    }
+  } else {
+    // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its pixels); the two
+    // warps of a lane quarter take alternate 32-column chunks.
+    const int q = warp & 3;
+    const int eh = (warp - WARP_EPI0) >> 2;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const int nch = (p.BN + 31) / 32;
+    uint32_t lt = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
+      const int m = tile / p.n_ntiles;
+      const int n0 = (tile - m * p.n_ntiles) * p.BN;
+      const int ty = m / p.tiles_x;
+      const int x0 = (m - ty * p.tiles_x) * p.bw;
+      const int y0 = ty * p.bh;
+      const uint32_t b = lt & 1;
+      const uint32_t dph = (lt >> 1) & 1;
+      const bool good = wait_bar(&dfull[b], dph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, good)) break;  // tcgen05.ld is warp-collective
+      tc_fence_after();
+
+      const int ml = q * 32 + (int)lane;
+      const int px = x0 + ml % p.bw;
+      const int py = y0 + ml / p.bw;
+      const bool valid = px < p.W && py < p.H;
+      const long long pix = (long long)py * p.W + px;
+      const float rs = (p.row_scale && valid) ? p.row_scale[pix] : 1.0f;
+
+      for (int c = eh; c < nch; c += 2) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + b * BN_MAX + c * 32, v);
+        tmem_wait_ld();
+        const int nb = n0 + c * 32;
+        const int nn = min(min(32, p.BN - c * 32), p.N - nb);
+        if (!valid || nn <= 0) continue;
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * rs;
+        if (p.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nn) f[j] += p.bias[nb + j];
+        }
+        const bool vec = nn == 32;
+        if (p.resid) {
+          const float* r = p.resid + pix * p.ld_resid + nb;
+          if (vec && (p.ld_resid & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 o = *reinterpret_cast<const float4*>(r + j);
+              f[j] += o.x;
+              f[j + 1] += o.y;
+              f[j + 2] += o.z;
+              f[j + 3] += o.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nn) f[j] += r[j];
+          }
+        }
+        switch (p.out_mode) {
+          case VOUT_F32: {
+            float* d = reinterpret_cast<float*>(p.out) + pix * p.ld_out + nb;
+            if (vec && (p.ld_out & 3) == 0) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(d + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nn) d[j] = f[j];
+            }
+            break;
+          }
+          case VOUT_F16:
+          case VOUT_BF16: {
+            const bool bf = p.out_mode == VOUT_BF16;
+            uint16_t* d = reinterpret_cast<uint16_t*>(p.out) + pix * p.ld_out + nb;
+            if (vec && (p.ld_out & 7) == 0) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 o;
+                o.x = bf ? pack_bf2(f[j], f[j + 1]) : pack_h2(f[j], f[j + 1]);
+                o.y = bf ? pack_bf2(f[j + 2], f[j + 3]) : pack_h2(f[j + 2], f[j + 3]);
+                o.z = bf ? pack_bf2(f[j + 4], f[j + 5]) : pack_h2(f[j + 4], f[j + 5]);
+                o.w = bf ? pack_bf2(f[j + 6], f[j + 7]) : pack_h2(f[j + 6], f[j + 7]);
+                *reinterpret_cast<uint4*>(d + j) = o;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nn)
+                  d[j] = bf ? __bfloat16_as_ushort(__float2bfloat16_rn(f[j]))
+                            : __half_as_ushort(__float2half_rn(f[j]));
+            }
+            break;
+          }
+          case VOUT_F16_T: {
+            __half* d = reinterpret_cast<__half*>(p.out) + pix;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nn) d[(long long)(nb + j) * p.ld_out] = __float2half_rn(f[j]);
+            break;
+          }
+          default: {  // VOUT_F32_NCHW
+            float* d = reinterpret_cast<float*>(p.out) + pix;
+            const long long plane = (long long)p.H * p.W;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nn) d[(long long)(nb + j) * plane] = f[j];
+            break;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(&dempty[b]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// Pixel tile bw x bh (= 128, bw a power of two in [8, 128]) with the least
+// padded area for a W x H image (ties go to the wider tile).
+void pick_pixel_tile(int H, int W, int& bw, int& bh) {
+  long long best = -1;
+  for (int cand = 128; cand >= 8; cand /= 2) {
+    const int ch = 128 / cand;
+    const long long area = (long long)((W + cand - 1) / cand) * cand * ((H + ch - 1) / ch) * ch;
+    if (best < 0 || area < best) {
+      best = area;
+      bw = cand;
+      bh = ch;
+    }
+  }
+}
+
+// Output-channel tile: the smallest power of two >= N up to 128; for wider
+// N, 256 unless 128 fills the SMs in fewer equivalent waves.
+int pick_bn(int N, long long mtiles, int sms) {
+  if (N <= 16) return 16;
+  if (N <= 32) return 32;
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  auto cost = [&](int bn) {
+    const long long tiles = mtiles * ((N + bn - 1) / bn);
+    const long long waves = (tiles + sms - 1) / sms;
+    return (double)waves * (bn + 32);
+  };
+  return cost(128) < cost(256) ? 128 : 256;
+}
+
+}  // namespace vconv
+
+int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
+  using namespace vconv;
+  if (a.taps != 1 && a.taps != 9) return fail(BONSAI_ERR_ARG, "vae conv: taps must be 1 or 9");
+  if (a.H <= 0 || a.W <= 0 || a.cin <= 0 || a.N <= 0)
+    return fail(BONSAI_ERR_ARG, "vae conv: empty shape");
+  if ((a.ld_in & 7) != 0 || (a.w_ld & 7) != 0 || a.ld_in < a.cin)
+    return fail(BONSAI_ERR_ARG, "vae conv: leading dimensions must be multiples of 8 elements");
+  if ((reinterpret_cast<uintptr_t>(a.in) & 15) != 0 || (reinterpret_cast<uintptr_t>(a.w) & 15) != 0)
+    return fail(BONSAI_ERR_ARG, "vae conv: operands must be 16-byte aligned");
+  const int cin_blocks = (a.cin + BK - 1) / BK;
+  const int k_per_tap = a.taps == 1 ? 0 : a.k_per_tap;
+  if (a.taps == 9 && k_per_tap < cin_blocks * BK)
+    return fail(BONSAI_ERR_ARG, "vae conv: weight taps must be padded to 64 channels");
+  const long long k_total = a.taps == 1 ? a.cin : (long long)a.taps * k_per_tap;
+  if (k_total > a.w_ld) return fail(BONSAI_ERR_ARG, "vae conv: weight row shorter than K");
+
+  auto fn = gemm::get_encode_fn();
+  if (!fn) return fail(-5, "cuTensorMapEncodeTiled entry point unavailable");
+  int bw = 128, bh = 1;
+  pick_pixel_tile(a.H, a.W, bw, bh);
+  const int tiles_x = (a.W + bw - 1) / bw;
+  const long long mtiles = (long long)tiles_x * ((a.H + bh - 1) / bh);
+  const int sms = num_sms();
+  const int BN = a.bn > 0 ? a.bn : pick_bn(a.N, mtiles, sms);
+  if (BN % 16 != 0 || BN < 16 || BN > BN_MAX) return fail(BONSAI_ERR_ARG, "vae conv: bad BN");
+  const long long n_ntiles = (a.N + BN - 1) / BN;
+  if (mtiles * n_ntiles > 0x7FFFFFFFLL) return fail(BONSAI_ERR_ARG, "vae conv: too many tiles");
+
+  const CUtensorMapDataType dt =
+      a.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap amap, bmap;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)a.cin, (cuuint64_t)a.W, (cuuint64_t)a.H};
+    cuuint64_t strides[2] = {(cuuint64_t)a.ld_in * 2, (cuuint64_t)a.ld_in * 2 * a.W};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)bw, (cuuint32_t)bh};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(&amap, dt, 3, const_cast<void*>(a.in), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(-5, "vae conv: activation tensor map (code " + std::to_string((int)r) + ")");
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)std::max(a.N, a.w_rows)};
+    cuuint64_t strides[1] = {(cuuint64_t)a.w_ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BN};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(&bmap, dt, 2, const_cast<void*>(a.w), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(-5, "vae conv: weight tensor map (code " + std::to_string((int)r) + ")");
+  }
+
+  Params p{};
+  p.H = a.H;
+  p.W = a.W;
+  p.bw = bw;
+  p.bh = bh;
+  p.tiles_x = tiles_x;
+  p.n_ntiles = (int)n_ntiles;
+  p.num_tiles = (int)(mtiles * n_ntiles);
+  p.BN = BN;
+  p.taps = a.taps;
+  p.cin_blocks = cin_blocks;
+  p.k_per_tap = k_per_tap;
+  p.N = a.N;
+  p.bias = a.bias;
+  p.row_scale = a.row_scale;
+  p.resid = a.resid;
+  p.ld_resid = a.ld_resid;
+  p.out = a.out;
+  p.ld_out = a.ld_out;
+  p.out_mode = a.out_mode;
+  p.err = device_error_word();
+  const uint32_t idesc = make_idesc_f16(BM, BN, a.bf16 ? 1 : 0, 0, 0);
+
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "vae conv: smem attribute");
+    attr_set = true;
+  }
+  const int grid = (int)std::min<long long>(p.num_tiles, sms);
+  const double flop = 2.0 * a.H * a.W * (double)a.N * a.cin * a.taps;
+  ProfScope prof("vae_conv", flop, 0.0, st);
+  conv_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(amap, bmap, p, idesc);
+  return launch_status("vae conv_kernel launch");
+}
+
+}  // namespace bonsai

@@ -341,6 +341,49 @@ int bonsai_safetensors_list(const char* path, char* out, int cap);
 int bonsai_dit_sample(bonsai_dit_t m, float* latents, const float* txt, const float* pooled,
                       int n_steps, float* stats, void* stream);
 
+/* ------------------------------------------------------------------ VAE
+ * The Flux VAE decoder of the reference's bonsai_vae program
+ * (src/vae_decoder.cpp:281-547, graph src/vae_graph.cpp:174-212) on the
+ * device.  A decoder is created for one encoded-latent size h x w
+ * (128 channels, the reference's --H / --W) and decodes it to a
+ * 3 x 16h x 16w image of raw decoder values. */
+typedef struct bonsai_vae* bonsai_vae_t;
+
+/* Allocate a decoder with seeded synthetic weights (conv / linear weights
+ * N(0, 1/fan_in), norm scales 1 + N(0, 0.1), biases N(0, 0.05), BatchNorm
+ * mean N(0, 0.25) and var U(0.25, 4)); load real ones with
+ * bonsai_vae_load_safetensors.  Replaces load_vae_weights
+ * (src/vae_decoder.cpp:214-250) plus the activation context of :427-444. */
+int bonsai_vae_create(int latent_h, int latent_w, unsigned long long seed, bonsai_vae_t* out);
+int bonsai_vae_destroy(bonsai_vae_t v);
+/* Load flux2-vae.safetensors: every tensor load_vae_weights reads
+ * (post_quant_conv.*, decoder.conv_in.*, decoder.mid_block.*,
+ * decoder.up_blocks.<i>.*, decoder.conv_norm_out.*, decoder.conv_out.*) and
+ * bn.running_mean / bn.running_var (:353-373), PyTorch layouts, F32 (F16
+ * and BF16 are converted).  A missing tensor or a wrong shape returns
+ * BONSAI_ERR_ARG (the reference throws); tensors are set in order. */
+int bonsai_vae_load_safetensors(bonsai_vae_t v, const char* path);
+/* latent: device f32 [128][h][w] (the reference's --latent .bin layout);
+ * image: device f32 [3][16h][16w].  Inverse BatchNorm + 2x2 un-tiling
+ * (:402-421) then the decoder graph; asynchronous on stream. */
+int bonsai_vae_decode(bonsai_vae_t v, const float* latent, float* image, void* stream);
+/* The same with host buffers: copies in, decodes, copies out, synchronises. */
+int bonsai_vae_decode_host(bonsai_vae_t v, const float* host_latent, float* host_image,
+                           void* stream);
+/* chw_f32_to_hwc_u8 (src/vae_decoder.cpp:262-281) on the device: rgb[y][x][c]
+ * = clamp((int)(sigmoid(image[c][y][x]) * 255), 0, 255). */
+int bonsai_vae_rgb8(const float* image, int height, int width, unsigned char* rgb, void* stream);
+/* One stride-1 'same'-padded convolution of the decoder, ggml_conv_2d_direct
+ * (w, x, 1, 1, k/2, k/2, 1, 1) + bias [+ resid] as src/vae_graph.cpp uses it,
+ * on the tcgen05 implicit-GEMM kernel: x device NHWC [H][W][cin] f16 (bf16
+ * when x_bf16), cin % 8 == 0; w device f32 PyTorch layout [cout][cin][k][k]
+ * (k = 1 or 3, converted to x's type per call); bias [cout] and resid
+ * (NHWC f32 [H][W][cout]) optional; y device NHWC f32 [H][W][cout]. */
+int bonsai_conv2d_nhwc(const void* x, int H, int W, int cin, int x_bf16, const float* w, int cout,
+                       int k, const float* bias, const float* resid, float* y, void* stream);
+/* Output image size of a decoder (16h x 16w). */
+int bonsai_vae_info(bonsai_vae_t v, int* image_h, int* image_w);
+
 #ifdef __cplusplus
 }
 #endif
