@@ -606,6 +606,127 @@ def run_configs(args):
     return 0
 
 
+def vae_flops(lh: int, lw: int, folded: bool) -> float:
+    """FLOPs of one decode of a lh x lw encoded latent: convolutions 2*P*Cin*Cout*k^2
+    (folded = the upsampling convs as four 2x2 phase convolutions, as executed;
+    else 3x3 over the upsampled image, as the reference computes them), the
+    attention projections and products (4*S^2*C)."""
+    H0, W0 = 2 * lh, 2 * lw
+    P = H0 * W0
+    f = 2.0 * P * 32 * 32 + 2.0 * P * 32 * 512 * 9            # post_quant, conv_in
+    res = lambda p, ci, co: 2.0 * p * (ci * co * 9 + co * co * 9 + (ci * co if ci != co else 0))
+    f += 2 * res(P, 512, 512) + 4 * 2.0 * P * 512 * 512 + 4.0 * P * P * 512  # mid block
+    ins, outs = [512, 512, 512, 256], [512, 512, 256, 128]
+    for i in range(4):
+        f += res(P, ins[i], outs[i]) + 2 * res(P, outs[i], outs[i])
+        if i < 3:
+            f += 2.0 * P * outs[i] * outs[i] * (16 if folded else 36)
+            P *= 4
+    return f + 2.0 * P * 128 * 3 * 9
+
+
+def run_vae(args):
+    """--vae: the Flux VAE decoder (the stage after the denoise loop in the
+    reference's pipeline, src/vae_decoder.cpp + src/vae_graph.cpp) decoding a
+    64 x 64 x 128 encoded latent to a 1024^2 image on one GPU, synthetic
+    seeded weights.  value = device-timed ms per decode (latent resident);
+    e2e = bonsai_vae_decode_host (latent copied in, image copied out);
+    cpu_baseline = the f32 NumPy restatement of the reference's decoder
+    (oracle/vae_oracle.py; the reference's own ggml path is not in its tree)
+    on an 8 x 8 latent (128^2 image), scaled to the 1024^2 decode by FLOPs."""
+    import torch
+    import bonsai_b200 as bb
+    torch.cuda.init()
+    bb.init(0)
+    lh = lw = 64
+    K, W = args.steps, args.warmup
+    v = bb.Vae(lh, lw, seed=1234)
+    rng = np.random.default_rng(7)
+    lat_h = torch.from_numpy(rng.uniform(-1, 1, (128, lh, lw)).astype(np.float32)).pin_memory()
+    lat = lat_h.cuda()
+    img = torch.empty(3, 16 * lh, 16 * lw, device="cuda")
+    for _ in range(W):
+        v.decode(lat, img)
+    torch.cuda.synchronize()
+    assert bb.device_error() == 0
+    stream = torch.cuda.current_stream()
+    clocks = ClockSampler(0, os.environ.get("BONSAI_CLOCK_LOG"))
+    clocks.start()
+    bb.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        v.decode(lat, img)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = bb.launch_count()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / K
+    assert bb.device_error() == 0
+    bb.profile_start()
+    for _ in range(K):
+        v.decode(lat, img)
+    prof = bb.profile_stop()
+    finite = bb.count_nonfinite(img) == 0
+    lat_np = lat_h.numpy()
+    v.decode_host(lat_np)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(K):
+        out_np = v.decode_host(lat_np)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = f0.elapsed_time(f1) / K
+    pk = peaks()
+    convs = {k: e for k, e in prof.items() if k.startswith(("vae_conv", "vae_attn_gemm"))}
+    c_flop = sum(e["flop"] for e in convs.values())
+    c_ms = sum(e["ms"] for e in convs.values())
+    conv_tf = c_flop / (c_ms / 1e3) / 1e12
+    gn = prof.get("vae_gn_apply", {})
+    total = sum(e["ms"] for e in prof.values())
+    line = {
+        "metric": "ms/VAE decode @1024² (Flux VAE decoder, latent 128x64x64 -> 3x1024x1024)",
+        "value": round(ms, 3), "unit": "ms", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16/bf16 operands, f32 accumulate and residual",
+        "data": "synthetic (seeded weights, U(-1,1) latent)",
+        "config": {"workload": "Flux VAE decoder, 1024^2 image (src/vae_graph.cpp:174-212)",
+                   "latent": [128, lh, lw], "image": [3, 16 * lh, 16 * lw],
+                   "decode_tflop_reference_form": round(vae_flops(lh, lw, False) / 1e12, 3),
+                   "decode_tflop_executed": round(vae_flops(lh, lw, True) / 1e12, 3),
+                   "l2": "activations of 0.5-1 GB per tensor stream through HBM"},
+        "roofline": {"bound": "tensor", "kernel": "vae conv (implicit-GEMM tcgen05)",
+                     "achieved": round(conv_tf, 1), "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
+                     "frac": round(conv_tf / pk["bf16_sustained"], 4),
+                     "peak_kind": f"{pk['source']} sustained bf16", "traffic": None,
+                     "measured": "sum of executed conv/GEMM FLOPs / sum of their CUDA-event durations"},
+        "gn_apply_gbs": round(gn["bytes"] / (gn["ms"] / 1e3) / 1e9, 1) if gn else None,
+        "kernels_per_decode": {k: {"launches": e["launches"] / K, "ms": round(e["ms"] / K, 4),
+                                   "share": round(e["ms"] / total, 4)} for k, e in prof.items()},
+        "gpu_launches": launches, "clocks": clk,
+        "e2e": {"value": round(ms_e2e, 3), "unit": "ms", "h2d_bytes_per_step": 128 * lh * lw * 4,
+                "d2h_bytes_per_step": 3 * 256 * lh * lw * 4,
+                "output_finite": bool(finite and np.isfinite(out_np).all())},
+    }
+    v.close()
+    if not args.no_cpu_baseline:
+        from oracle import vae_oracle as vo
+        sys.path.insert(0, str(ROOT / "tests"))
+        from vae_weights import make_state_dict
+        sd = make_state_dict(1234)
+        s_lat = rng.uniform(-1, 1, (128, 8, 8)).astype(np.float32)
+        t0 = time.perf_counter()
+        vo.decode(sd, s_lat)
+        s_sec = time.perf_counter() - t0
+        scale = vae_flops(lh, lw, False) / vae_flops(8, 8, False)
+        line["cpu_baseline"] = {"value": round(s_sec * 1e3 * scale, 1), "unit": "ms",
+                                "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": f"NumPy f32 restatement, 8x8 latent (128^2 image) in "
+                                          f"{s_sec:.2f} s, scaled x{scale:.1f} by FLOPs"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -619,9 +740,19 @@ def main():
     ap.add_argument("--configs", action="store_true",
                     help="instead of the step: BASELINE configs 1-3, GPU vs the reference CPU "
                          "path, one JSON line per config")
+    ap.add_argument("--vae", action="store_true",
+                    help="instead of the step: the Flux VAE decoder at 1024^2 (the next "
+                         "pipeline stage), one JSON line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.vae:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference's VAE decoder runs on ggml, which its tree does not "
+                              "contain (empty llama.cpp submodule); see cpu_baseline of the --vae line"}))
+            return 0
+        return run_vae(args)
     if args.configs:
         return run_configs(args)
     if args.impl == "reference":

@@ -7,14 +7,21 @@
 // (:262-281).
 //
 // Layout: activations are NHWC.  The residual stream h is f32; every
-// convolution / linear reads 16-bit operands that the preceding memory-bound
-// kernel writes: GroupNorm + SiLU outputs (bounded by the normalisation) in
-// f16, the raw stream fed to the upsampler convs and the 1x1 shortcuts in
-// bf16 (its range is not bounded).  Accumulation is f32 in TMEM.
+// convolution / linear reads 16-bit operands: GroupNorm + SiLU outputs
+// (bounded by the normalisation) in f16, written by the GroupNorm kernel;
+// the raw stream fed to the upsampler convs and the 1x1 shortcuts in bf16
+// (its range is not bounded), written as a second output by the epilogue of
+// the convolution that produces it.  Accumulation is f32 in TMEM.
 // Convolutions, linears and the two attention products run on the tcgen05
-// implicit-GEMM kernel (vae_conv.cu); the attention is unfused (scores f32,
-// softmax numerators f16, 1/rowsum applied in the P.V epilogue) and walks the
-// queries in chunks so the score matrix stays bounded at large images.
+// implicit-GEMM kernel (vae_conv.cu).  Each GroupNorm's statistics are
+// partial sums written by the epilogue of the convolution that produces its
+// input, so a GroupNorm costs one read of its input.  The nearest 2x
+// upsample + 3x3 conv of the up blocks is computed as four 2x2 convolutions
+// of the low-resolution input (one per output pixel phase, weights folded at
+// load time), 16 instead of 36 taps per input pixel.  The attention is
+// unfused (scores f32, softmax numerators f16, 1/rowsum applied in the P.V
+// epilogue) and walks the queries in chunks so the score matrix stays
+// bounded at large images.
 #include "internal.cuh"
 #include "vae.cuh"
 #include "bonsai_cuda.h"
@@ -31,8 +38,9 @@ namespace vae {
 
 struct Conv {
   int cin = 0, cout = 0, taps = 1, cin_pad = 0, rows = 0;
+  int phases = 1;      // 4: the 3x3 conv after a nearest 2x upsample, folded to 2x2 phases
   bool bf16 = false;
-  void* w = nullptr;   // 16-bit [rows][taps][cin_pad]
+  void* w = nullptr;   // 16-bit [phases][rows][taps][cin_pad]
   float* b = nullptr;  // [rows], zero beyond cout
 };
 struct Norm {
@@ -79,15 +87,19 @@ struct bonsai_vae {
   Norm attn_norm, norm_out;
   // activations
   float* hbuf[2] = {nullptr, nullptr};
-  float* t = nullptr;
-  void* a16 = nullptr;
-  void* u16 = nullptr;
+  float* t = nullptr;     // conv1 output
+  float* scb = nullptr;   // shortcut output
+  void* a16 = nullptr;    // f16 GroupNorm output (conv input)
+  void* u16 = nullptr;    // bf16 copy of the stream before an upsampling conv
+  void* u16b = nullptr;   // bf16 copy of an upsampling conv's output (shortcut input)
+  float* stat_part = nullptr;  // GroupNorm partials [slots][32] float4
+  long long stat_cap = 0, stat_used = 0;
   __half *q = nullptr, *k = nullptr, *vt = nullptr, *o = nullptr, *P = nullptr;
   float* S = nullptr;
   float* rowinv = nullptr;
   long long qchunk = 0, ldS = 0, ldP = 0, ldV = 0;
-  double* gn_part = nullptr;
   float* gn_stat = nullptr;
+  double* gn_scratch = nullptr;
   float* staging = nullptr;  // f32 upload / generation scratch
   long long staging_elems = 0;
   float *in_lat = nullptr, *out_img = nullptr;  // device copies for decode_host
@@ -114,17 +126,18 @@ long long round_up(long long x, long long m) { return (x + m - 1) / m * m; }
 // A convolution weight [cout][cin][k][k] (or, linear = true, an nn.Linear
 // weight [cout][cin]) and its bias [cout].
 int make_conv(bonsai_vae* v, const std::string& name, Conv& c, int cin, int cout, int k,
-              bool bf16, int rows = 0, bool linear = false) {
+              bool bf16, int rows = 0, bool linear = false, bool upsampling = false) {
   c.cin = cin;
   c.cout = cout;
-  c.taps = k * k;
+  c.taps = upsampling ? 4 : k * k;
+  c.phases = upsampling ? 4 : 1;
   c.cin_pad = (int)round_up(cin, 64);
   c.rows = rows > 0 ? rows : cout;
   c.bf16 = bf16;
-  RC(valloc(v, &c.w, (size_t)c.rows * c.taps * c.cin_pad * 2));
+  RC(valloc(v, &c.w, (size_t)c.phases * c.rows * c.taps * c.cin_pad * 2));
   RC(valloc(v, reinterpret_cast<void**>(&c.b), (size_t)c.rows * 4));
   RC(cuda_status(cudaMemset(c.b, 0, (size_t)c.rows * 4), "vae: bias clear"));
-  const float stdv = 1.0f / std::sqrt((float)cin * c.taps);
+  const float stdv = 1.0f / std::sqrt((float)cin * k * k);
   Entry w{name + ".weight", K_CONV_W, {cout, cin, k, k}, &c, nullptr, 0.f, stdv};
   if (linear) w.shape = {cout, cin};
   v->reg.push_back(w);
@@ -156,6 +169,9 @@ int make_res(bonsai_vae* v, const std::string& p, Res& r, int cin, int cout) {
 int commit_entry(bonsai_vae* v, const Entry& e, const float* dev_src, cudaStream_t st) {
   switch (e.kind) {
     case K_CONV_W:
+      if (e.conv->phases == 4)
+        return launch_vae_pack_subpixel_weight(dev_src, e.conv->cout, e.conv->cin, e.conv->cin_pad,
+                                               e.conv->w, e.conv->bf16, st);
       return launch_vae_pack_weight(dev_src, e.conv->cout, e.conv->cin, e.conv->taps, e.conv->rows,
                                     e.conv->cin_pad, e.conv->w, e.conv->bf16, st);
     case K_CONV_B:
@@ -186,9 +202,16 @@ long long numel(const std::vector<long long>& s) {
   return n;
 }
 
+struct Extra {
+  const float* resid = nullptr;
+  long long ld_resid = 0;
+  int n_out = 0;         // output channels written (0 = cout)
+  bool stats = false;    // GroupNorm partials of the output -> v->stat_part
+  void* out2 = nullptr;  // bf16 copy of the output
+};
+
 int conv(bonsai_vae* v, const Conv& c, const void* in, long long ld_in, int H, int W, void* out,
-         long long ld_out, int mode, cudaStream_t st, const float* resid = nullptr,
-         long long ld_resid = 0, int n_out = 0) {
+         long long ld_out, int mode, cudaStream_t st, const Extra& x = Extra()) {
   VaeConvArgs a;
   a.in = in;
   a.ld_in = ld_in;
@@ -197,43 +220,58 @@ int conv(bonsai_vae* v, const Conv& c, const void* in, long long ld_in, int H, i
   a.cin = c.cin_pad;
   a.bf16 = c.bf16;
   a.taps = c.taps;
+  a.phases = c.phases;
   a.w = c.w;
   a.w_ld = (long long)c.taps * c.cin_pad;
   a.k_per_tap = c.cin_pad;
-  a.N = n_out > 0 ? n_out : c.cout;
+  a.N = x.n_out > 0 ? x.n_out : c.cout;
   a.w_rows = c.rows;
   a.bias = c.b;
-  a.resid = resid;
-  a.ld_resid = ld_resid;
+  a.resid = x.resid;
+  a.ld_resid = x.ld_resid;
   a.out = out;
   a.ld_out = ld_out;
   a.out_mode = mode;
-  (void)v;
+  a.out2 = x.out2;
+  a.ld_out2 = a.N;
+  if (x.stats) {
+    a.stats = v->stat_part;
+    a.stats_slots = v->stat_cap;
+    a.stats_slots_used = &v->stat_used;
+  }
   return launch_vae_conv(a, st);
 }
 
+// GroupNorm of x with the statistics the producing conv left in stat_part.
 int group_norm(bonsai_vae* v, const float* x, long long P, const Norm& n, bool silu, void* y,
-               bool bf16, cudaStream_t st) {
-  RC(launch_vae_gn_stats(x, P, n.c, v->gn_part, v->gn_stat, kGnEps, st));
-  return launch_vae_gn_apply(x, P, n.c, v->gn_stat, n.g, n.b, silu, y, bf16, st);
+               cudaStream_t st) {
+  RC(launch_vae_gn_finalize(v->stat_part, v->stat_used, kGnEps, v->gn_stat, v->gn_scratch, st));
+  return launch_vae_gn_apply(x, P, n.c, v->gn_stat, n.g, n.b, silu, y, false, st);
 }
 
-// build_resnet (src/vae_graph.cpp:44-76) on the stream buffer hbuf[cur].
-int resnet(bonsai_vae* v, const Res& r, int& cur, int H, int W, cudaStream_t st) {
+// build_resnet (src/vae_graph.cpp:44-76) on the stream buffer hbuf[cur];
+// copy_out: also write a bf16 copy of the result into u16 (the input of the
+// next upsampling conv).  With a shortcut, the block's input is also in u16b
+// as bf16 (written by the upsampling conv before it).
+int resnet(bonsai_vae* v, const Res& r, int& cur, int H, int W, bool copy_out, cudaStream_t st) {
   const long long P = (long long)H * W;
   float* x = v->hbuf[cur];
   const int ci = r.c1.cin, co = r.c1.cout;
-  RC(group_norm(v, x, P, r.n1, true, v->a16, false, st));
-  RC(conv(v, r.c1, v->a16, ci, H, W, v->t, co, VOUT_F32, st));
-  RC(group_norm(v, v->t, P, r.n2, true, v->a16, false, st));
-  if (r.has_sc) {
-    RC(launch_vae_cast(x, P * ci, v->u16, true, st));
-    RC(conv(v, r.sc, v->u16, ci, H, W, v->t, co, VOUT_F32, st));
-    RC(conv(v, r.c2, v->a16, co, H, W, v->hbuf[cur ^ 1], co, VOUT_F32, st, v->t, co));
-    cur ^= 1;
-    return 0;
-  }
-  return conv(v, r.c2, v->a16, co, H, W, x, co, VOUT_F32, st, x, co);
+  if (r.has_sc) RC(conv(v, r.sc, v->u16b, ci, H, W, v->scb, co, VOUT_F32, st));
+  RC(group_norm(v, x, P, r.n1, true, v->a16, st));
+  Extra e1;
+  e1.stats = true;
+  RC(conv(v, r.c1, v->a16, ci, H, W, v->t, co, VOUT_F32, st, e1));
+  RC(group_norm(v, v->t, P, r.n2, true, v->a16, st));
+  Extra e2;
+  e2.stats = true;
+  e2.resid = r.has_sc ? v->scb : x;
+  e2.ld_resid = co;
+  e2.out2 = copy_out ? v->u16 : nullptr;
+  float* out = r.has_sc ? v->hbuf[cur ^ 1] : x;
+  RC(conv(v, r.c2, v->a16, co, H, W, out, co, VOUT_F32, st, e2));
+  if (r.has_sc) cur ^= 1;
+  return 0;
 }
 
 // build_attention (src/vae_graph.cpp:97-166): one head over all H*W pixels.
@@ -241,7 +279,7 @@ int attention(bonsai_vae* v, int cur, int H, int W, cudaStream_t st) {
   const long long P = (long long)H * W;
   constexpr int C = 512;
   float* x = v->hbuf[cur];
-  RC(group_norm(v, x, P, v->attn_norm, false, v->a16, false, st));
+  RC(group_norm(v, x, P, v->attn_norm, false, v->a16, st));
   RC(conv(v, v->to_q, v->a16, C, H, W, v->q, C, VOUT_F16, st));
   RC(conv(v, v->to_k, v->a16, C, H, W, v->k, C, VOUT_F16, st));
   RC(conv(v, v->to_v, v->a16, C, H, W, v->vt, v->ldV, VOUT_F16_T, st));
@@ -279,7 +317,11 @@ int attention(bonsai_vae* v, int cur, int H, int W, cudaStream_t st) {
     pv.out_mode = VOUT_F16;
     RC(launch_vae_conv(pv, st));
   }
-  return conv(v, v->to_out, v->o, C, H, W, x, C, VOUT_F32, st, x, C);
+  Extra eo;
+  eo.stats = true;
+  eo.resid = x;
+  eo.ld_resid = C;
+  return conv(v, v->to_out, v->o, C, H, W, x, C, VOUT_F32, st, eo);
 }
 
 int decode(bonsai_vae* v, const float* latent, float* image, cudaStream_t st) {
@@ -287,24 +329,30 @@ int decode(bonsai_vae* v, const float* latent, float* image, cudaStream_t st) {
   RC(launch_vae_preprocess(latent, v->lat_h, v->lat_w, v->bn_mean, v->bn_std,
                            static_cast<__half*>(v->a16), st));
   // post_quant_conv writes all 64 padded channels (rows 32..63 are zero).
-  RC(conv(v, v->post_quant, v->a16, 64, H, W, v->u16, 64, VOUT_F16, st, nullptr, 0, 64));
+  Extra pq;
+  pq.n_out = 64;
+  RC(conv(v, v->post_quant, v->a16, 64, H, W, v->u16, 64, VOUT_F16, st, pq));
   int cur = 0;
-  RC(conv(v, v->conv_in, v->u16, 64, H, W, v->hbuf[0], 512, VOUT_F32, st));
-  RC(resnet(v, v->mid[0], cur, H, W, st));
+  Extra ci;
+  ci.stats = true;
+  RC(conv(v, v->conv_in, v->u16, 64, H, W, v->hbuf[0], 512, VOUT_F32, st, ci));
+  RC(resnet(v, v->mid[0], cur, H, W, false, st));
   RC(attention(v, cur, H, W, st));
-  RC(resnet(v, v->mid[1], cur, H, W, st));
+  RC(resnet(v, v->mid[1], cur, H, W, false, st));
   for (int i = 0; i < 4; ++i) {
-    for (int j = 0; j < 3; ++j) RC(resnet(v, v->up[i][j], cur, H, W, st));
+    for (int j = 0; j < 3; ++j) RC(resnet(v, v->up[i][j], cur, H, W, j == 2 && i < 3, st));
     if (i < 3) {
       const int C = kUpOut[i];
-      RC(launch_vae_upsample2(v->hbuf[cur], H, W, C, v->u16, true, st));
+      Extra eu;
+      eu.stats = true;
+      eu.out2 = v->up[i + 1][0].has_sc ? v->u16b : nullptr;
+      RC(conv(v, v->upconv[i], v->u16, C, H, W, v->hbuf[cur ^ 1], C, VOUT_F32, st, eu));
+      cur ^= 1;
       H *= 2;
       W *= 2;
-      RC(conv(v, v->upconv[i], v->u16, C, H, W, v->hbuf[cur ^ 1], C, VOUT_F32, st));
-      cur ^= 1;
     }
   }
-  RC(group_norm(v, v->hbuf[cur], (long long)H * W, v->norm_out, true, v->a16, false, st));
+  RC(group_norm(v, v->hbuf[cur], (long long)H * W, v->norm_out, true, v->a16, st));
   return conv(v, v->conv_out, v->a16, 128, H, W, image, 0, VOUT_F32_NCHW, st);
 }
 
@@ -356,7 +404,7 @@ int bonsai_vae_create(int latent_h, int latent_w, unsigned long long seed, bonsa
                   m->up[i][j], j == 0 ? kUpIn[i] : kUpOut[i], kUpOut[i]));
     if (i < 3)
       RC(make_conv(m, "decoder.up_blocks." + std::to_string(i) + ".upsamplers.0.conv",
-                   m->upconv[i], kUpOut[i], kUpOut[i], 3, true));
+                   m->upconv[i], kUpOut[i], kUpOut[i], 3, true, 0, false, true));
   }
   RC(make_norm(m, "decoder.conv_norm_out", m->norm_out, 128));
   RC(make_conv(m, "decoder.conv_out", m->conv_out, 128, 3, 3, false, 16));
@@ -368,8 +416,16 @@ int bonsai_vae_create(int latent_h, int latent_w, unsigned long long seed, bonsa
   RC(valloc(m, reinterpret_cast<void**>(&m->hbuf[0]), (size_t)P0 * 16384 * 4));
   RC(valloc(m, reinterpret_cast<void**>(&m->hbuf[1]), (size_t)P0 * 16384 * 4));
   RC(valloc(m, reinterpret_cast<void**>(&m->t), (size_t)P0 * 8192 * 4));
+  RC(valloc(m, reinterpret_cast<void**>(&m->scb), (size_t)P0 * 8192 * 4));
   RC(valloc(m, &m->a16, (size_t)P0 * 16384 * 2));
-  RC(valloc(m, &m->u16, (size_t)P0 * 16384 * 2));
+  RC(valloc(m, &m->u16, (size_t)P0 * 4096 * 2));
+  RC(valloc(m, &m->u16b, (size_t)P0 * 16384 * 2));
+  for (int l = 0; l < 4; ++l) {
+    const int hl = m->H0 << l, wl = m->W0 << l;
+    m->stat_cap = std::max(m->stat_cap, vae_conv_stat_slots(hl, wl, 1));
+    if (l < 3) m->stat_cap = std::max(m->stat_cap, vae_conv_stat_slots(hl, wl, 4));
+  }
+  RC(valloc(m, reinterpret_cast<void**>(&m->stat_part), (size_t)m->stat_cap * kStatGroups * 16));
   RC(valloc(m, reinterpret_cast<void**>(&m->q), (size_t)P0 * 512 * 2));
   RC(valloc(m, reinterpret_cast<void**>(&m->k), (size_t)P0 * 512 * 2));
   RC(valloc(m, reinterpret_cast<void**>(&m->o), (size_t)P0 * 512 * 2));
@@ -381,8 +437,8 @@ int bonsai_vae_create(int latent_h, int latent_w, unsigned long long seed, bonsa
   RC(valloc(m, reinterpret_cast<void**>(&m->S), (size_t)m->qchunk * m->ldS * 4));
   RC(valloc(m, reinterpret_cast<void**>(&m->P), (size_t)m->qchunk * m->ldP * 2));
   RC(valloc(m, reinterpret_cast<void**>(&m->rowinv), (size_t)m->qchunk * 4));
-  RC(valloc(m, reinterpret_cast<void**>(&m->gn_part), (size_t)kGnMaxBlocks * 64 * 8));
   RC(valloc(m, reinterpret_cast<void**>(&m->gn_stat), 64 * 4));
+  RC(valloc(m, reinterpret_cast<void**>(&m->gn_scratch), (size_t)kGnMergeBlocks * 32 * 4 * 8));
   long long most = 0;
   for (const Entry& e : m->reg) most = std::max(most, numel(e.shape));
   m->staging_elems = most;

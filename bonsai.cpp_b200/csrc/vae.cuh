@@ -42,24 +42,30 @@ struct VaeConvArgs {
   long long ld_out = 0;
   int out_mode = VOUT_F32;
   int bn = 0;  // output-channel tile (0 = automatic)
+  int phases = 1;
+  void* out2 = nullptr;
+  long long ld_out2 = 0;
+  float* stats = nullptr;
+  long long stats_slots = 0;
+  long long* stats_slots_used = nullptr;
 };
 int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st);
+// GroupNorm partial slots a launch over an H x W input grid writes (upper bound).
+long long vae_conv_stat_slots(int H, int W, int phases);
+constexpr int kStatGroups = 32;   // partial slot = 32 float4 {sum, M2, count, 0}
 
-// GroupNorm(32) statistics of an f32 NHWC tensor [pixels][C] (C in {128,
-// 256, 512, 1024}): per-block f64 partial sums into partials[nblk][32][2],
-// then mean_rstd[32][2] = {mean, 1/sqrt(var + eps)}.  nblk <= kGnMaxBlocks.
-constexpr int kGnMaxBlocks = 1184;
-int launch_vae_gn_stats(const float* x, long long pixels, int C, double* partials,
-                        float* mean_rstd, float eps, cudaStream_t st);
-// y = [silu]((x - mean_g) * rstd_g * gamma_c + beta_c), f32 -> f16 / bf16.
+// GroupNorm(32) statistics from the conv epilogue's partials (slots x 32
+// float4 {sum, M2 about the slot mean, count}): mean_rstd[32][2] = {mean,
+// 1/sqrt(var + eps)}, reduced in f64 in a fixed order (deterministic).
+// scratch: kGnMergeBlocks * 32 * 4 doubles.
+constexpr int kGnMergeBlocks = 148;
+int launch_vae_gn_finalize(const float* partials, long long slots, float eps, float* mean_rstd,
+                           double* scratch, cudaStream_t st);
+// y = [silu]((x - mean_g) * rstd_g * gamma_c + beta_c), f32 [pixels][C] ->
+// f16 / bf16 (C = 128, 256, 512 or 1024).
 int launch_vae_gn_apply(const float* x, long long pixels, int C, const float* mean_rstd,
                         const float* gamma, const float* beta, bool silu, void* y, bool y_bf16,
                         cudaStream_t st);
-// Nearest 2x upsample of f32 NHWC [H][W][C] into 16-bit [2H][2W][C].
-int launch_vae_upsample2(const float* x, int H, int W, int C, void* y, bool y_bf16,
-                         cudaStream_t st);
-// f32 -> 16-bit copy of n elements (n % 4 == 0).
-int launch_vae_cast(const float* x, long long n, void* y, bool y_bf16, cudaStream_t st);
 // Encoded latent f32 [128][h][w] -> f16 NHWC [2h][2w][64]: channel c < 32 of
 // pixel (2i + di, 2j + dj) = latent[4c + 2di + dj][i][j] * bn_std + bn_mean,
 // channels 32..63 zero.
@@ -73,6 +79,12 @@ int launch_vae_softmax(const float* S, long long ld_s, int rows, int cols, float
 // (zero rows >= cout and columns >= cin).
 int launch_vae_pack_weight(const float* src, int cout, int cin, int taps, int rows, int cin_pad,
                            void* dst, bool bf16, cudaStream_t st);
+// The 3x3 kernel src [cout][cin][3][3] f32 folded into the four 2x2 kernels
+// of conv3x3(upsample_nearest_2x(x)): dst 16-bit [4 phases][cout][4 taps][cin_pad],
+// phase 2a + b, tap 2ry + rx = the sum of src[ky][kx] over the 3x3 taps
+// that read input row offset ry + a - 1 and column offset rx + b - 1.
+int launch_vae_pack_subpixel_weight(const float* src, int cout, int cin, int cin_pad, void* dst,
+                                    bool bf16, cudaStream_t st);
 // Seeded synthetic values: dst[i] = mean + std * N(0,1) (uniform = false) or
 // mean + std * U[0,1) (uniform = true), from a counter-based hash of (seed, i).
 int launch_vae_fill(float* dst, long long n, unsigned long long seed, float mean, float std,

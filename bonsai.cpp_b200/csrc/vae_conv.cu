@@ -39,28 +39,31 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn();
 
 namespace vconv {
 
-constexpr int BM = 128;       // pixels per tile (MMA M)
+constexpr int BM = 128;       // pixels per MMA (M)
 constexpr int BN_MAX = 256;   // output channels per tile (MMA N)
 constexpr int BK = 64;        // input channels per pipeline stage
 constexpr int STAGES = 4;
-constexpr int A_STAGE = BM * BK * 2;      // 16 KB
-constexpr int B_STAGE = BN_MAX * BK * 2;  // 32 KB
+constexpr int A_BYTES = BM * BK * 2;          // one 128-pixel A box: 16 KB
+constexpr int STAGE_BYTES = A_BYTES + BN_MAX * BK * 2;  // + BN * 128 B of B: 48 KB
 constexpr int TMEM_COLS = 2 * BN_MAX;
 constexpr int WARP_TMA = 0;
 constexpr int WARP_MMA = 1;
 constexpr int WARP_EPI0 = 2;
 constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = (WARP_EPI0 + EPI_WARPS) * 32;
-constexpr int SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + 256;
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
 
 struct Params {
-  int H, W;                // image (output pixels H*W; the input has the same size)
-  int bw, bh, tiles_x;     // pixel tile bw x bh = 128
-  int n_ntiles, num_tiles;
+  int H, W;                // input grid (the output is H*S x W*S, S = 2 when phases = 4)
+  int bw, bh, tiles_x;     // 128-pixel tile bw x bh
+  int n_mtiles, n_ntiles, num_tiles;
+  int phases;              // 1, or 4: nearest 2x upsample folded into per-phase 2x2 weights
   int BN;                  // output channels per tile (multiple of 16, <= 256)
-  int taps;                // 1 or 9
+  int taps;                // taps per phase
+  int8_t tap_dy[9], tap_dx[9];
   int cin_blocks;          // 64-channel blocks per tap
   int k_per_tap;           // weight K offset between taps
+  int w_rows_phase;        // weight rows per phase
   int N;                   // output channels
   const float* bias;
   const float* row_scale;
@@ -69,6 +72,10 @@ struct Params {
   void* out;
   long long ld_out;
   int out_mode;
+  uint16_t* out2;          // optional bf16 copy of the output (NHWC, ld_out2)
+  long long ld_out2;
+  float4* stats;           // optional GroupNorm partials [slot][32] {sum, M2, count, 0}
+  int gw;                  // channels per group (N / 32) when stats
   int* err;
 };
 
@@ -81,15 +88,71 @@ __device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// GroupNorm partials of one 32-column chunk over the warp's 32 pixels: for
+// each group of GW columns, the sum and the sum of squared deviations from
+// the chunk's own mean (combined with Chan's formula by the finalize
+// kernel), and the element count.
+template <int GW>
+__device__ __forceinline__ void chunk_stats(const float (&f)[32], bool valid, float nvalid,
+                                            float4* dst, uint32_t lane) {
+  constexpr int NG = 32 / GW;
+  float s[NG], m2[NG];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    float a = 0.0f;
+#pragma unroll
+    for (int k = 0; k < GW; ++k) a += f[g * GW + k];
+    s[g] = warp_sum(valid ? a : 0.0f);
+  }
+  const float cnt = nvalid * GW;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const float mean = cnt > 0.0f ? s[g] / cnt : 0.0f;
+    float d = 0.0f;
+#pragma unroll
+    for (int k = 0; k < GW; ++k) {
+      const float e = f[g * GW + k] - mean;
+      d = fmaf(e, e, d);
+    }
+    m2[g] = warp_sum(valid ? d : 0.0f);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < NG; ++g) dst[g] = make_float4(s[g], m2[g], cnt, 0.0f);
+  }
+}
+
+struct TileCoord {
+  int phase, n0, mt;
+};
+__device__ __forceinline__ TileCoord tile_coord(const Params& p, int tile) {
+  TileCoord t;
+  const int nt = tile % p.n_ntiles;
+  const int r = tile / p.n_ntiles;
+  t.phase = r % p.phases;
+  t.mt = r / p.phases;
+  t.n0 = nt * p.BN;
+  return t;
+}
+__device__ __forceinline__ void unit_origin(const Params& p, int u, int& x0, int& y0) {
+  const int ty = u / p.tiles_x;
+  x0 = (u - ty * p.tiles_x) * p.bw;
+  y0 = ty * p.bh;
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     conv_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
                 const Params p, const uint32_t idesc) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* as = smem;
-  uint8_t* bs = smem + STAGES * A_STAGE;
-  uint64_t* full = reinterpret_cast<uint64_t*>(bs + STAGES * B_STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* dfull = empty + STAGES;
   uint64_t* dempty = dfull + 2;
@@ -127,18 +190,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (elect_one()) {
       tma_prefetch_desc(&amap);
       tma_prefetch_desc(&bmap);
-      const uint32_t stage_bytes = (uint32_t)(A_STAGE + p.BN * BK * 2);
+      const uint32_t stage_bytes = (uint32_t)(A_BYTES + p.BN * BK * 2);
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int m = tile / p.n_ntiles;
-        const int n0 = (tile - m * p.n_ntiles) * p.BN;
-        const int ty = m / p.tiles_x;
-        const int x0 = (m - ty * p.tiles_x) * p.bw;
-        const int y0 = ty * p.bh;
+        const TileCoord tc = tile_coord(p, tile);
+        const int a = tc.phase >> 1, bph = tc.phase & 1;
+        int x0, y0;
+        unit_origin(p, tc.mt, x0, y0);
+        const int brow = tc.phase * p.w_rows_phase + tc.n0;
         for (int t = 0; t < p.taps && ok; ++t) {
-          const int dy = p.taps == 9 ? t / 3 - 1 : 0;
-          const int dx = p.taps == 9 ? t % 3 - 1 : 0;
+          const int dy = p.tap_dy[t] + a, dx = p.tap_dx[t] + bph;
           for (int cb = 0; cb < p.cin_blocks; ++cb, ++it) {
             const int s = it % STAGES;
             const uint32_t ph = (it / STAGES) & 1;
@@ -146,9 +208,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               ok = false;
               break;
             }
+            uint8_t* st = smem + s * STAGE_BYTES;
             bar_arrive_expect_tx(&full[s], stage_bytes);
-            tma_load_3d(as + s * A_STAGE, &amap, &full[s], cb * BK, x0 + dx, y0 + dy);
-            tma_load_2d(bs + s * B_STAGE, &bmap, &full[s], t * p.k_per_tap + cb * BK, n0);
+            tma_load_3d(st, &amap, &full[s], cb * BK, x0 + dx, y0 + dy);
+            tma_load_2d(st + A_BYTES, &bmap, &full[s], t * p.k_per_tap + cb * BK, brow);
           }
         }
       }
@@ -179,12 +242,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t aaddr = smem_u32(as + s * A_STAGE);
-          const uint32_t baddr = smem_u32(bs + s * B_STAGE);
+          const uint32_t saddr = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
           for (int k16 = 0; k16 < BK / 16; ++k16) {
-            const uint64_t adesc = make_smem_desc(aaddr + k16 * 32, 16, 1024);
-            const uint64_t bdesc = make_smem_desc(baddr + k16 * 32, 16, 1024);
+            const uint64_t adesc = make_smem_desc(saddr + k16 * 32, 16, 1024);
+            const uint64_t bdesc = make_smem_desc(saddr + A_BYTES + k16 * 32, 16, 1024);
             mma_ss(d_tmem, adesc, bdesc, idesc, (ks | k16) != 0 ? 1u : 0u);
           }
           tc_commit(&empty[s]);
@@ -209,110 +271,135 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int eh = (warp - WARP_EPI0) >> 2;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int nch = (p.BN + 31) / 32;
+    const int S = p.phases == 4 ? 2 : 1;
+    const long long Wout = (long long)p.W * S;
+    const long long plane = (long long)p.H * S * Wout;
     uint32_t lt = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
-      const int m = tile / p.n_ntiles;
-      const int n0 = (tile - m * p.n_ntiles) * p.BN;
-      const int ty = m / p.tiles_x;
-      const int x0 = (m - ty * p.tiles_x) * p.bw;
-      const int y0 = ty * p.bh;
+      const TileCoord tc = tile_coord(p, tile);
       const uint32_t b = lt & 1;
       const uint32_t dph = (lt >> 1) & 1;
       const bool good = wait_bar(&dfull[b], dph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, good)) break;  // tcgen05.ld is warp-collective
       tc_fence_after();
 
-      const int ml = q * 32 + (int)lane;
-      const int px = x0 + ml % p.bw;
-      const int py = y0 + ml / p.bw;
-      const bool valid = px < p.W && py < p.H;
-      const long long pix = (long long)py * p.W + px;
-      const float rs = (p.row_scale && valid) ? p.row_scale[pix] : 1.0f;
+      {
+        int x0, y0;
+        unit_origin(p, tc.mt, x0, y0);
+        const int ml = q * 32 + (int)lane;
+        const int px = x0 + ml % p.bw;
+        const int py = y0 + ml / p.bw;
+        const bool valid = px < p.W && py < p.H;
+        const long long pix =
+            (long long)(py * S + (tc.phase >> 1)) * Wout + (long long)px * S + (tc.phase & 1);
+        const float rs = (p.row_scale && valid) ? p.row_scale[pix] : 1.0f;
+        const float nvalid = (float)__popc(__ballot_sync(0xffffffffu, valid));
+        float4* srow =
+            p.stats ? p.stats + ((size_t)(tc.mt * p.phases + tc.phase) * 4 + q) * kStatGroups : nullptr;
 
-      for (int c = eh; c < nch; c += 2) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_base + b * BN_MAX + c * 32, v);
-        tmem_wait_ld();
-        const int nb = n0 + c * 32;
-        const int nn = min(min(32, p.BN - c * 32), p.N - nb);
-        if (!valid || nn <= 0) continue;
-        float f[32];
+        for (int c = eh; c < nch; c += 2) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_base + b * BN_MAX + c * 32, v);
+          tmem_wait_ld();
+          const int nb = tc.n0 + c * 32;
+          const int nn = min(min(32, p.BN - c * 32), p.N - nb);
+          if (nn <= 0) continue;
+          float f[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * rs;
-        if (p.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < nn) f[j] += p.bias[nb + j];
-        }
-        const bool vec = nn == 32;
-        if (p.resid) {
-          const float* r = p.resid + pix * p.ld_resid + nb;
-          if (vec && (p.ld_resid & 3) == 0) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 o = *reinterpret_cast<const float4*>(r + j);
-              f[j] += o.x;
-              f[j + 1] += o.y;
-              f[j + 2] += o.z;
-              f[j + 3] += o.w;
-            }
-          } else {
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * rs;
+          if (p.bias) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (j < nn) f[j] += r[j];
+              if (j < nn) f[j] += p.bias[nb + j];
           }
-        }
-        switch (p.out_mode) {
-          case VOUT_F32: {
-            float* d = reinterpret_cast<float*>(p.out) + pix * p.ld_out + nb;
-            if (vec && (p.ld_out & 3) == 0) {
+          const bool vec = nn == 32;
+          if (p.resid && valid) {
+            const float* r = p.resid + pix * p.ld_resid + nb;
+            if (vec && (p.ld_resid & 3) == 0) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(d + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < nn) d[j] = f[j];
-            }
-            break;
-          }
-          case VOUT_F16:
-          case VOUT_BF16: {
-            const bool bf = p.out_mode == VOUT_BF16;
-            uint16_t* d = reinterpret_cast<uint16_t*>(p.out) + pix * p.ld_out + nb;
-            if (vec && (p.ld_out & 7) == 0) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 o;
-                o.x = bf ? pack_bf2(f[j], f[j + 1]) : pack_h2(f[j], f[j + 1]);
-                o.y = bf ? pack_bf2(f[j + 2], f[j + 3]) : pack_h2(f[j + 2], f[j + 3]);
-                o.z = bf ? pack_bf2(f[j + 4], f[j + 5]) : pack_h2(f[j + 4], f[j + 5]);
-                o.w = bf ? pack_bf2(f[j + 6], f[j + 7]) : pack_h2(f[j + 6], f[j + 7]);
-                *reinterpret_cast<uint4*>(d + j) = o;
+              for (int j = 0; j < 32; j += 4) {
+                const float4 o = *reinterpret_cast<const float4*>(r + j);
+                f[j] += o.x;
+                f[j + 1] += o.y;
+                f[j + 2] += o.z;
+                f[j + 3] += o.w;
               }
             } else {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
-                if (j < nn)
-                  d[j] = bf ? __bfloat16_as_ushort(__float2bfloat16_rn(f[j]))
-                            : __half_as_ushort(__float2half_rn(f[j]));
+                if (j < nn) f[j] += r[j];
             }
-            break;
           }
-          case VOUT_F16_T: {
-            __half* d = reinterpret_cast<__half*>(p.out) + pix;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < nn) d[(long long)(nb + j) * p.ld_out] = __float2half_rn(f[j]);
-            break;
+          if (srow) {  // warp-uniform; N == 32 * gw so every chunk is full
+            float4* dst = srow + nb / p.gw;
+            if (p.gw == 16) chunk_stats<16>(f, valid, nvalid, dst, lane);
+            else if (p.gw == 8) chunk_stats<8>(f, valid, nvalid, dst, lane);
+            else chunk_stats<4>(f, valid, nvalid, dst, lane);
           }
-          default: {  // VOUT_F32_NCHW
-            float* d = reinterpret_cast<float*>(p.out) + pix;
-            const long long plane = (long long)p.H * p.W;
+          if (!valid) continue;
+          if (p.out2) {
+            uint16_t* d = p.out2 + pix * p.ld_out2 + nb;
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < nn) d[(long long)(nb + j) * plane] = f[j];
-            break;
+            for (int j = 0; j < 32; j += 8) {
+              uint4 o;
+              o.x = pack_bf2(f[j], f[j + 1]);
+              o.y = pack_bf2(f[j + 2], f[j + 3]);
+              o.z = pack_bf2(f[j + 4], f[j + 5]);
+              o.w = pack_bf2(f[j + 6], f[j + 7]);
+              *reinterpret_cast<uint4*>(d + j) = o;
+            }
+          }
+          switch (p.out_mode) {
+            case VOUT_F32: {
+              float* d = reinterpret_cast<float*>(p.out) + pix * p.ld_out + nb;
+              if (vec && (p.ld_out & 3) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                  *reinterpret_cast<float4*>(d + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < nn) d[j] = f[j];
+              }
+              break;
+            }
+            case VOUT_F16:
+            case VOUT_BF16: {
+              const bool bf = p.out_mode == VOUT_BF16;
+              uint16_t* d = reinterpret_cast<uint16_t*>(p.out) + pix * p.ld_out + nb;
+              if (vec && (p.ld_out & 7) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                  uint4 o;
+                  o.x = bf ? pack_bf2(f[j], f[j + 1]) : pack_h2(f[j], f[j + 1]);
+                  o.y = bf ? pack_bf2(f[j + 2], f[j + 3]) : pack_h2(f[j + 2], f[j + 3]);
+                  o.z = bf ? pack_bf2(f[j + 4], f[j + 5]) : pack_h2(f[j + 4], f[j + 5]);
+                  o.w = bf ? pack_bf2(f[j + 6], f[j + 7]) : pack_h2(f[j + 6], f[j + 7]);
+                  *reinterpret_cast<uint4*>(d + j) = o;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < nn)
+                    d[j] = bf ? __bfloat16_as_ushort(__float2bfloat16_rn(f[j]))
+                              : __half_as_ushort(__float2half_rn(f[j]));
+              }
+              break;
+            }
+            case VOUT_F16_T: {
+              __half* d = reinterpret_cast<__half*>(p.out) + pix;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nn) d[(long long)(nb + j) * p.ld_out] = __float2half_rn(f[j]);
+              break;
+            }
+            default: {  // VOUT_F32_NCHW
+              float* d = reinterpret_cast<float*>(p.out) + pix;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nn) d[(long long)(nb + j) * plane] = f[j];
+              break;
+            }
           }
         }
       }
@@ -329,7 +416,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-// Pixel tile bw x bh (= 128, bw a power of two in [8, 128]) with the least
+// 128-pixel unit tile bw x bh (bw a power of two in [8, 128]) with the least
 // padded area for a W x H image (ties go to the wider tile).
 void pick_pixel_tile(int H, int W, int& bw, int& bh) {
   long long best = -1;
@@ -346,13 +433,13 @@ void pick_pixel_tile(int H, int W, int& bw, int& bh) {
 
 // Output-channel tile: the smallest power of two >= N up to 128; for wider
 // N, 256 unless 128 fills the SMs in fewer equivalent waves.
-int pick_bn(int N, long long mtiles, int sms) {
+int pick_bn(int N, long long units, int sms) {
   if (N <= 16) return 16;
   if (N <= 32) return 32;
   if (N <= 64) return 64;
   if (N <= 128) return 128;
   auto cost = [&](int bn) {
-    const long long tiles = mtiles * ((N + bn - 1) / bn);
+    const long long tiles = units * ((N + bn - 1) / bn);
     const long long waves = (tiles + sms - 1) / sms;
     return (double)waves * (bn + 32);
   };
@@ -361,9 +448,20 @@ int pick_bn(int N, long long mtiles, int sms) {
 
 }  // namespace vconv
 
+long long vae_conv_stat_slots(int H, int W, int phases) {
+  int bw = 128, bh = 1;
+  vconv::pick_pixel_tile(H, W, bw, bh);
+  const long long units = (long long)((W + bw - 1) / bw) * ((H + bh - 1) / bh);
+  return units * 4 * (phases == 4 ? 4 : 1);
+}
+
 int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   using namespace vconv;
-  if (a.taps != 1 && a.taps != 9) return fail(BONSAI_ERR_ARG, "vae conv: taps must be 1 or 9");
+  const int phases = a.phases == 4 ? 4 : 1;
+  if (a.phases != 1 && a.phases != 4) return fail(BONSAI_ERR_ARG, "vae conv: phases must be 1 or 4");
+  if (phases == 1 && a.taps != 1 && a.taps != 9)
+    return fail(BONSAI_ERR_ARG, "vae conv: taps must be 1 or 9");
+  if (phases == 4 && a.taps != 4) return fail(BONSAI_ERR_ARG, "vae conv: the upsampling form has 4 taps");
   if (a.H <= 0 || a.W <= 0 || a.cin <= 0 || a.N <= 0)
     return fail(BONSAI_ERR_ARG, "vae conv: empty shape");
   if ((a.ld_in & 7) != 0 || (a.w_ld & 7) != 0 || a.ld_in < a.cin)
@@ -372,22 +470,32 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
     return fail(BONSAI_ERR_ARG, "vae conv: operands must be 16-byte aligned");
   const int cin_blocks = (a.cin + BK - 1) / BK;
   const int k_per_tap = a.taps == 1 ? 0 : a.k_per_tap;
-  if (a.taps == 9 && k_per_tap < cin_blocks * BK)
+  if (a.taps > 1 && k_per_tap < cin_blocks * BK)
     return fail(BONSAI_ERR_ARG, "vae conv: weight taps must be padded to 64 channels");
   const long long k_total = a.taps == 1 ? a.cin : (long long)a.taps * k_per_tap;
   if (k_total > a.w_ld) return fail(BONSAI_ERR_ARG, "vae conv: weight row shorter than K");
+  if (a.stats && (a.N % 32 != 0 || (a.N / 32 != 4 && a.N / 32 != 8 && a.N / 32 != 16)))
+    return fail(BONSAI_ERR_ARG, "vae conv: GroupNorm statistics need N in {128, 256, 512}");
+  if (a.out2 && (a.N % 32 != 0 || (a.ld_out2 & 7) != 0 ||
+                 (reinterpret_cast<uintptr_t>(a.out2) & 15) != 0))
+    return fail(BONSAI_ERR_ARG, "vae conv: the bf16 copy needs N % 32 == 0 and 16-byte rows");
 
   auto fn = gemm::get_encode_fn();
   if (!fn) return fail(-5, "cuTensorMapEncodeTiled entry point unavailable");
   int bw = 128, bh = 1;
   pick_pixel_tile(a.H, a.W, bw, bh);
   const int tiles_x = (a.W + bw - 1) / bw;
-  const long long mtiles = (long long)tiles_x * ((a.H + bh - 1) / bh);
+  const long long units = (long long)tiles_x * ((a.H + bh - 1) / bh);
   const int sms = num_sms();
-  const int BN = a.bn > 0 ? a.bn : pick_bn(a.N, mtiles, sms);
+  const int BN = a.bn > 0 ? a.bn : pick_bn(a.N, units * phases, sms);
   if (BN % 16 != 0 || BN < 16 || BN > BN_MAX) return fail(BONSAI_ERR_ARG, "vae conv: bad BN");
+  const long long n_mtiles = units;
   const long long n_ntiles = (a.N + BN - 1) / BN;
-  if (mtiles * n_ntiles > 0x7FFFFFFFLL) return fail(BONSAI_ERR_ARG, "vae conv: too many tiles");
+  const long long num_tiles = n_mtiles * phases * n_ntiles;
+  if (num_tiles > 0x7FFFFFFFLL) return fail(BONSAI_ERR_ARG, "vae conv: too many tiles");
+  if (a.stats && n_mtiles * phases * 4 > a.stats_slots)
+    return fail(BONSAI_ERR_ARG, "vae conv: GroupNorm partial buffer too small");
+  const int w_rows_phase = std::max(a.N, a.w_rows);
 
   const CUtensorMapDataType dt =
       a.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -403,7 +511,7 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
     if (r != CUDA_SUCCESS) return fail(-5, "vae conv: activation tensor map (code " + std::to_string((int)r) + ")");
   }
   {
-    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)std::max(a.N, a.w_rows)};
+    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)w_rows_phase * phases};
     cuuint64_t strides[1] = {(cuuint64_t)a.w_ld * 2};
     cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BN};
     cuuint32_t estr[2] = {1, 1};
@@ -419,12 +527,29 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   p.bw = bw;
   p.bh = bh;
   p.tiles_x = tiles_x;
+  p.n_mtiles = (int)n_mtiles;
   p.n_ntiles = (int)n_ntiles;
-  p.num_tiles = (int)(mtiles * n_ntiles);
+  p.num_tiles = (int)num_tiles;
+  p.phases = phases;
   p.BN = BN;
   p.taps = a.taps;
+  for (int t = 0; t < 9; ++t) {
+    // 3x3: offsets -1..1; 2x2 upsampling phases: base offsets -1..0 (+ the
+    // phase bit in the kernel); 1x1: 0.
+    if (a.taps == 9) {
+      p.tap_dy[t] = (int8_t)(t / 3 - 1);
+      p.tap_dx[t] = (int8_t)(t % 3 - 1);
+    } else if (a.taps == 4) {
+      p.tap_dy[t] = (int8_t)((t >> 1) - 1);
+      p.tap_dx[t] = (int8_t)((t & 1) - 1);
+    } else {
+      p.tap_dy[t] = 0;
+      p.tap_dx[t] = 0;
+    }
+  }
   p.cin_blocks = cin_blocks;
   p.k_per_tap = k_per_tap;
+  p.w_rows_phase = w_rows_phase;
   p.N = a.N;
   p.bias = a.bias;
   p.row_scale = a.row_scale;
@@ -433,6 +558,10 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   p.out = a.out;
   p.ld_out = a.ld_out;
   p.out_mode = a.out_mode;
+  p.out2 = static_cast<uint16_t*>(a.out2);
+  p.ld_out2 = a.ld_out2;
+  p.stats = reinterpret_cast<float4*>(a.stats);
+  p.gw = a.N / 32;
   p.err = device_error_word();
   const uint32_t idesc = make_idesc_f16(BM, BN, a.bf16 ? 1 : 0, 0, 0);
 
@@ -443,11 +572,17 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return cuda_status(e, "vae conv: smem attribute");
     attr_set = true;
   }
-  const int grid = (int)std::min<long long>(p.num_tiles, sms);
-  const double flop = 2.0 * a.H * a.W * (double)a.N * a.cin * a.taps;
-  ProfScope prof("vae_conv", flop, 0.0, st);
+  const int grid = (int)std::min<long long>(num_tiles, sms);
+  const double flop = 2.0 * a.H * a.W * phases * (double)a.N * a.cin * a.taps;
+  const char* kind = phases == 4 ? "vae_conv_up2x"
+                     : a.taps == 9 ? (BN == 128 ? "vae_conv3x3_n128" : "vae_conv3x3")
+                     : a.H == 1     ? "vae_attn_gemm"
+                                    : "vae_conv1x1";
+  ProfScope prof(kind, flop, 0.0, st);
   conv_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(amap, bmap, p, idesc);
-  return launch_status("vae conv_kernel launch");
+  if (int rc = launch_status("vae conv_kernel launch")) return rc;
+  if (a.stats_slots_used) *a.stats_slots_used = n_mtiles * phases * 4;
+  return 0;
 }
 
 }  // namespace bonsai

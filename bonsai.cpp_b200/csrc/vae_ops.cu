@@ -1,7 +1,9 @@
 // Memory-bound kernels of the Flux VAE decoder (src/vae_graph.cpp,
-// src/vae_decoder.cpp): GroupNorm statistics and GroupNorm + SiLU
-// application, nearest 2x upsampling, the latent preprocessing, the
-// attention softmax, weight packing and seeded synthetic weights.  All work
+// src/vae_decoder.cpp): the GroupNorm statistics finalize (the partial sums
+// come from the convolution epilogue) and GroupNorm + SiLU application, the
+// latent preprocessing, the attention softmax, weight packing (including the
+// 3x3 kernels folded for the upsampling convolutions) and seeded synthetic
+// weights.  All work
 // on NHWC tensors with vectorised 16-byte loads and grid-stride loops sized
 // to the SM count.
 #include "internal.cuh"
@@ -23,121 +25,108 @@ __device__ __forceinline__ uint2 pack4(float a, float b, float c, float d, bool 
   return o;
 }
 
-// Block b sums rows [b*rows_per_blk, ...) of x[pixels][C]: thread t owns the
-// 4 channels (t % (C/4))*4.. of every (256 / (C/4))-th row; the 8 threads of
-// a group (C/128 float4 columns x 1024/C row phases) are combined in f64.
-__global__ void gn_stats_kernel(const float* __restrict__ x, long long pixels, int C,
-                                long long rows_per_blk, double* __restrict__ part) {
-  const int c4n = C / 4;
-  const int rpp = 256 / c4n;
-  const int col4 = threadIdx.x % c4n;
-  const int r0 = threadIdx.x / c4n;
-  const long long row_begin = (long long)blockIdx.x * rows_per_blk;
-  const long long row_end = min(pixels, row_begin + rows_per_blk);
-  double s = 0.0, ss = 0.0;
-  for (long long r = row_begin + r0; r < row_end; r += rpp) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(x + r * C) + col4);
-    const float a = (v.x + v.y) + (v.z + v.w);
-    const float b = fmaf(v.x, v.x, v.y * v.y) + fmaf(v.z, v.z, v.w * v.w);
-    s += (double)a;
-    ss += (double)b;
+constexpr int kGnMergeWarps = 8;
+
+// Stage 1: block b reduces slots b*8 + w + k*(gridDim.x*8) (warp w, lane =
+// group; one coalesced 512-byte row per slot) into f64 sums of
+// {count, sum, M2, sum^2 / count}, combined over its warps in warp order.
+__global__ void __launch_bounds__(32 * kGnMergeWarps)
+    gn_merge_kernel(const float4* __restrict__ part, long long slots, double* __restrict__ out) {
+  const int g = threadIdx.x % 32;
+  const int w = threadIdx.x / 32;
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  for (long long i = (long long)blockIdx.x * kGnMergeWarps + w; i < slots;
+       i += (long long)gridDim.x * kGnMergeWarps) {
+    const float4 v = part[i * kStatGroups + g];
+    if (v.z > 0.0f) {
+      acc[0] += v.z;
+      acc[1] += v.x;
+      acc[2] += v.y;
+      acc[3] += (double)v.x * ((double)v.x / v.z);
+    }
   }
-  __shared__ double sh[2][256];
-  sh[0][threadIdx.x] = s;
-  sh[1][threadIdx.x] = ss;
+  __shared__ double sh[kGnMergeWarps][32][4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) sh[w][g][k] = acc[k];
   __syncthreads();
-  if (threadIdx.x < 32) {
-    const int g = threadIdx.x;
-    const int cpg4 = c4n / 32;
-    double a = 0.0, b = 0.0;
-    for (int r = 0; r < rpp; ++r)
-      for (int k = 0; k < cpg4; ++k) {
-        const int idx = r * c4n + g * cpg4 + k;
-        a += sh[0][idx];
-        b += sh[1][idx];
-      }
-    part[((long long)blockIdx.x * 32 + g) * 2] = a;
-    part[((long long)blockIdx.x * 32 + g) * 2 + 1] = b;
+  if (w == 0) {
+    for (int j = 1; j < kGnMergeWarps; ++j)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[k] += sh[j][g][k];
+    double* o = out + ((long long)blockIdx.x * 32 + g) * 4;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = acc[k];
   }
 }
 
-// Warp g folds group g's partials in a fixed order (deterministic).
-__global__ void gn_finalize_kernel(const double* __restrict__ part, int nblk, double count,
-                                   float eps, float* __restrict__ mean_rstd) {
+// Stage 2: warp g sums group g's block results (lane-strided, then a fixed
+// shuffle tree).  With N = count, S = sum: mean = S / N and
+// M2 = sum_k M2_k + sum_k n_k mean_k^2 - N mean^2 (the scatter of the slot
+// means about the mean; f64 keeps the cancellation harmless).
+__global__ void gn_merge_final_kernel(const double* __restrict__ in, int nblk, float eps,
+                                      float* __restrict__ mean_rstd) {
   const int g = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  double a = 0.0, b = 0.0;
-  for (int i = lane; i < nblk; i += 32) {
-    a += part[((long long)i * 32 + g) * 2];
-    b += part[((long long)i * 32 + g) * 2 + 1];
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int b = lane; b < nblk; b += 32) {
+    const double* r = in + ((long long)b * 32 + g) * 4;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] += r[k];
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    b += __shfl_xor_sync(0xffffffffu, b, o);
-  }
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], o);
   if (lane == 0) {
-    const double mean = a / count;
-    const double var = fmax(b / count - mean * mean, 0.0);
+    const double n = acc[0];
+    const double mean = n > 0.0 ? acc[1] / n : 0.0;
+    const double m2 = acc[2] + acc[3] - (n > 0.0 ? acc[1] * mean : 0.0);
+    const double var = n > 0.0 ? fmax(m2 / n, 0.0) : 0.0;
     mean_rstd[2 * g] = (float)mean;
     mean_rstd[2 * g + 1] = (float)(1.0 / sqrt(var + (double)eps));
   }
 }
 
-__global__ void gn_apply_kernel(const float* __restrict__ x, long long n4, int C,
-                                const float* __restrict__ mean_rstd,
-                                const float* __restrict__ gamma, const float* __restrict__ beta,
-                                int silu, uint2* __restrict__ y, int bf) {
-  __shared__ float st[64];
-  if (threadIdx.x < 64) st[threadIdx.x] = mean_rstd[threadIdx.x];
-  __syncthreads();
+// Thread t owns the 4 channels (t % (C/4))*4.. for every (256/(C/4))-th row
+// of its block's row range, so its group statistics and affine terms are
+// loaded once; four rows are in flight per iteration.
+__global__ void __launch_bounds__(256, 4)
+    gn_apply_kernel(const float* __restrict__ x, long long pixels, int C,
+                    long long rows_per_blk, const float* __restrict__ mean_rstd,
+                    const float* __restrict__ gamma, const float* __restrict__ beta, int silu,
+                    uint2* __restrict__ y, int bf) {
   const int c4n = C / 4;
-  const int cpg = C / 32;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % c4n) * 4;
-    const int g = c / cpg;
-    const float mean = st[2 * g], rstd = st[2 * g + 1];
-    const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
-    const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma + c));
-    const float4 be = __ldg(reinterpret_cast<const float4*>(beta + c));
-    float o[4] = {(v.x - mean) * rstd * ga.x + be.x, (v.y - mean) * rstd * ga.y + be.y,
-                  (v.z - mean) * rstd * ga.z + be.z, (v.w - mean) * rstd * ga.w + be.w};
+  const int rpp = 256 / c4n;
+  const int col4 = threadIdx.x % c4n;
+  const int r0 = threadIdx.x / c4n;
+  const int c = col4 * 4;
+  const int g = c / (C / 32);
+  const float mean = mean_rstd[2 * g], rstd = mean_rstd[2 * g + 1];
+  const float4 ga = __ldg(reinterpret_cast<const float4*>(gamma + c));
+  const float4 be = __ldg(reinterpret_cast<const float4*>(beta + c));
+  const float sc[4] = {rstd * ga.x, rstd * ga.y, rstd * ga.z, rstd * ga.w};
+  const float sh[4] = {be.x, be.y, be.z, be.w};
+  const long long row_begin = (long long)blockIdx.x * rows_per_blk;
+  const long long row_end = min(pixels, row_begin + rows_per_blk);
+  const float4* xin = reinterpret_cast<const float4*>(x);
+  auto emit = [&](long long r, float4 v) {
+    float o[4] = {(v.x - mean) * sc[0] + sh[0], (v.y - mean) * sc[1] + sh[1],
+                  (v.z - mean) * sc[2] + sh[2], (v.w - mean) * sc[3] + sh[3]};
     if (silu) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) o[k] = o[k] / (1.0f + __expf(-o[k]));
+      for (int k = 0; k < 4; ++k) o[k] = __fdividef(o[k], 1.0f + __expf(-o[k]));
     }
-    y[i] = pack4(o[0], o[1], o[2], o[3], bf != 0);
+    y[r * c4n + col4] = pack4(o[0], o[1], o[2], o[3], bf != 0);
+  };
+  long long r = row_begin + r0;
+  for (; r + 3 * rpp < row_end; r += 4 * rpp) {
+    float4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = __ldg(xin + (r + k * rpp) * c4n + col4);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) emit(r + k * rpp, v[k]);
   }
-}
-
-__global__ void upsample2_kernel(const float* __restrict__ x, int H, int W, int C,
-                                 uint2* __restrict__ y, int bf) {
-  const int c4n = C / 4;
-  const long long n4 = (long long)H * W * c4n;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c4 = (int)(i % c4n);
-    const long long pix = i / c4n;
-    const int yy = (int)(pix / W), xx = (int)(pix % W);
-    const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
-    const uint2 o = pack4(v.x, v.y, v.z, v.w, bf != 0);
-    const long long W2 = 2LL * W;
-    const long long base = ((2LL * yy) * W2 + 2LL * xx) * c4n + c4;
-    y[base] = o;
-    y[base + c4n] = o;
-    y[base + W2 * c4n] = o;
-    y[base + W2 * c4n + c4n] = o;
-  }
-}
-
-__global__ void cast_kernel(const float* __restrict__ x, long long n4, uint2* __restrict__ y,
-                            int bf) {
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-       i += (long long)gridDim.x * blockDim.x) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
-    y[i] = pack4(v.x, v.y, v.z, v.w, bf != 0);
-  }
+  for (; r < row_end; r += rpp) emit(r, __ldg(xin + r * c4n + col4));
 }
 
 __global__ void preprocess_kernel(const float* __restrict__ lat, int h, int w,
@@ -245,6 +234,37 @@ __global__ void pack_weight_kernel(const float* __restrict__ src, int cout, int 
   }
 }
 
+// Rows of 3x3 taps feeding 2x2 tap r of phase a: a = 0: {0}, {1, 2};
+// a = 1: {0, 1}, {2} (nearest upsampling repeats each input row twice).
+__device__ __forceinline__ void fold_range(int a, int r, int& lo, int& hi) {
+  lo = (a == 0) ? (r == 0 ? 0 : 1) : (r == 0 ? 0 : 2);
+  hi = (a == 0) ? (r == 0 ? 0 : 2) : (r == 0 ? 1 : 2);
+}
+
+__global__ void pack_subpixel_kernel(const float* __restrict__ src, int cout, int cin,
+                                     int cin_pad, long long total, uint16_t* __restrict__ dst,
+                                     int bf) {
+  const long long per_phase = (long long)cout * 4 * cin_pad;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int phase = (int)(i / per_phase);
+    const long long rem = i - phase * per_phase;
+    const int n = (int)(rem / (4 * cin_pad));
+    const int rem2 = (int)(rem - (long long)n * 4 * cin_pad);
+    const int t = rem2 / cin_pad, c = rem2 % cin_pad;
+    float v = 0.0f;
+    if (c < cin) {
+      int ylo, yhi, xlo, xhi;
+      fold_range(phase >> 1, t >> 1, ylo, yhi);
+      fold_range(phase & 1, t & 1, xlo, xhi);
+      const float* w = src + ((long long)n * cin + c) * 9;
+      for (int ky = ylo; ky <= yhi; ++ky)
+        for (int kx = xlo; kx <= xhi; ++kx) v += w[ky * 3 + kx];
+    }
+    dst[i] = to16(v, bf != 0);
+  }
+}
+
 __device__ __forceinline__ unsigned long long splitmix64(unsigned long long z) {
   z += 0x9E3779B97F4A7C15ull;
   z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
@@ -275,52 +295,33 @@ int grid_for(long long work, int threads) {
 
 }  // namespace vops
 
-int launch_vae_gn_stats(const float* x, long long pixels, int C, double* partials,
-                        float* mean_rstd, float eps, cudaStream_t st) {
-  if (C < 128 || C > 1024 || (256 % (C / 4)) != 0 || pixels <= 0)
-    return fail(BONSAI_ERR_ARG, "vae group norm: C must be 128, 256, 512 or 1024");
-  const int rpp = 256 / (C / 4);
-  const long long passes = (pixels + rpp - 1) / rpp;
-  const int nblk = (int)std::min<long long>(passes, kGnMaxBlocks);
-  const long long rows_per_blk = ((pixels + nblk - 1) / nblk + rpp - 1) / rpp * rpp;
-  const int used = (int)((pixels + rows_per_blk - 1) / rows_per_blk);
-  {
-    ProfScope prof("vae_gn_stats", 0.0, (double)pixels * C * 4, st);
-    vops::gn_stats_kernel<<<used, 256, 0, st>>>(x, pixels, C, rows_per_blk, partials);
-  }
-  if (int rc = launch_status("vae gn_stats_kernel launch")) return rc;
-  vops::gn_finalize_kernel<<<1, 1024, 0, st>>>(partials, used, (double)pixels * (C / 32), eps,
-                                               mean_rstd);
-  return launch_status("vae gn_finalize_kernel launch");
+int launch_vae_gn_finalize(const float* partials, long long slots, float eps, float* mean_rstd,
+                           double* scratch, cudaStream_t st) {
+  const long long want = (slots + 4 * vops::kGnMergeWarps - 1) / (4 * vops::kGnMergeWarps);
+  const int nblk = (int)std::max<long long>(1, std::min<long long>(want, kGnMergeBlocks));
+  ProfScope prof("vae_gn_stats", 0.0, (double)slots * kStatGroups * 16, st);
+  vops::gn_merge_kernel<<<nblk, 32 * vops::kGnMergeWarps, 0, st>>>(
+      reinterpret_cast<const float4*>(partials), slots, scratch);
+  if (int rc = launch_status("vae gn_merge_kernel launch")) return rc;
+  vops::gn_merge_final_kernel<<<1, 32 * kStatGroups, 0, st>>>(scratch, nblk, eps, mean_rstd);
+  return launch_status("vae gn_merge_final_kernel launch");
 }
 
 int launch_vae_gn_apply(const float* x, long long pixels, int C, const float* mean_rstd,
                         const float* gamma, const float* beta, bool silu, void* y, bool y_bf16,
                         cudaStream_t st) {
-  if (C % 32 != 0 || (C / 32) % 4 != 0) return fail(BONSAI_ERR_ARG, "vae group norm: C % 128");
-  const long long n4 = pixels * C / 4;
+  if (C < 128 || C > 1024 || 256 % (C / 4) != 0 || C % 4 != 0 || pixels <= 0)
+    return fail(BONSAI_ERR_ARG, "vae group norm: C must be 128, 256, 512 or 1024");
+  const int rpp = 256 / (C / 4);
+  const long long want_blocks = (long long)num_sms() * 8;
+  long long rows_per_blk = (pixels + want_blocks - 1) / want_blocks;
+  rows_per_blk = std::max<long long>(rpp, (rows_per_blk + rpp - 1) / rpp * rpp);
+  const long long blocks = (pixels + rows_per_blk - 1) / rows_per_blk;
   ProfScope prof("vae_gn_apply", 0.0, (double)pixels * C * 6, st);
-  vops::gn_apply_kernel<<<vops::grid_for(n4, 256), 256, 0, st>>>(
-      x, n4, C, mean_rstd, gamma, beta, silu ? 1 : 0, reinterpret_cast<uint2*>(y), y_bf16 ? 1 : 0);
+  vops::gn_apply_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, pixels, C, rows_per_blk, mean_rstd,
+                                                         gamma, beta, silu ? 1 : 0,
+                                                         reinterpret_cast<uint2*>(y), y_bf16 ? 1 : 0);
   return launch_status("vae gn_apply_kernel launch");
-}
-
-int launch_vae_upsample2(const float* x, int H, int W, int C, void* y, bool y_bf16,
-                         cudaStream_t st) {
-  if (C % 4 != 0) return fail(BONSAI_ERR_ARG, "vae upsample: C % 4");
-  const long long n4 = (long long)H * W * C / 4;
-  ProfScope prof("vae_upsample2", 0.0, (double)H * W * C * 12, st);
-  vops::upsample2_kernel<<<vops::grid_for(n4, 256), 256, 0, st>>>(
-      x, H, W, C, reinterpret_cast<uint2*>(y), y_bf16 ? 1 : 0);
-  return launch_status("vae upsample2_kernel launch");
-}
-
-int launch_vae_cast(const float* x, long long n, void* y, bool y_bf16, cudaStream_t st) {
-  if (n % 4 != 0) return fail(BONSAI_ERR_ARG, "vae cast: n % 4");
-  ProfScope prof("vae_cast", 0.0, (double)n * 6, st);
-  vops::cast_kernel<<<vops::grid_for(n / 4, 256), 256, 0, st>>>(
-      x, n / 4, reinterpret_cast<uint2*>(y), y_bf16 ? 1 : 0);
-  return launch_status("vae cast_kernel launch");
 }
 
 int launch_vae_preprocess(const float* latent, int h, int w, const float* bn_mean,
@@ -348,6 +349,14 @@ int launch_vae_pack_weight(const float* src, int cout, int cin, int taps, int ro
   vops::pack_weight_kernel<<<vops::grid_for(total, 256), 256, 0, st>>>(
       src, cout, cin, taps, total, cin_pad, reinterpret_cast<uint16_t*>(dst), bf16 ? 1 : 0);
   return launch_status("vae pack_weight_kernel launch");
+}
+
+int launch_vae_pack_subpixel_weight(const float* src, int cout, int cin, int cin_pad, void* dst,
+                                    bool bf16, cudaStream_t st) {
+  const long long total = 4LL * cout * 4 * cin_pad;
+  vops::pack_subpixel_kernel<<<vops::grid_for(total, 256), 256, 0, st>>>(
+      src, cout, cin, cin_pad, total, reinterpret_cast<uint16_t*>(dst), bf16 ? 1 : 0);
+  return launch_status("vae pack_subpixel_kernel launch");
 }
 
 int launch_vae_fill(float* dst, long long n, unsigned long long seed, float mean, float std,
