@@ -8,22 +8,32 @@
 //
 //   out[pix][n] = sum_tap sum_c in[pix + offset(tap)][c] * w[n][tap][c]
 //
-// One CTA (persistent, one per SM) computes 128 pixels x BN output channels
-// per tile with tcgen05.mma.cta_group::1.kind::f16 (M = 128, N = BN <= 256,
-// f32 accumulators in TMEM, two of them so the epilogue of one tile overlaps
-// the next tile's MMAs).  The 128 pixels are a bw x bh rectangle of the
-// image; for each tap the TMA warp loads the rectangle shifted by the tap's
-// offset as one 3-D box {64 channels, bw, bh} of the NHWC tensor.  Pixels
-// outside the image come back as zeros from the TMA's out-of-bounds fill,
-// which is exactly the convolution's zero padding; the box lands in shared
-// memory as 128 rows of 128 bytes in the 128-byte-swizzled K-major layout
-// the MMA reads.  The weight tile {64, BN} of w[n][tap*Cin + c] comes by a
-// 2-D TMA load.  A plain GEMM is the 1x1 case over a 1-row "image".
+// Two forms share the code (template parameter kPair):
+//  * the CTA-pair kernel (default): a cluster of two CTAs on the two SMs of a
+//    TPC computes 256 pixels x BN output channels per tile with
+//    tcgen05.mma.cta_group::2 (M = 256).  Each CTA loads its own 128-pixel
+//    unit and half of the weight tile (BN/2 rows) into its shared memory;
+//    the even CTA issues the MMAs and each CTA's TMEM receives its 128
+//    pixels x BN.  Per SM and k-step that reads 16 KB of activations + BN/2
+//    x 128 B of weights, against 16 KB + BN x 128 B for one CTA alone -- the
+//    shared-memory bandwidth that bounds a 128 x 128 tile.
+//  * the single-CTA kernel: 128 pixels x BN per tile (cta_group::1).
+// Both are persistent with f32 accumulators in TMEM (two of them, so the
+// epilogue of one tile overlaps the next tile's MMAs).  The 128 pixels of a
+// unit are a bw x bh rectangle of the image; for each tap the TMA warp loads
+// the rectangle shifted by the tap's offset as one 3-D box {64 channels, bw,
+// bh} of the NHWC tensor.  Pixels outside the image come back as zeros from
+// the TMA's out-of-bounds fill, which is exactly the convolution's zero
+// padding; the box lands in shared memory as 128 rows of 128 bytes in the
+// 128-byte-swizzled K-major layout the MMA reads.  The weight tile {64, rows}
+// of w[n][tap*Cin + c] comes by a 2-D TMA load.  A plain GEMM is the 1x1
+// case over a 1-row "image".  No load uses cluster multicast.
 //
-// The epilogue (8 warps) reads the accumulators with tcgen05.ld (one pixel
-// per thread), optionally scales by a per-pixel factor, adds the bias and an
-// f32 residual, and writes f32 / f16 / bf16 NHWC, an f16 transposed
-// [n][pixel] tensor, or f32 NCHW (the decoder's final image).
+// The epilogue (8 warps per CTA) reads the accumulators with tcgen05.ld (one
+// pixel per thread), optionally scales by a per-pixel factor, adds the bias
+// and an f32 residual, writes f32 / f16 / bf16 NHWC, an f16 transposed
+// [n][pixel] tensor or f32 NCHW (the decoder's final image), and optionally
+// a bf16 copy of the output and GroupNorm partial statistics.
 #include "internal.cuh"
 #include "ptx.cuh"
 #include "vae.cuh"
@@ -31,6 +41,8 @@
 
 #include <cudaTypedefs.h>
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 namespace bonsai {
 namespace gemm {
@@ -39,24 +51,30 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn();
 
 namespace vconv {
 
-constexpr int BM = 128;       // pixels per MMA (M)
+constexpr int BM = 128;       // pixels per CTA (MMA M per CTA)
 constexpr int BN_MAX = 256;   // output channels per tile (MMA N)
 constexpr int BK = 64;        // input channels per pipeline stage
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;          // one 128-pixel A box: 16 KB
-constexpr int STAGE_BYTES = A_BYTES + BN_MAX * BK * 2;  // + BN * 128 B of B: 48 KB
+constexpr int A_BYTES = BM * BK * 2;  // one 128-pixel A box: 16 KB
 constexpr int TMEM_COLS = 2 * BN_MAX;
 constexpr int WARP_TMA = 0;
 constexpr int WARP_MMA = 1;
 constexpr int WARP_EPI0 = 2;
 constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = (WARP_EPI0 + EPI_WARPS) * 32;
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+
+template <bool kPair>
+struct Cfg {
+  static constexpr int B_BYTES = (kPair ? BN_MAX / 2 : BN_MAX) * BK * 2;  // weight rows per CTA
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;                    // 32 / 48 KB
+  static constexpr int STAGES = kPair ? 6 : 4;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+};
 
 struct Params {
   int H, W;                // input grid (the output is H*S x W*S, S = 2 when phases = 4)
-  int bw, bh, tiles_x;     // 128-pixel tile bw x bh
-  int n_mtiles, n_ntiles, num_tiles;
+  int bw, bh, tiles_x;     // 128-pixel unit bw x bh
+  int units;               // units of the input grid
+  int n_mtiles, n_ntiles, num_tiles;  // m-tiles: units (single) or unit pairs (pair)
   int phases;              // 1, or 4: nearest 2x upsample folded into per-phase 2x2 weights
   int BN;                  // output channels per tile (multiple of 16, <= 256)
   int taps;                // taps per phase
@@ -96,8 +114,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // GroupNorm partials of one 32-column chunk over the warp's 32 pixels: for
 // each group of GW columns, the sum and the sum of squared deviations from
-// the chunk's own mean (combined with Chan's formula by the finalize
-// kernel), and the element count.
+// the chunk's own mean (combined by launch_vae_gn_finalize), and the
+// element count.
 template <int GW>
 __device__ __forceinline__ void chunk_stats(const float (&f)[32], bool valid, float nvalid,
                                             float4* dst, uint32_t lane) {
@@ -146,15 +164,122 @@ __device__ __forceinline__ void unit_origin(const Params& p, int u, int& x0, int
   y0 = ty * p.bh;
 }
 
+// One 32-column chunk of the epilogue: scale, bias, residual, statistics,
+// stores.  Warp-collective (the statistics shuffle); `valid` is per lane.
+__device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (&v)[32], int nb,
+                                               int nn, bool valid, long long pix, float rs,
+                                               float nvalid, float4* srow, long long plane,
+                                               uint32_t lane) {
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * rs;
+  if (p.bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nn) f[j] += p.bias[nb + j];
+  }
+  const bool vec = nn == 32;
+  if (p.resid && valid) {
+    const float* r = p.resid + pix * p.ld_resid + nb;
+    if (vec && (p.ld_resid & 3) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 o = *reinterpret_cast<const float4*>(r + j);
+        f[j] += o.x;
+        f[j + 1] += o.y;
+        f[j + 2] += o.z;
+        f[j + 3] += o.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nn) f[j] += r[j];
+    }
+  }
+  if (srow) {  // warp-uniform; N == 32 * gw so every chunk is full
+    float4* dst = srow + nb / p.gw;
+    if (p.gw == 16) chunk_stats<16>(f, valid, nvalid, dst, lane);
+    else if (p.gw == 8) chunk_stats<8>(f, valid, nvalid, dst, lane);
+    else chunk_stats<4>(f, valid, nvalid, dst, lane);
+  }
+  if (!valid) return;
+  if (p.out2) {
+    uint16_t* d = p.out2 + pix * p.ld_out2 + nb;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 o;
+      o.x = pack_bf2(f[j], f[j + 1]);
+      o.y = pack_bf2(f[j + 2], f[j + 3]);
+      o.z = pack_bf2(f[j + 4], f[j + 5]);
+      o.w = pack_bf2(f[j + 6], f[j + 7]);
+      *reinterpret_cast<uint4*>(d + j) = o;
+    }
+  }
+  switch (p.out_mode) {
+    case VOUT_F32: {
+      float* d = reinterpret_cast<float*>(p.out) + pix * p.ld_out + nb;
+      if (vec && (p.ld_out & 3) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4*>(d + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < nn) d[j] = f[j];
+      }
+      break;
+    }
+    case VOUT_F16:
+    case VOUT_BF16: {
+      const bool bf = p.out_mode == VOUT_BF16;
+      uint16_t* d = reinterpret_cast<uint16_t*>(p.out) + pix * p.ld_out + nb;
+      if (vec && (p.ld_out & 7) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 o;
+          o.x = bf ? pack_bf2(f[j], f[j + 1]) : pack_h2(f[j], f[j + 1]);
+          o.y = bf ? pack_bf2(f[j + 2], f[j + 3]) : pack_h2(f[j + 2], f[j + 3]);
+          o.z = bf ? pack_bf2(f[j + 4], f[j + 5]) : pack_h2(f[j + 4], f[j + 5]);
+          o.w = bf ? pack_bf2(f[j + 6], f[j + 7]) : pack_h2(f[j + 6], f[j + 7]);
+          *reinterpret_cast<uint4*>(d + j) = o;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < nn)
+            d[j] = bf ? __bfloat16_as_ushort(__float2bfloat16_rn(f[j]))
+                      : __half_as_ushort(__float2half_rn(f[j]));
+      }
+      break;
+    }
+    case VOUT_F16_T: {
+      __half* d = reinterpret_cast<__half*>(p.out) + pix;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nn) d[(long long)(nb + j) * p.ld_out] = __float2half_rn(f[j]);
+      break;
+    }
+    default: {  // VOUT_F32_NCHW
+      float* d = reinterpret_cast<float*>(p.out) + pix;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nn) d[(long long)(nb + j) * plane] = f[j];
+      break;
+    }
+  }
+}
+
+template <bool kPair>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     conv_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
                 const Params p, const uint32_t idesc) {
+  using C = Cfg<kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* dfull = empty + STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* dfull = empty + C::STAGES;
   uint64_t* dempty = dfull + 2;
   uint64_t* drain = dempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -162,56 +287,76 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x / 32;
   const uint32_t lane = lane_id();
+  // Pair: rank 0 issues the MMAs; the cluster walks the tiles.  Single: the CTA.
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const int first = kPair ? (int)cluster_id_x() : (int)blockIdx.x;
+  const int stride = kPair ? (int)cluster_count_x() : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       bar_init(&full[s], 1);
       bar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       bar_init(&dfull[b], 1);
-      bar_init(&dempty[b], EPI_WARPS);
+      bar_init(&dempty[b], (kPair ? 2 : 1) * EPI_WARPS);
     }
     bar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == WARP_MMA) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair) cluster_sync_all();  // barrier inits and TMEM of both CTAs visible
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int ksteps = p.taps * p.cin_blocks;
+  const int rows_per_cta = kPair ? p.BN / 2 : p.BN;
 
   if (warp == WARP_TMA) {
     if (elect_one()) {
       tma_prefetch_desc(&amap);
       tma_prefetch_desc(&bmap);
-      const uint32_t stage_bytes = (uint32_t)(A_BYTES + p.BN * BK * 2);
+      const uint32_t cta_bytes = (uint32_t)(A_BYTES + rows_per_cta * BK * 2);
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = first; tile < p.num_tiles && ok; tile += stride) {
         const TileCoord tc = tile_coord(p, tile);
         const int a = tc.phase >> 1, bph = tc.phase & 1;
         int x0, y0;
-        unit_origin(p, tc.mt, x0, y0);
-        const int brow = tc.phase * p.w_rows_phase + tc.n0;
+        unit_origin(p, kPair ? 2 * tc.mt + (int)rank : tc.mt, x0, y0);
+        const int brow = tc.phase * p.w_rows_phase + tc.n0 + (int)rank * rows_per_cta;
         for (int t = 0; t < p.taps && ok; ++t) {
           const int dy = p.tap_dy[t] + a, dx = p.tap_dx[t] + bph;
           for (int cb = 0; cb < p.cin_blocks; ++cb, ++it) {
-            const int s = it % STAGES;
-            const uint32_t ph = (it / STAGES) & 1;
+            const int s = it % C::STAGES;
+            const uint32_t ph = (it / C::STAGES) & 1;
             if (!wait_bar(&empty[s], ph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
               ok = false;
               break;
             }
-            uint8_t* st = smem + s * STAGE_BYTES;
-            bar_arrive_expect_tx(&full[s], stage_bytes);
-            tma_load_3d(st, &amap, &full[s], cb * BK, x0 + dx, y0 + dy);
-            tma_load_2d(st + A_BYTES, &bmap, &full[s], t * p.k_per_tap + cb * BK, brow);
+            uint8_t* st = smem + s * C::STAGE_BYTES;
+            const int kcol = t * p.k_per_tap + cb * BK;
+            if constexpr (kPair) {
+              // Both CTAs' loads count on the even CTA's barrier.
+              if (rank == 0) bar_arrive_expect_tx(&full[s], 2 * cta_bytes);
+              const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+              tma_load_3d_pair(st, &amap, fb, cb * BK, x0 + dx, y0 + dy);
+              tma_load_2d_pair(st + A_BYTES, &bmap, fb, kcol, brow);
+            } else {
+              bar_arrive_expect_tx(&full[s], cta_bytes);
+              tma_load_3d(st, &amap, &full[s], cb * BK, x0 + dx, y0 + dy);
+              tma_load_2d(st + A_BYTES, &bmap, &full[s], kcol, brow);
+            }
           }
         }
       }
@@ -223,38 +368,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == WARP_MMA) {
     if (elect_one()) {
-      uint32_t it = 0, lt = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++lt) {
-        const uint32_t b = lt & 1;
-        const uint32_t dph = (lt >> 1) & 1;
-        if (!wait_bar(&dempty[b], dph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem + b * BN_MAX;
-        for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          if (!wait_bar(&full[s], ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
+      if (rank == 0) {
+        uint32_t it = 0, lt = 0;
+        bool ok = true;
+        for (int tile = first; tile < p.num_tiles && ok; tile += stride, ++lt) {
+          const uint32_t b = lt & 1;
+          const uint32_t dph = (lt >> 1) & 1;
+          if (!wait_bar(&dempty[b], dph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t saddr = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t d_tmem = tmem + b * BN_MAX;
+          for (int ks = 0; ks < ksteps; ++ks, ++it) {
+            const int s = it % C::STAGES;
+            const uint32_t ph = (it / C::STAGES) & 1;
+            if (!wait_bar(&full[s], ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t saddr = smem_u32(smem + s * C::STAGE_BYTES);
 #pragma unroll
-          for (int k16 = 0; k16 < BK / 16; ++k16) {
-            const uint64_t adesc = make_smem_desc(saddr + k16 * 32, 16, 1024);
-            const uint64_t bdesc = make_smem_desc(saddr + A_BYTES + k16 * 32, 16, 1024);
-            mma_ss(d_tmem, adesc, bdesc, idesc, (ks | k16) != 0 ? 1u : 0u);
+            for (int k16 = 0; k16 < BK / 16; ++k16) {
+              const uint64_t adesc = make_smem_desc(saddr + k16 * 32, 16, 1024);
+              const uint64_t bdesc = make_smem_desc(saddr + A_BYTES + k16 * 32, 16, 1024);
+              if constexpr (kPair)
+                mma_ss_pair(d_tmem, adesc, bdesc, idesc, (ks | k16) != 0 ? 1u : 0u);
+              else
+                mma_ss(d_tmem, adesc, bdesc, idesc, (ks | k16) != 0 ? 1u : 0u);
+            }
+            if constexpr (kPair) tc_commit_pair(&empty[s], 0x3);
+            else tc_commit(&empty[s]);
           }
-          tc_commit(&empty[s]);
+          if (!ok) break;
+          if constexpr (kPair) tc_commit_pair(&dfull[b], 0x3);
+          else tc_commit(&dfull[b]);
         }
-        if (!ok) break;
-        tc_commit(&dfull[b]);
+        if constexpr (kPair) tc_commit_pair(drain, 0x3);
+        else tc_commit(drain);
       }
-      tc_commit(drain);
+      // Wait until every MMA has completed (the pair's commit arrives on the
+      // drain barrier of both CTAs).
       const uint32_t da = smem_u32(drain);
       const unsigned long long t0 = globaltimer_ns();
       while (!bar_try_wait(da, 0)) {
@@ -274,8 +429,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int S = p.phases == 4 ? 2 : 1;
     const long long Wout = (long long)p.W * S;
     const long long plane = (long long)p.H * S * Wout;
+    const uint32_t dempty_lead = kPair ? mapa_shared(smem_u32(&dempty[0]), 0) : 0u;
     uint32_t lt = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
+    for (int tile = first; tile < p.num_tiles; tile += stride, ++lt) {
       const TileCoord tc = tile_coord(p, tile);
       const uint32_t b = lt & 1;
       const uint32_t dph = (lt >> 1) & 1;
@@ -283,136 +439,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!__all_sync(0xffffffffu, good)) break;  // tcgen05.ld is warp-collective
       tc_fence_after();
 
-      {
-        int x0, y0;
-        unit_origin(p, tc.mt, x0, y0);
-        const int ml = q * 32 + (int)lane;
-        const int px = x0 + ml % p.bw;
-        const int py = y0 + ml / p.bw;
-        const bool valid = px < p.W && py < p.H;
-        const long long pix =
-            (long long)(py * S + (tc.phase >> 1)) * Wout + (long long)px * S + (tc.phase & 1);
-        const float rs = (p.row_scale && valid) ? p.row_scale[pix] : 1.0f;
-        const float nvalid = (float)__popc(__ballot_sync(0xffffffffu, valid));
-        float4* srow =
-            p.stats ? p.stats + ((size_t)(tc.mt * p.phases + tc.phase) * 4 + q) * kStatGroups : nullptr;
-
-        for (int c = eh; c < nch; c += 2) {
-          uint32_t v[32];
-          tmem_ld32(tmem + lane_base + b * BN_MAX + c * 32, v);
-          tmem_wait_ld();
-          const int nb = tc.n0 + c * 32;
-          const int nn = min(min(32, p.BN - c * 32), p.N - nb);
-          if (nn <= 0) continue;
-          float f[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * rs;
-          if (p.bias) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < nn) f[j] += p.bias[nb + j];
-          }
-          const bool vec = nn == 32;
-          if (p.resid && valid) {
-            const float* r = p.resid + pix * p.ld_resid + nb;
-            if (vec && (p.ld_resid & 3) == 0) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                const float4 o = *reinterpret_cast<const float4*>(r + j);
-                f[j] += o.x;
-                f[j + 1] += o.y;
-                f[j + 2] += o.z;
-                f[j + 3] += o.w;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < nn) f[j] += r[j];
-            }
-          }
-          if (srow) {  // warp-uniform; N == 32 * gw so every chunk is full
-            float4* dst = srow + nb / p.gw;
-            if (p.gw == 16) chunk_stats<16>(f, valid, nvalid, dst, lane);
-            else if (p.gw == 8) chunk_stats<8>(f, valid, nvalid, dst, lane);
-            else chunk_stats<4>(f, valid, nvalid, dst, lane);
-          }
-          if (!valid) continue;
-          if (p.out2) {
-            uint16_t* d = p.out2 + pix * p.ld_out2 + nb;
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 o;
-              o.x = pack_bf2(f[j], f[j + 1]);
-              o.y = pack_bf2(f[j + 2], f[j + 3]);
-              o.z = pack_bf2(f[j + 4], f[j + 5]);
-              o.w = pack_bf2(f[j + 6], f[j + 7]);
-              *reinterpret_cast<uint4*>(d + j) = o;
-            }
-          }
-          switch (p.out_mode) {
-            case VOUT_F32: {
-              float* d = reinterpret_cast<float*>(p.out) + pix * p.ld_out + nb;
-              if (vec && (p.ld_out & 3) == 0) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                  *reinterpret_cast<float4*>(d + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (j < nn) d[j] = f[j];
-              }
-              break;
-            }
-            case VOUT_F16:
-            case VOUT_BF16: {
-              const bool bf = p.out_mode == VOUT_BF16;
-              uint16_t* d = reinterpret_cast<uint16_t*>(p.out) + pix * p.ld_out + nb;
-              if (vec && (p.ld_out & 7) == 0) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 8) {
-                  uint4 o;
-                  o.x = bf ? pack_bf2(f[j], f[j + 1]) : pack_h2(f[j], f[j + 1]);
-                  o.y = bf ? pack_bf2(f[j + 2], f[j + 3]) : pack_h2(f[j + 2], f[j + 3]);
-                  o.z = bf ? pack_bf2(f[j + 4], f[j + 5]) : pack_h2(f[j + 4], f[j + 5]);
-                  o.w = bf ? pack_bf2(f[j + 6], f[j + 7]) : pack_h2(f[j + 6], f[j + 7]);
-                  *reinterpret_cast<uint4*>(d + j) = o;
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (j < nn)
-                    d[j] = bf ? __bfloat16_as_ushort(__float2bfloat16_rn(f[j]))
-                              : __half_as_ushort(__float2half_rn(f[j]));
-              }
-              break;
-            }
-            case VOUT_F16_T: {
-              __half* d = reinterpret_cast<__half*>(p.out) + pix;
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < nn) d[(long long)(nb + j) * p.ld_out] = __float2half_rn(f[j]);
-              break;
-            }
-            default: {  // VOUT_F32_NCHW
-              float* d = reinterpret_cast<float*>(p.out) + pix;
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < nn) d[(long long)(nb + j) * plane] = f[j];
-              break;
-            }
-          }
-        }
+      const int unit = kPair ? 2 * tc.mt + (int)rank : tc.mt;
+      int x0, y0;
+      unit_origin(p, unit, x0, y0);
+      const int ml = q * 32 + (int)lane;
+      const int px = x0 + ml % p.bw;
+      const int py = y0 + ml / p.bw;
+      const bool valid = unit < p.units && px < p.W && py < p.H;
+      const long long pix =
+          (long long)(py * S + (tc.phase >> 1)) * Wout + (long long)px * S + (tc.phase & 1);
+      const float rs = (p.row_scale && valid) ? p.row_scale[pix] : 1.0f;
+      const float nvalid = (float)__popc(__ballot_sync(0xffffffffu, valid));
+      const int slot = (tc.mt * p.phases + tc.phase) * (kPair ? 2 : 1) + (int)rank;
+      float4* srow = p.stats ? p.stats + ((size_t)slot * 4 + q) * kStatGroups : nullptr;
+      for (int c = eh; c < nch; c += 2) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + b * BN_MAX + c * 32, v);
+        tmem_wait_ld();
+        const int nb = tc.n0 + c * 32;
+        const int nn = min(min(32, p.BN - c * 32), p.N - nb);
+        if (nn <= 0) continue;
+        epilogue_chunk(p, v, nb, nn, valid, pix, rs, nvalid, srow, plane, lane);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) bar_arrive(&dempty[b]);
+      if (lane == 0) {
+        if constexpr (kPair) bar_arrive_remote(dempty_lead + b * 8u);
+        else bar_arrive(&dempty[b]);
+      }
     }
   }
 
+  tc_fence_before();
   __syncthreads();
+  if constexpr (kPair) cluster_sync_all();  // no pair MMA, remote arrive or TMEM access left
   if (warp == WARP_MMA) {
+    __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    if constexpr (kPair) tmem_dealloc_pair(tmem, TMEM_COLS);
+    else tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
@@ -452,8 +517,60 @@ long long vae_conv_stat_slots(int H, int W, int phases) {
   int bw = 128, bh = 1;
   vconv::pick_pixel_tile(H, W, bw, bh);
   const long long units = (long long)((W + bw - 1) / bw) * ((H + bh - 1) / bh);
-  return units * 4 * (phases == 4 ? 4 : 1);
+  return (units + 1) * 4 * (phases == 4 ? 4 : 1);  // + 1: the pair kernel rounds units up to even
 }
+
+namespace {
+
+enum class ConvKernel { Pair, Single };
+
+// BONSAI_VAE_CONV=single selects the one-CTA form (used by the tests to
+// check both); the CTA-pair form is the default.
+ConvKernel conv_kernel_choice() {
+  const char* e = getenv("BONSAI_VAE_CONV");
+  return (e && std::strcmp(e, "single") == 0) ? ConvKernel::Single : ConvKernel::Pair;
+}
+
+template <bool kPair>
+int ensure_smem_attr() {
+  static bool done = false;
+  if (!done) {
+    cudaError_t e = cudaFuncSetAttribute(vconv::conv_kernel<kPair>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         vconv::Cfg<kPair>::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "vae conv: smem attribute");
+    done = true;
+  }
+  return 0;
+}
+
+// Clusters of two conv CTAs that can be resident at once (0 if none).
+int conv_pair_slots() {
+  static int n = -1;
+  if (n >= 0) return n;
+  n = 0;
+  if (ensure_smem_attr<true>()) return n;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * std::max(1, num_sms() / 2));
+  cfg.blockDim = dim3(vconv::NUM_THREADS);
+  cfg.dynamicSmemBytes = vconv::Cfg<true>::SMEM_BYTES;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int c = 0;
+  if (cudaOccupancyMaxActiveClusters(&c, vconv::conv_kernel<true>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return n;
+  }
+  n = c;
+  return n;
+}
+
+}  // namespace
 
 int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   using namespace vconv;
@@ -487,13 +604,17 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   const int tiles_x = (a.W + bw - 1) / bw;
   const long long units = (long long)tiles_x * ((a.H + bh - 1) / bh);
   const int sms = num_sms();
+  const int slots = conv_pair_slots();
+  const bool pair = conv_kernel_choice() == ConvKernel::Pair && slots > 0;
   const int BN = a.bn > 0 ? a.bn : pick_bn(a.N, units * phases, sms);
   if (BN % 16 != 0 || BN < 16 || BN > BN_MAX) return fail(BONSAI_ERR_ARG, "vae conv: bad BN");
-  const long long n_mtiles = units;
+  const int rows_per_cta = pair ? BN / 2 : BN;
+  const long long n_mtiles = pair ? (units + 1) / 2 : units;
   const long long n_ntiles = (a.N + BN - 1) / BN;
   const long long num_tiles = n_mtiles * phases * n_ntiles;
+  const long long stat_slots = n_mtiles * phases * (pair ? 2 : 1) * 4;
   if (num_tiles > 0x7FFFFFFFLL) return fail(BONSAI_ERR_ARG, "vae conv: too many tiles");
-  if (a.stats && n_mtiles * phases * 4 > a.stats_slots)
+  if (a.stats && stat_slots > a.stats_slots)
     return fail(BONSAI_ERR_ARG, "vae conv: GroupNorm partial buffer too small");
   const int w_rows_phase = std::max(a.N, a.w_rows);
 
@@ -513,7 +634,7 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   {
     cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)w_rows_phase * phases};
     cuuint64_t strides[1] = {(cuuint64_t)a.w_ld * 2};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BN};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)rows_per_cta};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(&bmap, dt, 2, const_cast<void*>(a.w), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -527,6 +648,7 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   p.bw = bw;
   p.bh = bh;
   p.tiles_x = tiles_x;
+  p.units = (int)units;
   p.n_mtiles = (int)n_mtiles;
   p.n_ntiles = (int)n_ntiles;
   p.num_tiles = (int)num_tiles;
@@ -563,25 +685,38 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   p.stats = reinterpret_cast<float4*>(a.stats);
   p.gw = a.N / 32;
   p.err = device_error_word();
-  const uint32_t idesc = make_idesc_f16(BM, BN, a.bf16 ? 1 : 0, 0, 0);
+  const uint32_t idesc = make_idesc_f16(pair ? 2 * BM : BM, BN, a.bf16 ? 1 : 0, 0, 0);
 
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_status(e, "vae conv: smem attribute");
-    attr_set = true;
-  }
-  const int grid = (int)std::min<long long>(num_tiles, sms);
   const double flop = 2.0 * a.H * a.W * phases * (double)a.N * a.cin * a.taps;
   const char* kind = phases == 4 ? "vae_conv_up2x"
                      : a.taps == 9 ? (BN == 128 ? "vae_conv3x3_n128" : "vae_conv3x3")
                      : a.H == 1     ? "vae_attn_gemm"
                                     : "vae_conv1x1";
-  ProfScope prof(kind, flop, 0.0, st);
-  conv_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(amap, bmap, p, idesc);
-  if (int rc = launch_status("vae conv_kernel launch")) return rc;
-  if (a.stats_slots_used) *a.stats_slots_used = n_mtiles * phases * 4;
+  if (pair) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (unsigned)std::min<long long>(num_tiles, slots));
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = Cfg<true>::SMEM_BYTES;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ProfScope prof(kind, flop, 0.0, st);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, conv_kernel<true>, amap, bmap, p, idesc);
+    if (e != cudaSuccess) return cuda_status(e, "vae conv_kernel (pair) launch");
+    if (int rc = launch_status("vae conv_kernel (pair) launch")) return rc;
+  } else {
+    if (int rc = ensure_smem_attr<false>()) return rc;
+    const int grid = (int)std::min<long long>(num_tiles, sms);
+    ProfScope prof(kind, flop, 0.0, st);
+    conv_kernel<false><<<grid, NUM_THREADS, Cfg<false>::SMEM_BYTES, st>>>(amap, bmap, p, idesc);
+    if (int rc = launch_status("vae conv_kernel launch")) return rc;
+  }
+  if (a.stats_slots_used) *a.stats_slots_used = stat_slots;
   return 0;
 }
 

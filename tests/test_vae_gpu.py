@@ -4,7 +4,8 @@ against the reference.
 * bonsai_conv2d_nhwc (the tcgen05 implicit-GEMM kernel behind every conv and
   linear of the decoder) against torch's fp32 conv2d on the same 16-bit
   operands: 3x3 and 1x1, ragged images, narrow and wide channel counts, bias
-  and residual.
+  and residual -- in both forms of the kernel (CTA pair, the default, and
+  single CTA; BONSAI_VAE_CONV selects).
 * The whole decoder, loaded from a checkpoint in the reference's layout,
   against the reference's PyTorch decoder (golden fixtures) and against the
   f32 oracle at further sizes.  Tolerance: the reference's own bar for its
@@ -26,6 +27,12 @@ from vae_weights import make_state_dict
 pytestmark = pytest.mark.gpu
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(params=["pair", "single"])
+def conv_kernel(request, monkeypatch):
+    monkeypatch.setenv("BONSAI_VAE_CONV", request.param)
+    return request.param
 
 
 @pytest.fixture(scope="module")
@@ -54,8 +61,10 @@ def _metrics(out, ref):
     (40, 24, 128, 3, 3, "f16", False),
     (3, 300, 512, 320, 1, "f16", True),
     (1, 1, 64, 32, 3, "f16", False),
+    (24, 40, 64, 3, 3, "f16", True),
+    (33, 65, 128, 128, 3, "bf16", True),
 ])
-def test_conv2d_matches_torch(gpu, H, W, cin, cout, k, dtype, resid):
+def test_conv2d_matches_torch(gpu, conv_kernel, H, W, cin, cout, k, dtype, resid):
     import torch
     g = torch.Generator(device="cuda").manual_seed(H * 1000 + W)
     td = torch.float16 if dtype == "f16" else torch.bfloat16
@@ -75,7 +84,7 @@ def test_conv2d_matches_torch(gpu, H, W, cin, cout, k, dtype, resid):
 
 
 @pytest.mark.parametrize("hw", [(2, 2), (3, 5)])
-def test_decode_matches_reference_decoder(gpu, ckpt, hw):
+def test_decode_matches_reference_decoder(gpu, ckpt, conv_kernel, hw):
     import torch
     sd, path = ckpt
     g = np.load(GOLDEN / f"vae_{hw[0]}x{hw[1]}.npz")
@@ -90,7 +99,7 @@ def test_decode_matches_reference_decoder(gpu, ckpt, hw):
     finally:
         v.close()
     err, cos, png_mse = _metrics(out, g["raw"])
-    print(f"vae {hw}: max|err|/rms {err:.3e} cos {cos:.7f} png mse {png_mse:.2e}")
+    print(f"vae {hw} {conv_kernel}: max|err|/rms {err:.3e} cos {cos:.7f} png mse {png_mse:.2e}")
     assert png_mse < 5e-5
     assert cos >= 0.9999
     assert err <= 5e-2
