@@ -166,10 +166,34 @@ __device__ __forceinline__ void unit_origin(const Params& p, int u, int& x0, int
 
 // One 32-column chunk of the epilogue: scale, bias, residual, statistics,
 // stores.  Warp-collective (the statistics shuffle); `valid` is per lane.
-__device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (&v)[32], int nb,
-                                               int nn, bool valid, long long pix, float rs,
-                                               float nvalid, float4* srow, long long plane,
-                                               uint32_t lane) {
+// The residual of one chunk (zeros when there is none or the pixel is
+// invalid); loaded ahead of the accumulator so the DRAM latency overlaps.
+__device__ __forceinline__ void load_resid(const Params& p, int nb, int nn, bool valid,
+                                           long long pix, float (&r)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) r[j] = 0.0f;
+  if (!p.resid || !valid || nn <= 0) return;
+  const float* src = p.resid + pix * p.ld_resid + nb;
+  if (nn == 32 && (p.ld_resid & 3) == 0) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 o = __ldg(reinterpret_cast<const float4*>(src + j));
+      r[j] = o.x;
+      r[j + 1] = o.y;
+      r[j + 2] = o.z;
+      r[j + 3] = o.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nn) r[j] = src[j];
+  }
+}
+
+__device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (&v)[32],
+                                               const float (&res)[32], int nb, int nn, bool valid,
+                                               long long pix, float rs, float nvalid, float4* srow,
+                                               long long plane, uint32_t lane) {
   float f[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * rs;
@@ -179,23 +203,8 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (
       if (j < nn) f[j] += p.bias[nb + j];
   }
   const bool vec = nn == 32;
-  if (p.resid && valid) {
-    const float* r = p.resid + pix * p.ld_resid + nb;
-    if (vec && (p.ld_resid & 3) == 0) {
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 o = *reinterpret_cast<const float4*>(r + j);
-        f[j] += o.x;
-        f[j + 1] += o.y;
-        f[j + 2] += o.z;
-        f[j + 3] += o.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < nn) f[j] += r[j];
-    }
-  }
+  for (int j = 0; j < 32; ++j) f[j] += res[j];
   if (srow) {  // warp-uniform; N == 32 * gw so every chunk is full
     float4* dst = srow + nb / p.gw;
     if (p.gw == 16) chunk_stats<16>(f, valid, nvalid, dst, lane);
@@ -435,10 +444,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const TileCoord tc = tile_coord(p, tile);
       const uint32_t b = lt & 1;
       const uint32_t dph = (lt >> 1) & 1;
-      const bool good = wait_bar(&dfull[b], dph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE);
-      if (!__all_sync(0xffffffffu, good)) break;  // tcgen05.ld is warp-collective
-      tc_fence_after();
-
       const int unit = kPair ? 2 * tc.mt + (int)rank : tc.mt;
       int x0, y0;
       unit_origin(p, unit, x0, y0);
@@ -448,18 +453,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool valid = unit < p.units && px < p.W && py < p.H;
       const long long pix =
           (long long)(py * S + (tc.phase >> 1)) * Wout + (long long)px * S + (tc.phase & 1);
+      // The first chunk's residual is in flight while the tile's MMAs finish.
+      float res[32];
+      load_resid(p, tc.n0 + eh * 32, min(min(32, p.BN - eh * 32), p.N - tc.n0 - eh * 32), valid,
+                 pix, res);
+      const bool good = wait_bar(&dfull[b], dph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, good)) break;  // tcgen05.ld is warp-collective
+      tc_fence_after();
+
       const float rs = (p.row_scale && valid) ? p.row_scale[pix] : 1.0f;
       const float nvalid = (float)__popc(__ballot_sync(0xffffffffu, valid));
       const int slot = (tc.mt * p.phases + tc.phase) * (kPair ? 2 : 1) + (int)rank;
       float4* srow = p.stats ? p.stats + ((size_t)slot * 4 + q) * kStatGroups : nullptr;
       for (int c = eh; c < nch; c += 2) {
+        const int nb = tc.n0 + c * 32;
+        const int nn = min(min(32, p.BN - c * 32), p.N - nb);
+        if (c != eh) load_resid(p, nb, nn, valid, pix, res);
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + b * BN_MAX + c * 32, v);
         tmem_wait_ld();
-        const int nb = tc.n0 + c * 32;
-        const int nn = min(min(32, p.BN - c * 32), p.N - nb);
         if (nn <= 0) continue;
-        epilogue_chunk(p, v, nb, nn, valid, pix, rs, nvalid, srow, plane, lane);
+        epilogue_chunk(p, v, res, nb, nn, valid, pix, rs, nvalid, srow, plane, lane);
       }
       tc_fence_before();
       __syncwarp();
