@@ -318,6 +318,8 @@ def run_bonsai(args):
         from bonsai_b200 import headsplit
         if world > 1:
             model.set_partition(rank, world)
+            if args.exchange == "fused":
+                headsplit.enable_fused(model)
 
     rng = np.random.default_rng(1000 + (0 if split else rank))  # split: one shared image
     img_h = torch.from_numpy(rng.standard_normal((IMG, IN_CH)).astype(np.float32)).pin_memory()
@@ -428,7 +430,11 @@ def run_bonsai(args):
         "config": {"workload": WORKLOAD_2048 if split else WORKLOAD,
                    "global_batch": 1 if split else world, "img_tokens": IMG,
                    "txt_tokens": TXT,
-                   "parallelism": (f"head/row split over {world} GPUs (NCCL all-gather + all-to-all per block)"
+                   "parallelism": ((f"head/row split over {world} GPUs, exchanges fused into the "
+                                    "producing kernels over peer memory (CUDA IPC), one-element "
+                                    "all-reduce per phase for ordering"
+                                    if args.exchange == "fused" else
+                                    f"head/row split over {world} GPUs (NCCL all-gather + all-to-all per block)")
                                    if split else f"dp{world} (one image per GPU, no collective)"),
                    "l2": "inputs larger than L2: every step streams all 2.2 GB of B1_0 weights"},
         "images_per_s": round((1 if split else world) * 1000.0 / ms, 3),
@@ -737,6 +743,9 @@ def main():
     ap.add_argument("--workload", choices=["1024", "2048"], default="1024",
                     help="1024: config 4, one image per GPU (data parallel, default); "
                          "2048: config 5(b), one 2048^2 image split by heads/rows across the GPUs")
+    ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
+                    help="--workload 2048 on N > 1 GPUs: exchanges fused into the kernels over "
+                         "peer memory (default) or NCCL collectives between the phases")
     ap.add_argument("--configs", action="store_true",
                     help="instead of the step: BASELINE configs 1-3, GPU vs the reference CPU "
                          "path, one JSON line per config")

@@ -79,6 +79,9 @@ SIGNATURES = {
     "bonsai_dit_begin": (_c_int, [_vp, _vp, _vp, _vp, _fp, _vp]),
     "bonsai_dit_phase": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp]),
     "bonsai_dit_end": (_c_int, [_vp, _vp, _vp]),
+    "bonsai_dit_set_peers": (_c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _c_int]),
+    "bonsai_dit_ipc_handles": (_c_int, [_vp, _vp]),
+    "bonsai_dit_open_peers": (_c_int, [_vp, _vp, _c_int]),
     "bonsai_vae_create": (_c_int, [_c_int, _c_int, ctypes.c_ulonglong, ctypes.POINTER(_vp)]),
     "bonsai_vae_destroy": (_c_int, [_vp]),
     "bonsai_vae_load_safetensors": (_c_int, [_vp, ctypes.c_char_p]),
@@ -383,6 +386,26 @@ class Dit:
     # ---- partitioned (multi-GPU) driving, see bonsai_b200.headsplit
     def set_partition(self, rank: int, world: int):
         check(lib().bonsai_dit_set_partition(self.handle, rank, world), "bonsai_dit_set_partition")
+
+    def set_peers(self, xm_ptrs, cat_ptrs):
+        """Fused exchanges: every rank's xm / cat device pointers as seen
+        from this GPU ([rank] = this model's own); None switches back."""
+        if xm_ptrs is None:
+            check(lib().bonsai_dit_set_peers(self.handle, None, None, 0), "bonsai_dit_set_peers")
+            return
+        n = len(xm_ptrs)
+        xa = (_vp * n)(*xm_ptrs)
+        ca = (_vp * n)(*cat_ptrs)
+        check(lib().bonsai_dit_set_peers(self.handle, xa, ca, n), "bonsai_dit_set_peers")
+
+    def ipc_handles(self) -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        check(lib().bonsai_dit_ipc_handles(self.handle, buf), "bonsai_dit_ipc_handles")
+        return buf.raw
+
+    def open_peers(self, handles: bytes, world: int):
+        assert len(handles) == 128 * world
+        check(lib().bonsai_dit_open_peers(self.handle, handles, world), "bonsai_dit_open_peers")
 
     def buffer(self, name: str, dtype, shape):
         """Engine buffer as a torch tensor view (no copy)."""

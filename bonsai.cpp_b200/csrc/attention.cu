@@ -64,6 +64,7 @@ struct Params {
   float scale_log2;  // softmax scale * log2(e)
   __half* out;
   long long ld_out;
+  RowRoutes routes;  // routes.n == 0: every row through out
   int* err;
 };
 
@@ -405,7 +406,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const float inv_l = 1.0f / l;
         const int q = q0 + g * BQ + row;
-        __half* dst = p.out + (size_t)q * p.ld_out + (size_t)head * HD;
+        __half* base = p.out;
+        if (p.routes.n > 0) {
+          int r = 0;
+          while (r + 1 < p.routes.n && q >= p.routes.row_bound[r + 1]) ++r;
+          base = p.routes.outs[r];
+        }
+        __half* dst = base + (size_t)q * p.ld_out + (size_t)head * HD;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
@@ -425,6 +432,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               d4[i] = make_uint4(hv[4 * i], hv[4 * i + 1], hv[4 * i + 2], hv[4 * i + 3]);
           }
         }
+        if (p.routes.n > 0) __threadfence_system();  // peer stores ordered before the kernel's end
       }
     }
     tc_fence_before();
@@ -438,8 +446,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 int encode_tmap_heads(CUtensorMap* map, const void* base, int n_heads, int seq, int head_dim);
 
 int launch_attention(const __half* q, const __half* k, const __half* v, int n_heads, int seq,
-                     int head_dim, float scale, __half* out, long long ld_out, cudaStream_t st) {
+                     int head_dim, float scale, __half* out, long long ld_out, cudaStream_t st,
+                     const RowRoutes* routes) {
   if (seq == 0 || n_heads == 0) return 0;
+  if (routes && routes->n > 0) {
+    if (routes->n > kMaxPeers || routes->row_bound[0] != 0 || routes->row_bound[routes->n] != seq)
+      return fail(-1, "attention: row routes must cover [0, seq) with at most 8 destinations");
+    for (int r = 0; r < routes->n; ++r)
+      if (!routes->outs[r] || (reinterpret_cast<uintptr_t>(routes->outs[r]) & 15) != 0 ||
+          routes->row_bound[r + 1] < routes->row_bound[r])
+        return fail(-1, "attention: bad row route");
+  }
   if (head_dim != attn::HD) return fail(-2, "attention: head_dim must be 128");
   if (!q || !k || !v || !out) return fail(-1, "attention: null tensor");
   if (seq < 0 || n_heads < 0) return fail(-1, "attention: negative shape");
@@ -457,6 +474,7 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = out;
   p.ld_out = ld_out;
+  if (routes) p.routes = *routes;
   p.err = device_error_word();
   static bool attr = false;
   if (!attr) {

@@ -164,6 +164,14 @@ struct bonsai_dit {
   // rows [r0, r1) and heads [h0, h0 + hl).  world == 1: everything.
   int rank = 0, world = 1;
   int r0 = 0, r1 = 0, h0 = 0, hl = 24;
+  // Fused exchanges (bonsai_dit_set_peers): every rank's "xm" and "cat" as
+  // seen from this device (peer mappings; [rank] = this model's own).  Phase
+  // 0 then stores its xm rows into every rank's xm and phase 1 stores each
+  // attention row into its owner's cat: no separate all-gather / all-to-all.
+  bool fused = false;
+  __half* peer_xm[kMaxPeers] = {};
+  __half* peer_cat[kMaxPeers] = {};
+  std::vector<void*> ipc_opened;  // peer mappings opened by bonsai_dit_open_peers
   // device copies of caller inputs for the host-buffer entry point
   float *in_img = nullptr, *in_txt = nullptr, *in_pooled = nullptr, *out_buf = nullptr;
 };
@@ -347,6 +355,28 @@ int join_aux(bonsai_dit* m, cudaStream_t st) {
   return cuda_status(cudaStreamWaitEvent(st, m->ev_join, 0), "join wait");
 }
 
+// The other ranks' xm at the rows starting at `row` (fused exchanges only).
+PeerCopies xm_copies(const bonsai_dit* m, int row) {
+  PeerCopies pc;
+  if (!m->fused) return pc;
+  for (int r = 0; r < m->world; ++r)
+    if (r != m->rank) pc.y[pc.n++] = m->peer_xm[r] + (size_t)row * m->c.H;
+  return pc;
+}
+// Attention rows of this rank's heads routed to their owners' cat.
+RowRoutes cat_routes(const bonsai_dit* m) {
+  RowRoutes rr;
+  if (!m->fused) return rr;
+  const int rows = m->c.L / m->world;
+  rr.n = m->world;
+  for (int r = 0; r < m->world; ++r) {
+    rr.outs[r] = m->peer_cat[r] + (size_t)m->h0 * m->c.hd;
+    rr.row_bound[r] = r * rows;
+  }
+  rr.row_bound[m->world] = m->c.L;
+  return rr;
+}
+
 int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
   const Cfg& c = m->c;
   const DoubleW& w = m->dbl[i];
@@ -361,10 +391,10 @@ int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
   // into st before anything that reads both (and at the end of every phase).
   if (phase == 0) {
     RC(fork_aux(m, st));
-    RC(launch_ln_modulate_f16(m->hidden + (size_t)tx.a * H, tx.n(), H, mt + 0 * H, mt + 1 * H,
-                              1e-6f, m->xm + (size_t)tx.a * H, H, ts));
-    RC(launch_ln_modulate_f16(m->hidden + (size_t)im.a * H, im.n(), H, mi + 0 * H, mi + 1 * H,
-                              1e-6f, m->xm + (size_t)im.a * H, H, st));
+    RC(launch_ln_modulate_f16_peers(m->hidden + (size_t)tx.a * H, tx.n(), H, mt + 0 * H, mt + 1 * H,
+                                    1e-6f, m->xm + (size_t)tx.a * H, H, xm_copies(m, tx.a), ts));
+    RC(launch_ln_modulate_f16_peers(m->hidden + (size_t)im.a * H, im.n(), H, mi + 0 * H, mi + 1 * H,
+                                    1e-6f, m->xm + (size_t)im.a * H, H, xm_copies(m, im.a), st));
     return join_aux(m, st);
   }
   if (phase == 1) {
@@ -384,8 +414,9 @@ int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
     RC(launch_qk_norm_rope(q, k, m->hl, c.L, w.nq_txt, w.nq_img, w.nk_txt, w.nk_img, Lt, 1e-6f,
                            m->cos_t, m->sin_t, st));
     // joint attention over [txt; img] (:393-416)
+    const RowRoutes rr = cat_routes(m);
     return launch_attention(q, k, v, m->hl, c.L, c.hd, 1.0f / sqrtf((float)c.hd),
-                            m->cat + (size_t)m->h0 * c.hd, C, st);
+                            m->cat + (size_t)m->h0 * c.hd, C, st, m->fused ? &rr : nullptr);
   }
   // phase 2, per stream on this rank's rows (text on its own stream)
   const int act_mode = c.swiglu ? EPI_SWIGLU_F16 : EPI_GELU_F16;
@@ -425,8 +456,8 @@ int single_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
   const float* md = single_mods(m, i);
   const int rows = m->r1 - m->r0;
   if (phase == 0)
-    return launch_ln_modulate_f16(m->hidden + (size_t)m->r0 * H, rows, H, md, md + H, 1e-6f,
-                                  m->xm + (size_t)m->r0 * H, H, st);
+    return launch_ln_modulate_f16_peers(m->hidden + (size_t)m->r0 * H, rows, H, md, md + H, 1e-6f,
+                                        m->xm + (size_t)m->r0 * H, H, xm_copies(m, m->r0), st);
   if (phase == 1) {
     TileSel sel = head_tiles(m);
     EpiSeg s = seg_qkv(c, 3 * H, m->qkv, 0);
@@ -436,8 +467,9 @@ int single_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
     __half* k = m->qkv + (size_t)(c.heads + m->h0) * hs;
     __half* v = m->qkv + (size_t)(2 * c.heads + m->h0) * hs;
     RC(launch_qk_norm_rope(q, k, m->hl, L, w.nq, w.nq, w.nk, w.nk, L, 1e-6f, m->cos_t, m->sin_t, st));
+    const RowRoutes rr = cat_routes(m);
     return launch_attention(q, k, v, m->hl, L, c.hd, 1.0f / sqrtf((float)c.hd),
-                            m->cat + (size_t)m->h0 * c.hd, C, st);
+                            m->cat + (size_t)m->h0 * c.hd, C, st, m->fused ? &rr : nullptr);
   }
   // MLP part of to_qkv_mlp_proj (rows [3H, 3H + mlp_in_rows)) on this rank's rows
   TileSel mlp;
@@ -685,6 +717,7 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
 int bonsai_dit_destroy(bonsai_dit_t m) {
   if (!m) return 0;
   cudaDeviceSynchronize();
+  for (void* p : m->ipc_opened) cudaIpcCloseMemHandle(p);
   if (m->graph) cudaGraphExecDestroy(m->graph);
   if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
   if (m->aux) cudaStreamDestroy(m->aux);
@@ -855,11 +888,69 @@ int bonsai_dit_set_partition(bonsai_dit_t m, int rank, int world) {
   m->r1 = m->r0 + rows;
   m->hl = c.heads / world;
   m->h0 = rank * m->hl;
+  m->fused = false;  // peers belong to a partition: set them again after a change
   if (m->graph) {
     cudaGraphExecDestroy(m->graph);
     m->graph = nullptr;
   }
   return 0;
+}
+
+int bonsai_dit_set_peers(bonsai_dit_t m, void* const* xm, void* const* cat, int world) {
+  if (!m) return fail(BONSAI_ERR_ARG, "dit_set_peers: null model");
+  if (!xm || !cat) {
+    m->fused = false;
+    return 0;
+  }
+  if (world != m->world || world < 2 || world > kMaxPeers)
+    return fail(BONSAI_ERR_ARG, "dit_set_peers: world must match bonsai_dit_set_partition (2..8)");
+  if (xm[m->rank] != m->xm || cat[m->rank] != m->cat)
+    return fail(BONSAI_ERR_ARG, "dit_set_peers: entry [rank] must be this model's own xm / cat");
+  for (int r = 0; r < world; ++r) {
+    if (!xm[r] || !cat[r] || (reinterpret_cast<uintptr_t>(xm[r]) & 15) ||
+        (reinterpret_cast<uintptr_t>(cat[r]) & 15))
+      return fail(BONSAI_ERR_ARG, "dit_set_peers: null or misaligned buffer");
+    m->peer_xm[r] = static_cast<__half*>(xm[r]);
+    m->peer_cat[r] = static_cast<__half*>(cat[r]);
+  }
+  m->fused = true;
+  return 0;
+}
+
+int bonsai_dit_ipc_handles(bonsai_dit_t m, void* out) {
+  if (!m || !out) return fail(BONSAI_ERR_ARG, "dit_ipc_handles: null argument");
+  cudaIpcMemHandle_t h[2];
+  RC(cuda_status(cudaIpcGetMemHandle(&h[0], m->xm), "dit_ipc_handles: xm"));
+  RC(cuda_status(cudaIpcGetMemHandle(&h[1], m->cat), "dit_ipc_handles: cat"));
+  std::memcpy(out, h, sizeof(h));
+  return 0;
+}
+
+int bonsai_dit_open_peers(bonsai_dit_t m, const void* handles, int world) {
+  if (!m || !handles) return fail(BONSAI_ERR_ARG, "dit_open_peers: null argument");
+  if (world != m->world || world < 2 || world > kMaxPeers)
+    return fail(BONSAI_ERR_ARG, "dit_open_peers: world must match bonsai_dit_set_partition (2..8)");
+  for (void* p : m->ipc_opened) cudaIpcCloseMemHandle(p);
+  m->ipc_opened.clear();
+  m->fused = false;
+  void* xm[kMaxPeers] = {};
+  void* cat[kMaxPeers] = {};
+  const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int r = 0; r < world; ++r) {
+    if (r == m->rank) {
+      xm[r] = m->xm;
+      cat[r] = m->cat;
+      continue;
+    }
+    for (int b = 0; b < 2; ++b) {
+      void* p = nullptr;
+      RC(cuda_status(cudaIpcOpenMemHandle(&p, h[2 * r + b], cudaIpcMemLazyEnablePeerAccess),
+                     "dit_open_peers: open handle"));
+      m->ipc_opened.push_back(p);
+      (b == 0 ? xm : cat)[r] = p;
+    }
+  }
+  return bonsai_dit_set_peers(m, xm, cat, world);
 }
 
 int bonsai_dit_buffer(bonsai_dit_t m, const char* name, void** ptr, long long* bytes) {

@@ -118,16 +118,39 @@ struct StFile {
 int st_open(const char* path, StFile& out);                     // 0 or a BONSAI_ERR_* code
 int st_read(StFile& f, const StTensor& t, void* dst, long long bytes);
 
+// Peer copies of an f16 output: the same rows are also stored, at the same
+// offsets, into copies[0..n) (other GPUs' buffers reached through peer
+// mappings, or other buffers of this GPU).  The kernel ends with a
+// system-scope fence after its stores.
+constexpr int kMaxPeers = 8;
+struct PeerCopies {
+  __half* y[kMaxPeers - 1] = {};
+  int n = 0;
+};
+
 // ------------------------------------------------------------- attention
 // q, k, v: f16 [n_heads][seq][128]; out: f16 [seq][ld_out], head h at columns h*128.
+// routes (optional): query row t is stored through outs[r] for the r with
+// row_bound[r] <= t < row_bound[r + 1] instead of out (each rank's buffer
+// of a head/row split, peer-mapped); the kernel then ends with a
+// system-scope fence after its stores.
+struct RowRoutes {
+  __half* outs[kMaxPeers] = {};
+  int row_bound[kMaxPeers + 1] = {};
+  int n = 0;
+};
 int launch_attention(const __half* q, const __half* k, const __half* v, int n_heads, int seq,
-                     int head_dim, float scale, __half* out, long long ld_out, cudaStream_t st);
+                     int head_dim, float scale, __half* out, long long ld_out, cudaStream_t st,
+                     const RowRoutes* routes = nullptr);
 
 // ------------------------------------------------------------ pointwise
 int launch_f32_to_f16(const float* src, __half* dst, long long n, cudaStream_t st);
 int launch_ln_modulate_f16(const float* x, int rows, int dim, const float* shift,
                            const float* scale, float eps, __half* y, long long ld_y,
                            cudaStream_t st);
+int launch_ln_modulate_f16_peers(const float* x, int rows, int dim, const float* shift,
+                                 const float* scale, float eps, __half* y, long long ld_y,
+                                 const PeerCopies& copies, cudaStream_t st);
 int launch_ln_modulate_f32(const float* x, int rows, int dim, const float* shift,
                            const float* scale, float eps, float* y, long long ld_y,
                            cudaStream_t st);

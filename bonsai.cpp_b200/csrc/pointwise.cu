@@ -81,7 +81,8 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, int rows, int di
 template <int VPT, typename OutT>
 __global__ void __launch_bounds__(128) ln_modulate_block_kernel(
     const float* __restrict__ x, int rows, int dim, const float* __restrict__ shift,
-    const float* __restrict__ scale, float eps, OutT* __restrict__ y, long long ld_y) {
+    const float* __restrict__ scale, float eps, OutT* __restrict__ y, long long ld_y,
+    const PeerCopies copies) {
   __shared__ float red[2][4];
   const int row = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -129,11 +130,16 @@ __global__ void __launch_bounds__(128) ln_modulate_block_kernel(
       uint2 pk;
       pk.x = *reinterpret_cast<uint32_t*>(&a);
       pk.y = *reinterpret_cast<uint32_t*>(&b);
-      *reinterpret_cast<uint2*>(y + (size_t)row * ld_y + idx * 4) = pk;
+      const size_t off = (size_t)row * ld_y + idx * 4;
+      *reinterpret_cast<uint2*>(y + off) = pk;
+#pragma unroll
+      for (int k = 0; k < kMaxPeers - 1; ++k)  // static indices: the copies stay in parameter space
+        if (k < copies.n) *reinterpret_cast<uint2*>(copies.y[k] + off) = pk;
     } else {
       *reinterpret_cast<float4*>(y + (size_t)row * ld_y + idx * 4) = make_float4(o0, o1, o2, o3);
     }
   }
+  if (copies.n > 0) __threadfence_system();  // peer stores ordered before the kernel's end
 }
 
 // Generic (any dim) three-pass version for rows that do not fit registers.
@@ -280,7 +286,8 @@ static int row_grid(long long rows, int warps_per_block) {
 
 template <typename OutT>
 static int ln_mod_impl(const float* x, int rows, int dim, const float* shift, const float* scale,
-                       float eps, OutT* y, long long ld_y, cudaStream_t st) {
+                       float eps, OutT* y, long long ld_y, cudaStream_t st,
+                       const PeerCopies& copies = PeerCopies()) {
   if (rows == 0) return 0;
   if (!x || !shift || !scale || !y || rows < 0 || dim <= 0 || ld_y < dim)
     return fail(-1, "ln_modulate: bad arguments");
@@ -290,9 +297,16 @@ static int ln_mod_impl(const float* x, int rows, int dim, const float* shift, co
                      reinterpret_cast<uintptr_t>(scale)) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(y) & (sizeof(OutT) == 2 ? 7 : 15)) == 0;
   const int n4 = dim / 4;
-  ProfScope prof("ln_modulate", 0.0, (double)rows * dim * (4 + sizeof(OutT)), st);
+  if (copies.n > 0) {
+    bool ok = vec && n4 <= 6 * 128 && copies.n < kMaxPeers;
+    for (int k = 0; k < copies.n && ok; ++k)
+      ok = copies.y[k] && (reinterpret_cast<uintptr_t>(copies.y[k]) & 7) == 0;
+    if (!ok) return fail(-1, "ln_modulate: peer copies need the vectorised row kernel (dim <= 3072)");
+  }
+  ProfScope prof("ln_modulate", 0.0, (double)rows * dim * (4 + sizeof(OutT) * (1 + copies.n)), st);
   if (vec && n4 <= 6 * 128)
-    pw::ln_modulate_block_kernel<6, OutT><<<rows, 128, 0, st>>>(x, rows, dim, shift, scale, eps, y, ld_y);
+    pw::ln_modulate_block_kernel<6, OutT><<<rows, 128, 0, st>>>(x, rows, dim, shift, scale, eps, y,
+                                                                 ld_y, copies);
   else if (vec && n4 <= 24 * 32)
     pw::ln_modulate_kernel<24, OutT><<<row_grid(rows, wpb), wpb * 32, 0, st>>>(x, rows, dim, shift, scale, eps, y, ld_y);
   else if (vec && n4 <= 48 * 32)
@@ -306,6 +320,11 @@ int launch_ln_modulate_f16(const float* x, int rows, int dim, const float* shift
                            const float* scale, float eps, __half* y, long long ld_y,
                            cudaStream_t st) {
   return ln_mod_impl<__half>(x, rows, dim, shift, scale, eps, y, ld_y, st);
+}
+int launch_ln_modulate_f16_peers(const float* x, int rows, int dim, const float* shift,
+                                 const float* scale, float eps, __half* y, long long ld_y,
+                                 const PeerCopies& copies, cudaStream_t st) {
+  return ln_mod_impl<__half>(x, rows, dim, shift, scale, eps, y, ld_y, st, copies);
 }
 int launch_ln_modulate_f32(const float* x, int rows, int dim, const float* shift,
                            const float* scale, float eps, float* y, long long ld_y,

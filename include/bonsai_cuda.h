@@ -285,6 +285,25 @@ int bonsai_dit_single_block(bonsai_dit_t m, int i, void* stream);
  * the rest by token rows).  With world == 1 the phases are exactly
  * bonsai_dit_forward.  The reference has no multi-device path. */
 int bonsai_dit_set_partition(bonsai_dit_t m, int rank, int world);
+/* Fused exchanges: give the partitioned model every rank's "xm" and "cat"
+ * as device pointers valid on this GPU (entry [rank] = its own buffers,
+ * the others peer-mapped, e.g. by bonsai_dit_open_peers).  Phase 0 then also
+ * stores its LN-modulated rows into every rank's xm, and phase 1's attention
+ * stores each output row into its owner's cat (this rank's head columns):
+ * the caller drops the all-gather and the all-to-all and only has to order
+ * the ranks after phases 0 and 1 (a stream-ordered barrier, e.g. a one-element
+ * NCCL all-reduce), because a rank writes into the others' buffers.  Both
+ * kernels end with a system-scope fence after their peer stores.  NULL
+ * pointers switch back to caller-side exchanges; bonsai_dit_set_partition
+ * does too. */
+int bonsai_dit_set_peers(bonsai_dit_t m, void* const* xm, void* const* cat, int world);
+/* CUDA IPC handles (2 x 64 bytes: xm, cat) of this model's buffers, for the
+ * other ranks' bonsai_dit_open_peers. */
+int bonsai_dit_ipc_handles(bonsai_dit_t m, void* out);
+/* Open the handles of all ranks (world x 2 x 64 bytes, rank-major, this
+ * rank's own entry ignored) and set them as peers; the mappings are closed
+ * by the next call or bonsai_dit_destroy. */
+int bonsai_dit_open_peers(bonsai_dit_t m, const void* handles, int world);
 /* Device pointer and size of an engine buffer shared with the caller's
  * collectives: "hidden" f32 [L][3072], "xm" f16 [L][3072],
  * "cat" f16 [L][3072 + mlp], "qkv" f16 [3][24][L][128]. */

@@ -4,8 +4,11 @@
 phases of each block in lock step; the two exchanges that NCCL performs on a
 real multi-GPU run (all-gather of token rows, all-to-all of attention-head
 columns; bonsai_b200.headsplit) are done here with device copies between the
-models' buffers.  Every rank's prediction must equal the unpartitioned
-forward.  World 3 and 8 give 8 and 3 heads per rank, so the Q/K/V weight-tile
+models' buffers -- or, fused, by the kernels themselves: each model is given
+the other models' xm / cat as its peers (bonsai_dit_set_peers), so phase 0
+stores its rows into every model's xm and phase 1's attention stores every
+row into its owner's cat, the path a multi-GPU run takes over peer-mapped
+memory.  Every rank's prediction must equal the unpartitioned forward.  World 3 and 8 give 8 and 3 heads per rank, so the Q/K/V weight-tile
 selections have even and odd tile counts; each GEMM kernel is forced in turn.
 """
 import numpy as np
@@ -28,7 +31,7 @@ def _inputs(m, seed=3):
     return img, txt, pooled
 
 
-def _emulated_forward(preset, world, img, txt, pooled, t):
+def _emulated_forward(preset, world, img, txt, pooled, t, fused=False):
     import torch
     ms = [bb.Dit(preset, IMG_H * IMG_W, TXT, IMG_H, IMG_W, depth=1, depth_single=1, seed=5)
           for _ in range(world)]
@@ -41,6 +44,9 @@ def _emulated_forward(preset, world, img, txt, pooled, t):
         xm = [m.buffer("xm", torch.float16, (L, H)) for m in ms]
         cat = [m.buffer("cat", torch.float16, (L, C)) for m in ms]
         hidden = [m.buffer("hidden", torch.float32, (L, H)) for m in ms]
+        if fused:
+            for m in ms:
+                m.set_peers([b.data_ptr() for b in xm], [b.data_ptr() for b in cat])
 
         def gather_rows(bufs):
             for r in range(world):
@@ -61,10 +67,12 @@ def _emulated_forward(preset, world, img, txt, pooled, t):
             for i in range(n):
                 for m in ms:
                     m.phase(kind, i, 0)
-                gather_rows(xm)
+                if not fused:
+                    gather_rows(xm)
                 for m in ms:
                     m.phase(kind, i, 1)
-                heads_to_rows()
+                if not fused:
+                    heads_to_rows()
                 for m in ms:
                     m.phase(kind, i, 2)
         gather_rows(hidden)
@@ -80,9 +88,10 @@ def _emulated_forward(preset, world, img, txt, pooled, t):
             m.close()
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("kernel", ["single", "pair"])
 @pytest.mark.parametrize("world", [2, 3, 8])
-def test_headsplit_emulated_matches_forward(gpu, monkeypatch, world, kernel):
+def test_headsplit_emulated_matches_forward(gpu, monkeypatch, world, kernel, fused):
     import torch
     monkeypatch.setenv("BONSAI_B1_KERNEL", kernel)
     preset = bb.PRESET_FLUX1
@@ -94,11 +103,11 @@ def test_headsplit_emulated_matches_forward(gpu, monkeypatch, world, kernel):
         torch.cuda.synchronize()
     finally:
         ref_m.close()
-    outs = _emulated_forward(preset, world, img, txt, pooled, 600.0)
+    outs = _emulated_forward(preset, world, img, txt, pooled, 600.0, fused=fused)
     r = ref.double().flatten()
     for rank, o in enumerate(outs):
         g = o.double().flatten()
         cos = float(g @ r / (g.norm() * r.norm()))
         rel = float((g - r).abs().max() / r.pow(2).mean().sqrt())
-        assert cos >= 0.99999 and rel <= 1e-3, (world, kernel, rank, cos, rel)
+        assert cos >= 0.99999 and rel <= 1e-3, (world, kernel, fused, rank, cos, rel)
     assert bb.device_error() == 0
