@@ -119,6 +119,7 @@ using namespace bonsai;
 using namespace bonsai::dit;
 
 struct bonsai_dit {
+  ~bonsai_dit();
   Cfg c;
   std::map<std::string, TensorInfo> reg;
   std::vector<void*> allocs;
@@ -714,16 +715,20 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
   return 0;
 }
 
-int bonsai_dit_destroy(bonsai_dit_t m) {
-  if (!m) return 0;
+// Releases everything the model owns (also when bonsai_dit_create fails
+// part-way and its unique_ptr deletes the half-built model).
+bonsai_dit::~bonsai_dit() {
   cudaDeviceSynchronize();
-  for (void* p : m->ipc_opened) cudaIpcCloseMemHandle(p);
-  if (m->graph) cudaGraphExecDestroy(m->graph);
-  if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
-  if (m->aux) cudaStreamDestroy(m->aux);
-  if (m->ev_fork) cudaEventDestroy(m->ev_fork);
-  if (m->ev_join) cudaEventDestroy(m->ev_join);
-  for (void* p : m->allocs) cudaFree(p);
+  for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
+  if (graph) cudaGraphExecDestroy(graph);
+  if (cap_stream) cudaStreamDestroy(cap_stream);
+  if (aux) cudaStreamDestroy(aux);
+  if (ev_fork) cudaEventDestroy(ev_fork);
+  if (ev_join) cudaEventDestroy(ev_join);
+  for (void* p : allocs) cudaFree(p);
+}
+
+int bonsai_dit_destroy(bonsai_dit_t m) {
   delete m;
   return 0;
 }

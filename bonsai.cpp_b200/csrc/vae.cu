@@ -77,6 +77,7 @@ using namespace bonsai;
 using namespace bonsai::vae;
 
 struct bonsai_vae {
+  ~bonsai_vae();
   int lat_h = 0, lat_w = 0, H0 = 0, W0 = 0;
   std::vector<void*> allocs;
   std::vector<Entry> reg;
@@ -110,6 +111,15 @@ struct bonsai_vae {
   long long graph_kernels = 0;
   int decodes = 0;
 };
+
+// Releases everything the decoder owns (also when bonsai_vae_create fails
+// part-way and its unique_ptr deletes the half-built decoder).
+bonsai_vae::~bonsai_vae() {
+  cudaDeviceSynchronize();
+  if (graph) cudaGraphExecDestroy(graph);
+  if (cap_stream) cudaStreamDestroy(cap_stream);
+  for (void* p : allocs) cudaFree(p);
+}
 
 namespace {
 
@@ -509,11 +519,6 @@ int bonsai_vae_create(int latent_h, int latent_w, unsigned long long seed, bonsa
 }
 
 int bonsai_vae_destroy(bonsai_vae_t v) {
-  if (!v) return 0;
-  cudaDeviceSynchronize();
-  if (v->graph) cudaGraphExecDestroy(v->graph);
-  if (v->cap_stream) cudaStreamDestroy(v->cap_stream);
-  for (void* p : v->allocs) cudaFree(p);
   delete v;
   return 0;
 }
