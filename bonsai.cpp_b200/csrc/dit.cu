@@ -15,6 +15,7 @@
 #include "internal.cuh"
 
 #include <cmath>
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -133,6 +134,10 @@ struct bonsai_dit {
   float *vec_w1 = nullptr, *vec_b1 = nullptr, *vec_w2 = nullptr, *vec_b2 = nullptr;
   float *mod_img_w = nullptr, *mod_txt_w = nullptr, *mod_single_w = nullptr;
   float *norm_out_w = nullptr, *norm_out_b = nullptr, *proj_out_w = nullptr, *proj_out_b = nullptr;
+  // The token-wide f32 edge linears (context embedder, image input, output
+  // projection) also as bf16x3 weights [N][3K] for the tensor cores, kept in
+  // step with the f32 ones; a3 = the split activations [M][3K].
+  __nv_bfloat16 *txt_in_w3 = nullptr, *img_in_w3 = nullptr, *proj_out_w3 = nullptr, *a3 = nullptr;
   // workspace
   float* hidden = nullptr;   // [L][H]
   __half* xm = nullptr;      // [L][H]
@@ -231,6 +236,15 @@ int make_f32(bonsai_dit* m, const std::string& name, long long rows, long long c
   ti.f32 = *out;
   m->reg[name] = ti;
   return gen_f32_into(m->c, ti, *out, 0);
+}
+
+// Re-split one of the token-wide edge weights into its bf16x3 copy.
+int refresh_edge_w3(bonsai_dit* m, const std::string& name, cudaStream_t st) {
+  const Cfg& c = m->c;
+  if (name == "txt_in.w") return launch_split_bf16x3(m->txt_in_w, c.ctx_dim, c.H, c.ctx_dim, true, m->txt_in_w3, st);
+  if (name == "img_in.w") return launch_split_bf16x3(m->img_in_w, c.in_ch, c.H, c.in_ch, true, m->img_in_w3, st);
+  if (name == "proj_out.w") return launch_split_bf16x3(m->proj_out_w, c.H, c.in_ch, c.H, true, m->proj_out_w3, st);
+  return 0;
 }
 
 long long tensor_bytes(const TensorInfo& ti) {
@@ -656,6 +670,15 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
     RC(make_f32(m.get(), "vec.b2", 1, H, 0.f, bstd, &m->vec_b2));
   }
 
+  // bf16x3 copies of the token-wide edge weights
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->txt_in_w3), (size_t)H * 3 * c.ctx_dim * 2));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->img_in_w3), (size_t)H * 3 * c.in_ch * 2));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->proj_out_w3), (size_t)c.in_ch * 3 * H * 2));
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->a3),
+               (size_t)std::max({(long long)c.txt * c.ctx_dim, (long long)c.img * c.in_ch,
+                                 (long long)c.img * H}) * 3 * 2));
+  for (const char* n : {"txt_in.w", "img_in.w", "proj_out.w"}) RC(refresh_edge_w3(m.get(), n, st));
+
   // -------------------------------------------------------- workspace
   const long long C = c.C();
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->hidden), (size_t)L * H * 4));
@@ -762,26 +785,37 @@ static int dit_prepare_vec(bonsai_dit* m, const float* pooled, cudaStream_t st) 
   return compute_mods(m, st);
 }
 
+// A token-wide f32 edge linear: on the tensor cores as bf16x3 when the
+// activations allow it (rows 16-byte aligned, K % 8 == 0), else the f32 CUDA
+// core kernel with its split-K workspace.
+static int edge_linear(bonsai_dit* m, const float* x, long long ldx, int M, int K, const float* W,
+                       const __nv_bfloat16* w3, const float* b, int N, float* y, long long ldy,
+                       cudaStream_t st, float* ws, long long ws_elems) {
+  if (K % 8 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
+    return launch_linear_bf16x3(x, ldx, M, K, w3, b, N, y, ldy, m->a3, st);
+  return launch_linear_f32(x, ldx, M, K, W, b, N, y, ldy, false, st, ws, ws_elems);
+}
+
 // Everything of the step after the timestep upload (all stream-ordered kernel
 // launches with fixed pointers).
 static int dit_forward_body(bonsai_dit* m, const float* img, const float* txt, const float* pooled,
                             float* out, cudaStream_t st) {
   const Cfg& c = m->c;
   // input projections (:283-286), text rows first in the hidden state
-  RC(launch_linear_f32(txt, c.ctx_dim, c.txt, c.ctx_dim, m->txt_in_w, m->txt_in_b, c.H, m->hidden,
-                       c.H, false, st, m->tmp32, (long long)c.img * c.H));
-  RC(launch_linear_f32(img, c.in_ch, c.img, c.in_ch, m->img_in_w, m->img_in_b, c.H,
-                       m->hidden + (size_t)c.txt * c.H, c.H, false, st));
+  RC(edge_linear(m, txt, c.ctx_dim, c.txt, c.ctx_dim, m->txt_in_w, m->txt_in_w3, m->txt_in_b, c.H,
+                 m->hidden, c.H, st, m->tmp32, (long long)c.img * c.H));
+  RC(edge_linear(m, img, c.in_ch, c.img, c.in_ch, m->img_in_w, m->img_in_w3, m->img_in_b, c.H,
+                 m->hidden + (size_t)c.txt * c.H, c.H, st, nullptr, 0));
   RC(dit_prepare_vec(m, pooled, st));
   for (int i = 0; i < c.depth; ++i) RC(run_double(m, i, st));
   for (int i = 0; i < c.depth_single; ++i) RC(run_single(m, i, st));
   // output head (:544-556): norm_out modulation is (scale, shift)
   const float* h_img = m->hidden + (size_t)c.txt * c.H;
   RC(launch_ln_modulate_f32(h_img, c.img, c.H, m->fin + c.H, m->fin, 1e-6f, m->tmp32, c.H, st));
-  // cat (free by now) holds the split-K partial sums of the narrow projection
-  return launch_linear_f32(m->tmp32, c.H, c.img, c.H, m->proj_out_w, m->proj_out_b, c.in_ch, out,
-                           c.in_ch, false, st, reinterpret_cast<float*>(m->cat),
-                           (long long)c.L * c.C() / 2);
+  // (f32 fallback: cat, free by now, holds the split-K partial sums)
+  return edge_linear(m, m->tmp32, c.H, c.img, c.H, m->proj_out_w, m->proj_out_w3, m->proj_out_b,
+                     c.in_ch, out, c.in_ch, st, reinterpret_cast<float*>(m->cat),
+                     (long long)c.L * c.C() / 2);
 }
 
 int bonsai_dit_forward(bonsai_dit_t m, const float* img, const float* txt, const float* pooled,
@@ -981,12 +1015,12 @@ int bonsai_dit_begin(bonsai_dit_t m, const float* img, const float* txt, const f
   RC(dit_upload_timestep(m, timestep, st));
   // input projections of this rank's rows (:283-286)
   const Span tx = own_txt(m), im = own_img(m);
-  RC(launch_linear_f32(txt + (size_t)tx.a * c.ctx_dim, c.ctx_dim, tx.n(), c.ctx_dim, m->txt_in_w,
-                       m->txt_in_b, c.H, m->hidden + (size_t)tx.a * c.H, c.H, false, st, m->tmp32,
-                       (long long)c.img * c.H));
-  RC(launch_linear_f32(img + (size_t)(im.a - c.txt) * c.in_ch, c.in_ch, im.n(), c.in_ch,
-                       m->img_in_w, m->img_in_b, c.H, m->hidden + (size_t)im.a * c.H, c.H, false,
-                       st));
+  RC(edge_linear(m, txt + (size_t)tx.a * c.ctx_dim, c.ctx_dim, tx.n(), c.ctx_dim, m->txt_in_w,
+                 m->txt_in_w3, m->txt_in_b, c.H, m->hidden + (size_t)tx.a * c.H, c.H, st, m->tmp32,
+                 (long long)c.img * c.H));
+  RC(edge_linear(m, img + (size_t)(im.a - c.txt) * c.in_ch, c.in_ch, im.n(), c.in_ch, m->img_in_w,
+                 m->img_in_w3, m->img_in_b, c.H, m->hidden + (size_t)im.a * c.H, c.H, st, nullptr,
+                 0));
   return dit_prepare_vec(m, pooled, st);
 }
 
@@ -1011,10 +1045,10 @@ int bonsai_dit_end(bonsai_dit_t m, float* out, void* stream) {
   // output head (:544-556) on every image row (the caller has gathered them)
   const float* h_img = m->hidden + (size_t)c.txt * c.H;
   RC(launch_ln_modulate_f32(h_img, c.img, c.H, m->fin + c.H, m->fin, 1e-6f, m->tmp32, c.H, st));
-  // cat (free by now) holds the split-K partial sums of the narrow projection
-  return launch_linear_f32(m->tmp32, c.H, c.img, c.H, m->proj_out_w, m->proj_out_b, c.in_ch, out,
-                           c.in_ch, false, st, reinterpret_cast<float*>(m->cat),
-                           (long long)c.L * c.C() / 2);
+  // (f32 fallback: cat, free by now, holds the split-K partial sums)
+  return edge_linear(m, m->tmp32, c.H, c.img, c.H, m->proj_out_w, m->proj_out_w3, m->proj_out_b,
+                     c.in_ch, out, c.in_ch, st, reinterpret_cast<float*>(m->cat),
+                     (long long)c.L * c.C() / 2);
 }
 
 long long bonsai_dit_weight(bonsai_dit_t m, const char* name, void* buf, long long cap) {
@@ -1049,8 +1083,11 @@ int bonsai_dit_set_weight(bonsai_dit_t m, const char* name, const void* host, lo
                                     std::to_string(bytes));
   // No forward of this model may be running while its weights change.
   RC(cuda_status(cudaDeviceSynchronize(), "dit_set_weight: synchronize"));
-  if (ti.kind == KIND_F32)
-    return cuda_status(cudaMemcpy(ti.f32, host, bytes, cudaMemcpyHostToDevice), "dit_set_weight copy");
+  if (ti.kind == KIND_F32) {
+    RC(cuda_status(cudaMemcpy(ti.f32, host, bytes, cudaMemcpyHostToDevice), "dit_set_weight copy"));
+    RC(refresh_edge_w3(m, name, 0));
+    return cuda_status(cudaDeviceSynchronize(), "dit_set_weight: edge split");
+  }
   void* tmp = nullptr;
   if (cudaMalloc(&tmp, bytes) != cudaSuccess) return fail(BONSAI_ERR_NOMEM, "dit_set_weight: staging allocation failed");
   int rc = cuda_status(cudaMemcpy(tmp, host, bytes, cudaMemcpyHostToDevice), "dit_set_weight copy");

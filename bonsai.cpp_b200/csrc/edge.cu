@@ -4,6 +4,14 @@
 // :544-556), plus small elementwise helpers.  They are < 1% of the step's
 // FLOPs; the dense linear is a plain SIMT tiled kernel (f32 accumulate).
 #include "internal.cuh"
+#include "vae.cuh"
+#include "bonsai_cuda.h"
+
+#define RC_EDGE(x)       \
+  do {                   \
+    int _rc = (x);       \
+    if (_rc) return _rc; \
+  } while (0)
 
 #include <algorithm>
 
@@ -267,7 +275,71 @@ __global__ void __launch_bounds__(kEulerThreads)
   }
 }
 
+// x [M][K] (leading dimension ldx) -> out [M][3K] bf16: with hi = bf16(x),
+// lo = bf16(x - hi), activations as [hi | hi | lo] (weights = false) and
+// weights as [hi | lo | hi] (weights = true), so that one GEMM over 3K
+// accumulates x_hi w_hi + x_hi w_lo + x_lo w_hi.
+__global__ void split_bf16x3_kernel(const float* __restrict__ x, long long ldx, int M, int K,
+                                    int weights, __nv_bfloat16* __restrict__ out) {
+  const int k4n = K / 4;
+  const long long total = (long long)M * k4n;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / k4n;
+    const int k = (int)(i - m * k4n) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(x + m * ldx + k);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    __nv_bfloat16 hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      hi[j] = __float2bfloat16_rn(f[j]);
+      lo[j] = __float2bfloat16_rn(f[j] - __bfloat162float(hi[j]));
+    }
+    __nv_bfloat16* o = out + m * 3LL * K + k;
+    const uint2 h2 = *reinterpret_cast<const uint2*>(hi);
+    const uint2 l2 = *reinterpret_cast<const uint2*>(lo);
+    *reinterpret_cast<uint2*>(o) = h2;
+    *reinterpret_cast<uint2*>(o + K) = weights ? l2 : h2;
+    *reinterpret_cast<uint2*>(o + 2 * K) = weights ? h2 : l2;
+  }
+}
+
 }  // namespace edge
+
+int launch_split_bf16x3(const float* x, long long ldx, int M, int K, bool weights,
+                        __nv_bfloat16* out, cudaStream_t st) {
+  if (M <= 0) return 0;
+  if (K % 8 != 0 || ldx % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+    return fail(BONSAI_ERR_ARG, "split_bf16x3: K % 8, ldx % 4 and 16-byte rows required");
+  const long long work = (long long)M * (K / 4);
+  const int blocks = (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, (long long)num_sms() * 8));
+  edge::split_bf16x3_kernel<<<blocks, 256, 0, st>>>(x, ldx, M, K, weights ? 1 : 0, out);
+  return launch_status("split_bf16x3_kernel launch");
+}
+
+int launch_linear_bf16x3(const float* x, long long ldx, int M, int K, const __nv_bfloat16* w3,
+                         const float* bias, int N, float* y, long long ldy, __nv_bfloat16* a3,
+                         cudaStream_t st) {
+  if (M <= 0) return 0;
+  RC_EDGE(launch_split_bf16x3(x, ldx, M, K, false, a3, st));
+  VaeConvArgs a;
+  a.in = a3;
+  a.ld_in = 3LL * K;
+  a.H = 1;
+  a.W = M;
+  a.cin = 3 * K;
+  a.bf16 = true;
+  a.taps = 1;
+  a.w = w3;
+  a.w_ld = 3LL * K;
+  a.N = N;
+  a.bias = bias;
+  a.out = y;
+  a.ld_out = ldy;
+  a.out_mode = VOUT_F32;
+  a.prof_name = "edge_linear_bf16x3";
+  return launch_vae_conv(a, st);
+}
 
 int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* W, const float* b,
                       int N, float* y, long long ldy, bool silu_in, cudaStream_t st,

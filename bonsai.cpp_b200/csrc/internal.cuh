@@ -175,6 +175,17 @@ void rope_pair_table(const int* axes_dim, int n_axes, float theta, int* pair_axi
 int launch_linear_f32(const float* x, long long ldx, int T, int K, const float* W, const float* b,
                       int N, float* y, long long ldy, bool silu_in, cudaStream_t st,
                       float* workspace = nullptr, long long workspace_elems = 0);
+// f32 linear on the tensor cores as bf16x3: x = x_hi + x_lo and
+// W = W_hi + W_lo in bf16, y = x_hi W_hi + x_hi W_lo + x_lo W_hi (+ bias)
+// with f32 accumulation (every bf16 product is exact in f32; the dropped
+// x_lo W_lo term is ~2^-16 relative).  w3 = the weight [N][K] split once by
+// launch_split_bf16x3(weights = true) into [N][3K]; a3: scratch [M][3K].
+// K % 8 == 0, x rows 16-byte aligned.  One split kernel + one GEMM launch.
+int launch_split_bf16x3(const float* x, long long ldx, int M, int K, bool weights,
+                        __nv_bfloat16* out, cudaStream_t st);
+int launch_linear_bf16x3(const float* x, long long ldx, int M, int K, const __nv_bfloat16* w3,
+                         const float* bias, int N, float* y, long long ldy, __nv_bfloat16* a3,
+                         cudaStream_t st);
 int launch_silu_f32(const float* x, long long n, float* y, cudaStream_t st);
 int launch_add_f32(const float* a, const float* b, long long n, float* y, cudaStream_t st);
 // *dev_count += number of NaN / Inf values in x[0, n).

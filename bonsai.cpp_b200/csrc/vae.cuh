@@ -48,6 +48,7 @@ struct VaeConvArgs {
   float* stats = nullptr;
   long long stats_slots = 0;
   long long* stats_slots_used = nullptr;
+  const char* prof_name = nullptr;  // per-launch profiling label (static string; default by shape)
 };
 int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st);
 // GroupNorm partial slots a launch over an H x W input grid writes (upper bound).

@@ -702,7 +702,8 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   const uint32_t idesc = make_idesc_f16(pair ? 2 * BM : BM, BN, a.bf16 ? 1 : 0, 0, 0);
 
   const double flop = 2.0 * a.H * a.W * phases * (double)a.N * a.cin * a.taps;
-  const char* kind = phases == 4 ? "vae_conv_up2x"
+  const char* kind = a.prof_name ? a.prof_name
+                     : phases == 4 ? "vae_conv_up2x"
                      : a.taps == 9 ? (BN == 128 ? "vae_conv3x3_n128" : "vae_conv3x3")
                      : a.H == 1     ? "vae_attn_gemm"
                                     : "vae_conv1x1";
