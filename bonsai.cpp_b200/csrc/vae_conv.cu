@@ -106,43 +106,73 @@ __device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-// GroupNorm partials of one 32-column chunk over the warp's 32 pixels: for
-// each group of GW columns, the sum and the sum of squared deviations from
-// the chunk's own mean (combined by launch_vae_gn_finalize), and the
-// element count.
+// GroupNorm partials of one 32-column chunk over the warp's 32 pixels, one
+// pass: per group of GW columns each lane forms the sum and the sum of
+// squares of its values centred on the group's mean bias (a uniform shift,
+// so the variance is unchanged and the f32 cancellation of q - s^2/n only
+// depends on how far the data's mean sits from it), then the warp reduces
+// all 2 * (32/GW) values at once by a transpose reduce-scatter (each level
+// exchanges half of the remaining values: 16 / 9 / 6 shuffles for GW = 4 / 8
+// / 16 instead of a butterfly per value).  Writes {sum, M2 about the chunk
+// mean, count} per group (combined by launch_vae_gn_finalize).
 template <int GW>
-__device__ __forceinline__ void chunk_stats(const float (&f)[32], bool valid, float nvalid,
-                                            float4* dst, uint32_t lane) {
+__device__ __forceinline__ void chunk_stats(const float (&f)[32], const float* bias, int nb,
+                                            bool valid, float nvalid, float4* dst, uint32_t lane) {
   constexpr int NG = 32 / GW;
-  float s[NG], m2[NG];
+  constexpr int V = 2 * NG;  // s and q of every group
+  float shift[NG];
 #pragma unroll
   for (int g = 0; g < NG; ++g) {
-    float a = 0.0f;
+    float b = 0.0f;
+    if (bias) {
 #pragma unroll
-    for (int k = 0; k < GW; ++k) a += f[g * GW + k];
-    s[g] = warp_sum(valid ? a : 0.0f);
+      for (int k = 0; k < GW; ++k) b += bias[nb + g * GW + k];
+    }
+    shift[g] = b * (1.0f / GW);
   }
-  const float cnt = nvalid * GW;
+  float v[V];
 #pragma unroll
   for (int g = 0; g < NG; ++g) {
-    const float mean = cnt > 0.0f ? s[g] / cnt : 0.0f;
-    float d = 0.0f;
+    float a = 0.0f, q = 0.0f;
 #pragma unroll
     for (int k = 0; k < GW; ++k) {
-      const float e = f[g * GW + k] - mean;
-      d = fmaf(e, e, d);
+      const float e = f[g * GW + k] - shift[g];
+      a += e;
+      q = fmaf(e, e, q);
     }
-    m2[g] = warp_sum(valid ? d : 0.0f);
+    v[2 * g] = valid ? a : 0.0f;
+    v[2 * g + 1] = valid ? q : 0.0f;
   }
-  if (lane == 0) {
+  // Reduce-scatter: at offset o the lane keeps the upper half of its values
+  // if bit o of its lane id is set, else the lower half, and adds the
+  // partner's copy of the half it keeps.
 #pragma unroll
-    for (int g = 0; g < NG; ++g) dst[g] = make_float4(s[g], m2[g], cnt, 0.0f);
+  for (int h = V / 2, o = 16; h >= 1; h >>= 1, o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float send = upper ? v[i] : v[i + h];
+      const float keep = upper ? v[i + h] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  // Lanes now hold value index (lane / (32 / V)) % V summed over the lanes
+  // that differ in the used bits; the rest of the lanes sum by butterfly.
+  constexpr int REP = 32 / V;
+#pragma unroll
+  for (int o = REP / 2; o >= 1; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+  const int idx = (int)(lane / REP) % V;
+  const float other = __shfl_xor_sync(0xffffffffu, v[0], REP);  // the q next to this s
+  if ((idx & 1) == 0 && (lane % REP) == 0) {
+    const int g = idx >> 1;
+    const float cnt = nvalid * GW;
+    const float sc = v[0], qc = other;
+    const float m2 = cnt > 0.0f ? fmaxf(qc - sc * (sc / cnt), 0.0f) : 0.0f;
+    float sh = 0.0f;
+#pragma unroll
+    for (int gg = 0; gg < NG; ++gg)  // static indices keep shift[] in registers
+      if (gg == g) sh = shift[gg];
+    dst[g] = make_float4(sc + cnt * sh, m2, cnt, 0.0f);
   }
 }
 
@@ -207,9 +237,9 @@ __device__ __forceinline__ void epilogue_chunk(const Params& p, const uint32_t (
   for (int j = 0; j < 32; ++j) f[j] += res[j];
   if (srow) {  // warp-uniform; N == 32 * gw so every chunk is full
     float4* dst = srow + nb / p.gw;
-    if (p.gw == 16) chunk_stats<16>(f, valid, nvalid, dst, lane);
-    else if (p.gw == 8) chunk_stats<8>(f, valid, nvalid, dst, lane);
-    else chunk_stats<4>(f, valid, nvalid, dst, lane);
+    if (p.gw == 16) chunk_stats<16>(f, p.bias, nb, valid, nvalid, dst, lane);
+    else if (p.gw == 8) chunk_stats<8>(f, p.bias, nb, valid, nvalid, dst, lane);
+    else chunk_stats<4>(f, p.bias, nb, valid, nvalid, dst, lane);
   }
   if (!valid) return;
   if (p.out2) {
