@@ -62,13 +62,18 @@ constexpr int WARP_EPI0 = 2;
 constexpr int EPI_WARPS = 8;
 constexpr int NUM_THREADS = (WARP_EPI0 + EPI_WARPS) * 32;
 
-template <bool kPair>
-struct Cfg {
-  static constexpr int B_BYTES = (kPair ? BN_MAX / 2 : BN_MAX) * BK * 2;  // weight rows per CTA
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;                    // 32 / 48 KB
-  static constexpr int STAGES = kPair ? 6 : 4;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
-};
+// Shared memory: barriers in the first 1 KB, then the pipeline stages (each
+// the 16 KB pixel box + this CTA's weight rows), as many as fit in
+// kStageBudget: a stage lasts BN/2 x 4 clocks of MMA (pair) or BN x 4
+// (single), so the narrow-N tiles get more stages in flight.
+constexpr int kMaxStages = 8;
+constexpr int kStageBudget = 224 * 1024;
+// Horizontal-tap sharing: when a tile is one 128-pixel image row, the taps of
+// one kernel row (dx = -1, 0, 1; or the two of an upsampling phase) read the
+// same pixels shifted by one: one box of kHaloPix pixels serves all of them,
+// the MMA reading it from row j (descriptor base offset j).
+constexpr int kHaloPix = 136;  // 128 + 2, rounded up to the 8-row swizzle atom
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + 1024 /*barriers*/ + kStageBudget;
 
 struct Params {
   int H, W;                // input grid (the output is H*S x W*S, S = 2 when phases = 4)
@@ -79,6 +84,9 @@ struct Params {
   int BN;                  // output channels per tile (multiple of 16, <= 256)
   int taps;                // taps per phase
   int8_t tap_dy[9], tap_dx[9];
+  int stages, stage_bytes; // pipeline depth and stage size (shared memory layout)
+  int group;               // taps sharing one pixel box (1, or 3 / 2 with a halo box)
+  int a_bytes;             // pixel box bytes per stage (16 KB, or the halo box)
   int cin_blocks;          // 64-channel blocks per tap
   int k_per_tap;           // weight K offset between taps
   int w_rows_phase;        // weight rows per phase
@@ -312,13 +320,15 @@ template <bool kPair>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     conv_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
                 const Params p, const uint32_t idesc) {
-  using C = Cfg<kPair>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
-  uint64_t* empty = full + C::STAGES;
-  uint64_t* dfull = empty + C::STAGES;
+  uint8_t* smem = base + 1024;  // stages (1024-aligned)
+  const int STAGES = p.stages;
+  const int STAGE_BYTES = p.stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(base);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* dfull = empty + kMaxStages;
   uint64_t* dempty = dfull + 2;
   uint64_t* drain = dempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -332,7 +342,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int stride = kPair ? (int)cluster_count_x() : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       bar_init(&full[s], 1);
       bar_init(&empty[s], 1);
     }
@@ -358,14 +368,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if constexpr (kPair) cluster_sync_all();  // barrier inits and TMEM of both CTAs visible
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int ksteps = p.taps * p.cin_blocks;
+  const int ksteps = (p.taps / p.group) * p.cin_blocks;
   const int rows_per_cta = kPair ? p.BN / 2 : p.BN;
+  const int b_tap_bytes = rows_per_cta * BK * 2;
 
   if (warp == WARP_TMA) {
     if (elect_one()) {
       tma_prefetch_desc(&amap);
       tma_prefetch_desc(&bmap);
-      const uint32_t cta_bytes = (uint32_t)(A_BYTES + rows_per_cta * BK * 2);
+      const uint32_t cta_bytes = (uint32_t)(p.a_bytes + p.group * b_tap_bytes);
       uint32_t it = 0;
       bool ok = true;
       for (int tile = first; tile < p.num_tiles && ok; tile += stride) {
@@ -374,27 +385,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int x0, y0;
         unit_origin(p, kPair ? 2 * tc.mt + (int)rank : tc.mt, x0, y0);
         const int brow = tc.phase * p.w_rows_phase + tc.n0 + (int)rank * rows_per_cta;
-        for (int t = 0; t < p.taps && ok; ++t) {
-          const int dy = p.tap_dy[t] + a, dx = p.tap_dx[t] + bph;
+        for (int t0 = 0; t0 < p.taps && ok; t0 += p.group) {
+          // the group's taps share dy; its box starts at the first tap's dx
+          const int dy = p.tap_dy[t0] + a, dx = p.tap_dx[t0] + bph;
           for (int cb = 0; cb < p.cin_blocks; ++cb, ++it) {
-            const int s = it % C::STAGES;
-            const uint32_t ph = (it / C::STAGES) & 1;
+            const int s = it % STAGES;
+            const uint32_t ph = (it / STAGES) & 1;
             if (!wait_bar(&empty[s], ph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
               ok = false;
               break;
             }
-            uint8_t* st = smem + s * C::STAGE_BYTES;
-            const int kcol = t * p.k_per_tap + cb * BK;
+            uint8_t* st = smem + s * STAGE_BYTES;
             if constexpr (kPair) {
               // Both CTAs' loads count on the even CTA's barrier.
               if (rank == 0) bar_arrive_expect_tx(&full[s], 2 * cta_bytes);
               const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
               tma_load_3d_pair(st, &amap, fb, cb * BK, x0 + dx, y0 + dy);
-              tma_load_2d_pair(st + A_BYTES, &bmap, fb, kcol, brow);
+              for (int j = 0; j < p.group; ++j)
+                tma_load_2d_pair(st + p.a_bytes + j * b_tap_bytes, &bmap, fb,
+                                 (t0 + j) * p.k_per_tap + cb * BK, brow);
             } else {
               bar_arrive_expect_tx(&full[s], cta_bytes);
               tma_load_3d(st, &amap, &full[s], cb * BK, x0 + dx, y0 + dy);
-              tma_load_2d(st + A_BYTES, &bmap, &full[s], kcol, brow);
+              for (int j = 0; j < p.group; ++j)
+                tma_load_2d(st + p.a_bytes + j * b_tap_bytes, &bmap, &full[s],
+                            (t0 + j) * p.k_per_tap + cb * BK, brow);
             }
           }
         }
@@ -420,22 +435,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           const uint32_t d_tmem = tmem + b * BN_MAX;
           for (int ks = 0; ks < ksteps; ++ks, ++it) {
-            const int s = it % C::STAGES;
-            const uint32_t ph = (it / C::STAGES) & 1;
+            const int s = it % STAGES;
+            const uint32_t ph = (it / STAGES) & 1;
             if (!wait_bar(&full[s], ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t saddr = smem_u32(smem + s * C::STAGE_BYTES);
+            const uint32_t saddr = smem_u32(smem + s * STAGE_BYTES);
+            for (int j = 0; j < p.group; ++j) {
+              // tap j of the group reads the pixel box from row j
+              const uint32_t arow = saddr + (uint32_t)j * 128u;
+              const uint32_t bbase = saddr + (uint32_t)(p.a_bytes + j * b_tap_bytes);
 #pragma unroll
-            for (int k16 = 0; k16 < BK / 16; ++k16) {
-              const uint64_t adesc = make_smem_desc(saddr + k16 * 32, 16, 1024);
-              const uint64_t bdesc = make_smem_desc(saddr + A_BYTES + k16 * 32, 16, 1024);
-              if constexpr (kPair)
-                mma_ss_pair(d_tmem, adesc, bdesc, idesc, (ks | k16) != 0 ? 1u : 0u);
-              else
-                mma_ss(d_tmem, adesc, bdesc, idesc, (ks | k16) != 0 ? 1u : 0u);
+              for (int k16 = 0; k16 < BK / 16; ++k16) {
+                // the 128-byte swizzle follows the address bits, so a start j rows
+                // into the 1024-byte-aligned box needs no base offset (as the
+                // +32-byte k16 steps within a row need none)
+                const uint64_t adesc = make_smem_desc(arow + k16 * 32, 16, 1024);
+                const uint64_t bdesc = make_smem_desc(bbase + k16 * 32, 16, 1024);
+                const uint32_t acc = (ks | j | k16) != 0 ? 1u : 0u;
+                if constexpr (kPair)
+                  mma_ss_pair(d_tmem, adesc, bdesc, idesc, acc);
+                else
+                  mma_ss(d_tmem, adesc, bdesc, idesc, acc);
+              }
             }
             if constexpr (kPair) tc_commit_pair(&empty[s], 0x3);
             else tc_commit(&empty[s]);
@@ -581,7 +605,7 @@ int ensure_smem_attr() {
   if (!done) {
     cudaError_t e = cudaFuncSetAttribute(vconv::conv_kernel<kPair>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         vconv::Cfg<kPair>::SMEM_BYTES);
+                                         vconv::SMEM_BYTES);
     if (e != cudaSuccess) return cuda_status(e, "vae conv: smem attribute");
     done = true;
   }
@@ -602,7 +626,7 @@ int conv_pair_slots() {
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(2 * std::max(1, num_sms() / 2));
   cfg.blockDim = dim3(vconv::NUM_THREADS);
-  cfg.dynamicSmemBytes = vconv::Cfg<true>::SMEM_BYTES;
+  cfg.dynamicSmemBytes = vconv::SMEM_BYTES;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int c = 0;
@@ -662,13 +686,19 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
     return fail(BONSAI_ERR_ARG, "vae conv: GroupNorm partial buffer too small");
   const int w_rows_phase = std::max(a.N, a.w_rows);
 
+  // Halo boxes when a tile is one 128-pixel row and at least three stages fit.
+  bool halo = bw == 128 && bh == 1 && (a.taps == 9 || a.taps == 4);
+  if (halo) {
+    const int group = a.taps == 9 ? 3 : 2;
+    halo = kStageBudget / (kHaloPix * BK * 2 + group * rows_per_cta * BK * 2) >= 3;
+  }
   const CUtensorMapDataType dt =
       a.bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap amap, bmap;
   {
     cuuint64_t dims[3] = {(cuuint64_t)a.cin, (cuuint64_t)a.W, (cuuint64_t)a.H};
     cuuint64_t strides[2] = {(cuuint64_t)a.ld_in * 2, (cuuint64_t)a.ld_in * 2 * a.W};
-    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)bw, (cuuint32_t)bh};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)(halo ? kHaloPix : bw), (cuuint32_t)bh};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(&amap, dt, 3, const_cast<void*>(a.in), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -713,6 +743,15 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
       p.tap_dx[t] = 0;
     }
   }
+  p.group = 1;
+  p.a_bytes = A_BYTES;
+  p.stage_bytes = A_BYTES + rows_per_cta * BK * 2;
+  if (halo) {
+    p.group = a.taps == 9 ? 3 : 2;
+    p.a_bytes = kHaloPix * BK * 2;
+    p.stage_bytes = p.a_bytes + p.group * rows_per_cta * BK * 2;
+  }
+  p.stages = std::min(kMaxStages, kStageBudget / p.stage_bytes);
   p.cin_blocks = cin_blocks;
   p.k_per_tap = k_per_tap;
   p.w_rows_phase = w_rows_phase;
@@ -746,7 +785,7 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * (unsigned)std::min<long long>(num_tiles, slots));
     cfg.blockDim = dim3(NUM_THREADS);
-    cfg.dynamicSmemBytes = Cfg<true>::SMEM_BYTES;
+    cfg.dynamicSmemBytes = SMEM_BYTES;
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
@@ -758,7 +797,7 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
     if (int rc = ensure_smem_attr<false>()) return rc;
     const int grid = (int)std::min<long long>(num_tiles, sms);
     ProfScope prof(kind, flop, 0.0, st);
-    conv_kernel<false><<<grid, NUM_THREADS, Cfg<false>::SMEM_BYTES, st>>>(amap, bmap, p, idesc);
+    conv_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(amap, bmap, p, idesc);
     if (int rc = launch_status("vae conv_kernel launch")) return rc;
   }
   if (a.stats_slots_used) *a.stats_slots_used = stat_slots;

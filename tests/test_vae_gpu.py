@@ -63,6 +63,13 @@ def _metrics(out, ref):
     (1, 1, 64, 32, 3, "f16", False),
     (24, 40, 64, 3, 3, "f16", True),
     (33, 65, 128, 128, 3, "bf16", True),
+    # widths that are multiples of 128: one 128-pixel row per tile, the three
+    # horizontal taps share one halo box
+    (4, 256, 64, 128, 3, "f16", True),
+    (3, 384, 128, 256, 3, "bf16", False),
+    (2, 128, 512, 512, 3, "f16", True),
+    (6, 128, 256, 3, 3, "f16", False),
+    (9, 512, 128, 128, 3, "f16", True),
 ])
 def test_conv2d_matches_torch(gpu, conv_kernel, H, W, cin, cout, k, dtype, resid):
     import torch
@@ -105,7 +112,7 @@ def test_decode_matches_reference_decoder(gpu, ckpt, conv_kernel, hw):
     assert err <= 5e-2
 
 
-@pytest.mark.parametrize("hw", [(1, 1), (4, 4), (1, 7), (8, 8)])
+@pytest.mark.parametrize("hw", [(1, 1), (4, 4), (1, 7), (8, 8), (16, 16)])
 def test_decode_matches_oracle(gpu, ckpt, hw):
     sd, path = ckpt
     lat = np.random.default_rng(hw[0] * 10 + hw[1]).uniform(-1, 1, (128, *hw)).astype(np.float32)
