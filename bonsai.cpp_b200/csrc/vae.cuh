@@ -23,6 +23,19 @@ enum VaeOut : int {
 // w: 16-bit [w_rows][w_ld] (same type as in); for taps = 9, k_per_tap >= cin
 // rounded up to 64 and the padding columns hold zeros.  bias, row_scale and
 // resid are optional.  in, w, resid and out must be 16-byte aligned.
+//
+// phases = 4 (with taps = 4) computes conv3x3(upsample_nearest_2x(in)) on the
+// 2H x 2W output without forming the upsampled tensor: output pixel
+// (2y + a, 2x + b) is a 2x2 convolution of `in` around (y, x) (row offsets
+// {a - 1, a}, column offsets {b - 1, b}) with the phase's weights
+// w[(2a + b) * w_rows + n] (launch_vae_pack_subpixel_weight folds the 3x3
+// kernel into the four 2x2 ones).
+//
+// Optional epilogue extras (NHWC outputs only): out2, a bf16 NHWC copy of the
+// output (ld_out2, N % 32 == 0); stats, GroupNorm(32) partials of the output
+// for launch_vae_gn_finalize (N in {128, 256, 512}; stats_slots = capacity,
+// *stats_slots_used = slots written).  prof_name labels the launch for
+// bonsai_profile_stop (a static string; by default the shape decides).
 struct VaeConvArgs {
   const void* in = nullptr;
   long long ld_in = 0;
@@ -48,7 +61,7 @@ struct VaeConvArgs {
   float* stats = nullptr;
   long long stats_slots = 0;
   long long* stats_slots_used = nullptr;
-  const char* prof_name = nullptr;  // per-launch profiling label (static string; default by shape)
+  const char* prof_name = nullptr;
 };
 int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st);
 // GroupNorm partial slots a launch over an H x W input grid writes (upper bound).

@@ -661,6 +661,8 @@ int launch_vae_conv(const VaeConvArgs& a, cudaStream_t st) {
   if (k_total > a.w_ld) return fail(BONSAI_ERR_ARG, "vae conv: weight row shorter than K");
   if (a.stats && (a.N % 32 != 0 || (a.N / 32 != 4 && a.N / 32 != 8 && a.N / 32 != 16)))
     return fail(BONSAI_ERR_ARG, "vae conv: GroupNorm statistics need N in {128, 256, 512}");
+  if ((a.out_mode == VOUT_F16_T || a.out_mode == VOUT_F32_NCHW) && (a.resid || a.stats || a.out2))
+    return fail(BONSAI_ERR_ARG, "vae conv: transposed / planar outputs take no residual, statistics or copy");
   if (a.out2 && (a.N % 32 != 0 || (a.ld_out2 & 7) != 0 ||
                  (reinterpret_cast<uintptr_t>(a.out2) & 15) != 0))
     return fail(BONSAI_ERR_ARG, "vae conv: the bf16 copy needs N % 32 == 0 and 16-byte rows");
