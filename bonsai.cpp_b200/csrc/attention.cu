@@ -13,20 +13,24 @@
 //               O_g in TMEM is rescaled) when a tile's max exceeds it by more
 //               than 8 (p <= 2^8 stays accurate in f16); the final 1/l is
 //               exact.  Scale/subtract and the row sum use packed f32x2 ops.
-//   warp 8      TMA: Q0/Q1 once, then K_j / V_j tiles (128 keys x 128 dims,
-//               two 64-dim halves, 128-byte swizzle) through 2-deep rings.
+//   warp 8      TMA: Q0/Q1 once, then K_j / V_j blocks (64 keys x 128 dims,
+//               two 64-dim halves, 128-byte swizzle) through 4-deep rings.
 //   warp 9      one thread issues tcgen05.mma:
-//                 S_g  = Q_g K_j^T   (A, B from SMEM)          g = 0, 1
-//                 O_g += P_g V_j     (A = P_g from TMEM, B = V MN-major)
+//                 S_g(j) = Q_g K_j^T   (A, B from SMEM)          g = 0, 1
+//                 O_g   += P_g(j) V_j  (A = P_g from TMEM, B = V MN-major)
+//               S runs two blocks ahead of P V (S double-buffered per tile),
+//               so a tile's softmax goes from block to block without waiting
+//               for that tile's products.
 //   warps 10-11 idle (they complete the third warpgroup).
 // setmaxnreg gives the softmax warpgroups 224 registers per thread (the whole
 // S row stays in registers) and the TMA/MMA warpgroup 56; the three
 // warpgroups' code paths never rejoin, so each keeps its own budget, and the
 // MMA warp frees TMEM after every softmax warp has signalled it is done.
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
-// P_g (f16 pairs, 64 columns) overwrites the first half of S_g once the
-// softmax has read S_g; the next S_g is issued after P_g V_j in the same
-// in-order MMA stream.
+// TMEM (512 columns): S_{0,0} [0,64) S_{0,1} [64,128) S_{1,0} [128,192)
+// S_{1,1} [192,256) O0 [256,384) O1 [384,512); block j of tile g uses
+// S_{g, j&1}.  P_g(j) (f16 pairs, 32 columns) overwrites the first half of
+// that buffer once the softmax has read S_g(j); S_g(j + 2) is issued after
+// P_g(j) V_j in the same in-order MMA stream.
 #include "internal.cuh"
 #include "ptx.cuh"
 
@@ -36,12 +40,14 @@ namespace bonsai {
 namespace attn {
 
 constexpr int BQ = 128;   // queries per tile (two tiles per CTA)
-constexpr int BKV = 128;
+constexpr int BKV = 64;   // keys per block
 constexpr int HD = 128;
-constexpr int KS = 2;  // K ring depth
-constexpr int VS = 2;  // V ring depth
-constexpr int TILE_BYTES = BKV * HD * 2;  // 32 KB (two 16 KB halves)
-constexpr int HALF_BYTES = TILE_BYTES / 2;
+constexpr int KS = 4;  // K ring depth
+constexpr int VS = 4;  // V ring depth
+constexpr int Q_BYTES = BQ * HD * 2;      // 32 KB per query tile (two 16 KB halves of 64 dims)
+constexpr int Q_HALF = Q_BYTES / 2;
+constexpr int KV_BYTES = BKV * HD * 2;    // 16 KB per K or V block (two 8 KB halves)
+constexpr int KV_HALF = KV_BYTES / 2;
 // Warpgroup 0: softmax of query tile 0, warpgroup 1: tile 1 (one thread per
 // query row); warpgroup 2: TMA warp, MMA warp and two idle warps.  setmaxnreg
 // moves registers from warpgroup 2 to the softmax warpgroups.
@@ -54,9 +60,14 @@ constexpr int kAuxRegs = 56;
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kAuxRegs <= NUM_THREADS * kLaunchRegs,
               "register split exceeds the launch allocation");
 constexpr int TMEM_COLS = 512;
+// S_{g,b} (query tile g, buffer b = block parity): 64 columns at g*128 + b*64;
+// O_g: 128 columns at 256 + g*128.
 constexpr int S_COL = 0, O_COL = 256;
-constexpr int SMEM_BYTES = 1024 + TILE_BYTES * (2 + KS + VS) + 256;
+constexpr int SMEM_BYTES = 1024 + 2 * Q_BYTES + (KS + VS) * KV_BYTES + 512;
 constexpr float kRescaleThreshold = 8.0f;
+// Pairs of a row whose exponentials take the polynomial (bit k: pair
+// positions k mod 16); the rest go to the MUFU.
+constexpr unsigned kPolyPairs = 0x8080;
 
 struct Params {
   int seq;
@@ -109,6 +120,32 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return r;
 }
 
+// 2^x for a pair on the FMA and ALU pipes, to take part of the exponentials
+// off the MUFU (16 ex2 per clock per SM, the softmax's narrowest pipe).
+// x = n + f with n = round(x) (the 1.5 * 2^23 shift leaves n in the low
+// mantissa bits of t) and f in [-0.5, 0.5]; 2^f by a degree-3 polynomial
+// (coefficients from a Remez exchange on the relative error, max 7.5e-5,
+// below the f16 rounding of P); 2^n added to the exponent field.  x is
+// clamped at -126 so that n + the exponent of 2^f stays >= 0; results below
+// 2^-126 are not needed (P is rounded to f16).
+constexpr float kRoundShift = 12582912.0f;  // 1.5 * 2^23
+__device__ __forceinline__ void ex2_poly2(unsigned long long x2, float& a, float& b) {
+  float x0, x1;
+  unpack2(x2, x0, x1);
+  const unsigned long long xc = pack2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const unsigned long long t = add2(xc, pack2(kRoundShift, kRoundShift));
+  const unsigned long long r = add2(t, pack2(-kRoundShift, -kRoundShift));
+  const unsigned long long f = fma2(r, pack2(-1.0f, -1.0f), xc);
+  unsigned long long p = fma2(f, pack2(0.0551716685f, 0.0551716685f), pack2(0.2426111251f, 0.2426111251f));
+  p = fma2(p, f, pack2(0.6932609677f, 0.6932609677f));
+  p = fma2(p, f, pack2(0.9999280572f, 0.9999280572f));
+  float p0, p1, t0, t1;
+  unpack2(p, p0, p1);
+  unpack2(t, t0, t1);
+  a = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  b = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
 __device__ __forceinline__ uint32_t cvt_h2(float lo, float hi) {
   uint32_t y;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(y) : "f"(hi), "f"(lo));
@@ -123,18 +160,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* qs = smem;  // Q0 then Q1
-  uint8_t* ks = qs + 2 * TILE_BYTES;
-  uint8_t* vs = ks + KS * TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + VS * TILE_BYTES);
+  uint8_t* ks = qs + 2 * Q_BYTES;
+  uint8_t* vs = ks + KS * KV_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + VS * KV_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
   uint64_t* k_empty = k_full + KS;
   uint64_t* v_full = k_empty + KS;
   uint64_t* v_empty = v_full + VS;
-  uint64_t* s_full = v_empty + VS;   // [2] one per query tile
-  uint64_t* p_ready = s_full + 2;    // [2]
-  uint64_t* pv_done = p_ready + 2;   // [2]
-  uint64_t* drain = pv_done + 2;
+  uint64_t* s_full = v_empty + VS;   // [4] per query tile g and buffer b: g * 2 + b
+  uint64_t* p_ready = s_full + 4;    // [4]
+  uint64_t* pv_done = p_ready + 4;   // [4]
+  uint64_t* drain = pv_done + 4;
   uint64_t* sm_done = drain + 1;     // softmax warps finished with TMEM
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -155,10 +192,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bar_init(&v_full[s], 1);
       bar_init(&v_empty[s], 1);
     }
-    for (int g = 0; g < 2; ++g) {
-      bar_init(&s_full[g], 1);
-      bar_init(&p_ready[g], 4);
-      bar_init(&pv_done[g], 1);
+    for (int i = 0; i < 4; ++i) {
+      bar_init(&s_full[i], 1);
+      bar_init(&p_ready[i], 4);
+      bar_init(&pv_done[i], 1);
     }
     bar_init(drain, 1);
     bar_init(sm_done, 8);
@@ -181,10 +218,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      bar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      bar_arrive_expect_tx(q_full, 2 * Q_BYTES);
       for (int g = 0; g < 2; ++g) {
-        tma_load_3d(qs + g * TILE_BYTES, &qmap, q_full, 0, q0 + g * BQ, head);
-        tma_load_3d(qs + g * TILE_BYTES + HALF_BYTES, &qmap, q_full, 64, q0 + g * BQ, head);
+        tma_load_3d(qs + g * Q_BYTES, &qmap, q_full, 0, q0 + g * BQ, head);
+        tma_load_3d(qs + g * Q_BYTES + Q_HALF, &qmap, q_full, 64, q0 + g * BQ, head);
       }
       bool ok = true;
       for (int j = 0; j < nkv && ok; ++j) {
@@ -193,17 +230,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
-        bar_arrive_expect_tx(&k_full[sk], TILE_BYTES);
-        tma_load_3d(ks + sk * TILE_BYTES, &kmap, &k_full[sk], 0, j * BKV, head);
-        tma_load_3d(ks + sk * TILE_BYTES + HALF_BYTES, &kmap, &k_full[sk], 64, j * BKV, head);
+        bar_arrive_expect_tx(&k_full[sk], KV_BYTES);
+        tma_load_3d(ks + sk * KV_BYTES, &kmap, &k_full[sk], 0, j * BKV, head);
+        tma_load_3d(ks + sk * KV_BYTES + KV_HALF, &kmap, &k_full[sk], 64, j * BKV, head);
         const int sv = j % VS;
         if (!wait_bar(&v_empty[sv], ((j / VS) & 1) ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
           ok = false;
           break;
         }
-        bar_arrive_expect_tx(&v_full[sv], TILE_BYTES);
-        tma_load_3d(vs + sv * TILE_BYTES, &vmap, &v_full[sv], 0, j * BKV, head);
-        tma_load_3d(vs + sv * TILE_BYTES + HALF_BYTES, &vmap, &v_full[sv], 64, j * BKV, head);
+        bar_arrive_expect_tx(&v_full[sv], KV_BYTES);
+        tma_load_3d(vs + sv * KV_BYTES, &vmap, &v_full[sv], 0, j * BKV, head);
+        tma_load_3d(vs + sv * KV_BYTES + KV_HALF, &vmap, &v_full[sv], 64, j * BKV, head);
       }
       if (!ok) {
         const unsigned long long t0 = globaltimer_ns();
@@ -216,53 +253,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc_s = make_idesc_f16(BQ, BKV, 0, 0, 0);   // K-major A and B
       constexpr uint32_t idesc_o = make_idesc_f16(BQ, HD, 0, 0, 1);    // B (V) MN-major
       bool ok = wait_bar(q_full, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA);
-      // S_g = Q_g K_j^T into S_g (g = query tile); the K stage is released
-      // after the second tile's product.
+      // S_g(j) = Q_g K_j^T into S_{g, j&1}; the K stage is released after the
+      // second tile's product.
       auto issue_s = [&](int j, int g) -> bool {
         const int sk = j % KS;
         if (g == 0 &&
             !wait_bar(&k_full[sk], (j / KS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
           return false;
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(qs + g * TILE_BYTES);
-        const uint32_t k_addr = smem_u32(ks + sk * TILE_BYTES);
-        const uint32_t d = tmem + S_COL + g * BKV;
+        const uint32_t q_addr = smem_u32(qs + g * Q_BYTES);
+        const uint32_t k_addr = smem_u32(ks + sk * KV_BYTES);
+        const uint32_t d = tmem + S_COL + g * 128 + (j & 1) * BKV;
 #pragma unroll
         for (int k16 = 0; k16 < HD / 16; ++k16) {
-          const uint32_t off = (k16 >> 2) * HALF_BYTES + (k16 & 3) * 32;
-          mma_ss(d, make_smem_desc(q_addr + off, 16, 1024), make_smem_desc(k_addr + off, 16, 1024),
+          const uint32_t qo = (k16 >> 2) * Q_HALF + (k16 & 3) * 32;
+          const uint32_t ko = (k16 >> 2) * KV_HALF + (k16 & 3) * 32;
+          mma_ss(d, make_smem_desc(q_addr + qo, 16, 1024), make_smem_desc(k_addr + ko, 16, 1024),
                  idesc_s, k16 > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[g]);
+        tc_commit(&s_full[g * 2 + (j & 1)]);
         if (g == 1) tc_commit(&k_empty[sk]);
         return true;
       };
-      // O_g += P_g V_j; the V stage is released after the second tile's product.
+      // O_g += P_g(j) V_j with P_g(j) over the first 32 columns of S_{g, j&1};
+      // the V stage is released after the second tile's product.
       auto issue_pv = [&](int j, int g) -> bool {
-        if (!wait_bar(&p_ready[g], j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) return false;
+        const int b = j & 1;
+        if (!wait_bar(&p_ready[g * 2 + b], (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
+          return false;
         const int sv = j % VS;
         if (g == 0 &&
             !wait_bar(&v_full[sv], (j / VS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
           return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(vs + sv * TILE_BYTES);
+        const uint32_t v_addr = smem_u32(vs + sv * KV_BYTES);
 #pragma unroll
         for (int k16 = 0; k16 < BKV / 16; ++k16) {
           // 16 keys per step: rows k16*16.. of both 64-dim halves (LBO = half stride).
-          mma_ts(tmem + O_COL + g * HD, tmem + S_COL + g * BKV + k16 * 8,
-                 make_smem_desc(v_addr + k16 * 16 * 128, HALF_BYTES, 1024), idesc_o,
+          mma_ts(tmem + O_COL + g * HD, tmem + S_COL + g * 128 + b * BKV + k16 * 8,
+                 make_smem_desc(v_addr + k16 * 16 * 128, KV_HALF, 1024), idesc_o,
                  (j > 0 || k16 > 0) ? 1u : 0u);
         }
-        tc_commit(&pv_done[g]);
+        tc_commit(&pv_done[g * 2 + b]);
         if (g == 1) tc_commit(&v_empty[sv]);
         return true;
       };
+      // S runs two blocks ahead of P V: S_g(j + 2) reuses the buffer of
+      // P_g(j) and follows P_g(j) V_j in the in-order MMA stream, so the
+      // softmax of block j + 1 never waits for the products of block j.
       if (ok) ok = issue_s(0, 0) && issue_s(0, 1);
+      if (ok && nkv > 1) ok = issue_s(1, 0) && issue_s(1, 1);
       for (int j = 0; j < nkv && ok; ++j) {
         ok = issue_pv(j, 0);
-        if (ok && j + 1 < nkv) ok = issue_s(j + 1, 0);
+        if (ok && j + 2 < nkv) ok = issue_s(j + 2, 0);
         if (ok) ok = issue_pv(j, 1);
-        if (ok && j + 1 < nkv) ok = issue_s(j + 1, 1);
+        if (ok && j + 2 < nkv) ok = issue_s(j + 2, 1);
       }
       tc_commit(drain);
       const uint32_t da = smem_u32(drain);
@@ -296,13 +341,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int g = warp >> 2;
     const int qd = warp & 3;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-    const uint32_t s_addr = tmem + lane_base + S_COL + g * BKV;
     const uint32_t o_addr = tmem + lane_base + O_COL + g * HD;
     const int row = qd * 32 + (int)lane;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      bool good = wait_bar(&s_full[g], j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+      const int buf = j & 1;
+      const uint32_t s_addr = tmem + lane_base + S_COL + g * 128 + buf * BKV;
+      bool good = wait_bar(&s_full[g * 2 + buf], (j >> 1) & 1, abort_flag, p.err,
+                           DEV_ERR_TIMEOUT_SOFTMAX);
       if (!__all_sync(0xffffffffu, good)) {
         ok = false;
         break;
@@ -310,19 +357,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       float s[BKV];
       {
-        // All four 32-column loads in flight before the one wait.
-        uint32_t r0[32], r1[32], r2[32], r3[32];
+        // Both 32-column loads in flight before the one wait.
+        uint32_t r0[32], r1[32];
         tmem_ld32(s_addr, r0);
         tmem_ld32(s_addr + 32, r1);
-        tmem_ld32(s_addr + 64, r2);
-        tmem_ld32(s_addr + 96, r3);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           s[i] = __uint_as_float(r0[i]);
           s[32 + i] = __uint_as_float(r1[i]);
-          s[64 + i] = __uint_as_float(r2[i]);
-          s[96 + i] = __uint_as_float(r3[i]);
         }
       }
       const int kbase = j * BKV;
@@ -349,16 +392,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         alpha = ex2(m - mx);
         m = mx;
       }
-      if (j > 0) {
-        // P_g and O_g are free once the previous P_g V has completed (it
-        // precedes S_g of this step in the MMA stream, so this is immediate).
-        bool good2 = wait_bar(&pv_done[g], (j - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        // O_g is rescaled once P_g(j - 1) V_{j-1} has completed (it may still
+        // be in flight: S runs ahead of P V).  P_g(j) V_j waits for this
+        // block's p_ready, so nothing else writes O_g meanwhile.
+        const int pb = (j - 1) & 1;
+        bool good2 = wait_bar(&pv_done[g * 2 + pb], ((j - 1) >> 1) & 1, abort_flag, p.err,
+                              DEV_ERR_TIMEOUT_SOFTMAX);
         if (!__all_sync(0xffffffffu, good2)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+        {
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
@@ -374,16 +420,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const unsigned long long sc2 = pack2(p.scale_log2, p.scale_log2);
       const unsigned long long nm2 = pack2(-m, -m);
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
+      for (int ch = 0; ch < BKV / 32; ++ch) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int c = ch * 16 + i;
           const unsigned long long x2 = fma2(pack2(s[2 * c], s[2 * c + 1]), sc2, nm2);
-          float x0, x1;
-          unpack2(x2, x0, x1);
-          const float a = ex2(x0);
-          const float b = ex2(x1);
+          float a, b;
+          if ((kPolyPairs >> i) & 1) {
+            ex2_poly2(x2, a, b);
+          } else {
+            float x0, x1;
+            unpack2(x2, x0, x1);
+            a = ex2(x0);
+            b = ex2(x1);
+          }
           rs2[c & 3] = add2(rs2[c & 3], pack2(a, b));
           pk[i] = cvt_h2(a, b);
         }
@@ -397,11 +448,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) bar_arrive(&p_ready[g]);
+      if (lane == 0) bar_arrive(&p_ready[g * 2 + buf]);
     }
     if (ok) {
       const bool good =
-          wait_bar(&pv_done[g], (nkv - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+          wait_bar(&pv_done[g * 2 + ((nkv - 1) & 1)], ((nkv - 1) >> 1) & 1, abort_flag, p.err,
+                   DEV_ERR_TIMEOUT_SOFTMAX);
       if (__all_sync(0xffffffffu, good)) {
         tc_fence_after();
         const float inv_l = 1.0f / l;
@@ -443,7 +495,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 }  // namespace attn
 
-int encode_tmap_heads(CUtensorMap* map, const void* base, int n_heads, int seq, int head_dim);
+int encode_tmap_heads(CUtensorMap* map, const void* base, int n_heads, int seq, int head_dim,
+                      int box_rows);
 
 int launch_attention(const __half* q, const __half* k, const __half* v, int n_heads, int seq,
                      int head_dim, float scale, __half* out, long long ld_out, cudaStream_t st,
@@ -464,9 +517,9 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
       (reinterpret_cast<uintptr_t>(out) & 15) != 0)
     return fail(-1, "attention: out must be 16-byte aligned with ld_out % 8 == 0 and >= heads*128");
   CUtensorMap qm, km, vm;
-  int rc = encode_tmap_heads(&qm, q, n_heads, seq, head_dim);
-  if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim);
-  if (!rc) rc = encode_tmap_heads(&vm, v, n_heads, seq, head_dim);
+  int rc = encode_tmap_heads(&qm, q, n_heads, seq, head_dim, attn::BQ);
+  if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim, attn::BKV);
+  if (!rc) rc = encode_tmap_heads(&vm, v, n_heads, seq, head_dim, attn::BKV);
   if (rc) return rc;
   attn::Params p{};
   p.seq = seq;

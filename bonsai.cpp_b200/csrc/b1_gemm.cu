@@ -846,14 +846,15 @@ int encode_tmap_2d_16b(CUtensorMap* map, const void* base, long long rows, long 
   return 0;
 }
 
-// 3-D head-major [n_heads][seq][head_dim] f16 tensor, box {64, 128, 1}, 128B swizzle.
-int encode_tmap_heads(CUtensorMap* map, const void* base, int n_heads, int seq, int head_dim) {
+// 3-D head-major [n_heads][seq][head_dim] f16 tensor, box {64, box_rows, 1}, 128B swizzle.
+int encode_tmap_heads(CUtensorMap* map, const void* base, int n_heads, int seq, int head_dim,
+                      int box_rows) {
   auto fn = gemm::get_encode_fn();
   if (!fn) return fail(-5, "cuTensorMapEncodeTiled entry point unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(-1, "attention: q/k/v must be 16-byte aligned");
   cuuint64_t dims[3] = {(cuuint64_t)head_dim, (cuuint64_t)seq, (cuuint64_t)n_heads};
   cuuint64_t strides[2] = {(cuuint64_t)head_dim * 2, (cuuint64_t)seq * head_dim * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -43,7 +43,7 @@ def _attn_gpu(q, k, v, scale):
     return out.float().cpu().numpy()
 
 
-@pytest.mark.parametrize("seq,H", [(128, 1), (200, 2), (333, 3), (1280, 2), (77, 1)])
+@pytest.mark.parametrize("seq,H", [(128, 1), (200, 2), (333, 3), (1280, 2), (77, 1), (64, 1), (65, 2), (1, 1), (191, 1)])
 def test_attention_vs_oracle(gpu, seq, H):
     rng = np.random.default_rng(seq * 10 + H)
     q, k, v = (rng.standard_normal((seq, H, 128)).astype(np.float32) for _ in range(3))
