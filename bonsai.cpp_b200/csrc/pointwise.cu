@@ -176,8 +176,10 @@ __global__ void ln_modulate_generic_kernel(const float* __restrict__ x, int rows
 // row, x / sqrt(mean(x^2) + eps) * w (rms_norm_qk, src/diffuser_graph.cpp:71-79)
 // followed by the pair rotation of rope_2d_fwd_f32 (src/b1_0_kernel.h:339-352).
 // Tokens < split use the *_lo weights (text stream of a double block).
-// One warp per row; lane handles elements 4*lane .. 4*lane+3 (two pairs).
-constexpr int QK_HEADS_PER_WARP = 4;
+// One warp per (tensor, token, group of 8 heads): half-warp h takes heads
+// h0 + h, h0 + h + 2, ..., 16 lanes per row with 8 elements (16 bytes) each,
+// all four rows' loads in flight before the first reduction.
+constexpr int QK_HEADS_PER_WARP = 8;
 __global__ void qk_norm_rope_kernel(__half* __restrict__ q, __half* __restrict__ k, int n_heads,
                                     int seq, const float* __restrict__ wq_lo,
                                     const float* __restrict__ wq_hi,
@@ -190,6 +192,7 @@ __global__ void qk_norm_rope_kernel(__half* __restrict__ q, __half* __restrict__
   const int warps = blockDim.x / 32;
   const long long gw = (long long)blockIdx.x * warps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
+  const int half = lane >> 4, hl = lane & 15;
   const int groups = (n_heads + QK_HEADS_PER_WARP - 1) / QK_HEADS_PER_WARP;
   const long long per_tensor = (long long)groups * seq;
   const long long total = k ? 2 * per_tensor : per_tensor;
@@ -197,33 +200,47 @@ __global__ void qk_norm_rope_kernel(__half* __restrict__ q, __half* __restrict__
   const bool is_k = gw >= per_tensor;
   const long long r = is_k ? gw - per_tensor : gw;
   const int t = (int)(r % seq);
-  const int h0 = (int)(r / seq) * QK_HEADS_PER_WARP;
-  const int nh = min(QK_HEADS_PER_WARP, n_heads - h0);
-  __half* base = (is_k ? k : q) + ((size_t)h0 * seq + t) * 128 + lane * 4;
-  const size_t hstride = (size_t)seq * 128;
+  const int h0 = (int)(r / seq) * QK_HEADS_PER_WARP + half;
+  __half* base = (is_k ? k : q) + ((size_t)h0 * seq + t) * 128 + hl * 8;
+  const size_t hstride = (size_t)2 * seq * 128;
   const float* w = is_k ? (t < split ? wk_lo : wk_hi) : (t < split ? wq_lo : wq_hi);
-  uint2 raw[QK_HEADS_PER_WARP];
+  constexpr int R = QK_HEADS_PER_WARP / 2;
+  uint4 raw[R];
 #pragma unroll
-  for (int i = 0; i < QK_HEADS_PER_WARP; ++i)
-    if (i < nh) raw[i] = *reinterpret_cast<const uint2*>(base + i * hstride);
-  const float4 w4 = *reinterpret_cast<const float4*>(w + lane * 4);
-  const float2 c2 = *reinterpret_cast<const float2*>(cos_t + (size_t)t * 64 + lane * 2);
-  const float2 s2 = *reinterpret_cast<const float2*>(sin_t + (size_t)t * 64 + lane * 2);
+  for (int i = 0; i < R; ++i)
+    raw[i] = h0 + 2 * i < n_heads ? *reinterpret_cast<const uint4*>(base + i * hstride)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+  const float4 wa = *reinterpret_cast<const float4*>(w + hl * 8);
+  const float4 wb = *reinterpret_cast<const float4*>(w + hl * 8 + 4);
+  const float4 c4 = *reinterpret_cast<const float4*>(cos_t + (size_t)t * 64 + hl * 4);
+  const float4 s4 = *reinterpret_cast<const float4*>(sin_t + (size_t)t * 64 + hl * 4);
+  const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+  const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+  const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-  for (int i = 0; i < QK_HEADS_PER_WARP; ++i) {
-    if (i >= nh) break;
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw[i].x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw[i].y));
-    const float ss = warp_sum((a.x * a.x + a.y * a.y) + (b.x * b.x + b.y * b.y));
+  for (int i = 0; i < R; ++i) {
+    const uint32_t u[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[e]));
+      x[2 * e] = f.x;
+      x[2 * e + 1] = f.y;
+    }
+    float ss = ((x[0] * x[0] + x[1] * x[1]) + (x[2] * x[2] + x[3] * x[3])) +
+               ((x[4] * x[4] + x[5] * x[5]) + (x[6] * x[6] + x[7] * x[7]));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);  // within the half-warp
     const float sc = 1.0f / sqrtf(ss / 128.0f + eps);
-    const float x0 = (a.x * sc) * w4.x, x1 = (a.y * sc) * w4.y;
-    const float x2 = (b.x * sc) * w4.z, x3 = (b.y * sc) * w4.w;
-    const __half2 o01 = __floats2half2_rn(x0 * c2.x - x1 * s2.x, x0 * s2.x + x1 * c2.x);
-    const __half2 o23 = __floats2half2_rn(x2 * c2.y - x3 * s2.y, x2 * s2.y + x3 * c2.y);
-    uint2 out;
-    out.x = *reinterpret_cast<const uint32_t*>(&o01);
-    out.y = *reinterpret_cast<const uint32_t*>(&o23);
-    *reinterpret_cast<uint2*>(base + i * hstride) = out;
+    uint32_t o4[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float x0 = (x[2 * e] * sc) * wv[2 * e], x1 = (x[2 * e + 1] * sc) * wv[2 * e + 1];
+      const __half2 h = __floats2half2_rn(x0 * cv[e] - x1 * sv[e], x0 * sv[e] + x1 * cv[e]);
+      o4[e] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    if (h0 + 2 * i < n_heads)
+      *reinterpret_cast<uint4*>(base + i * hstride) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
   }
 }
 
