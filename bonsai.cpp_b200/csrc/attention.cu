@@ -36,6 +36,9 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
+
 namespace bonsai {
 namespace attn {
 
@@ -47,7 +50,6 @@ constexpr int VS = 4;  // V ring depth
 constexpr int Q_BYTES = BQ * HD * 2;      // 32 KB per query tile (two 16 KB halves of 64 dims)
 constexpr int Q_HALF = Q_BYTES / 2;
 constexpr int KV_BYTES = BKV * HD * 2;    // 16 KB per K or V block (two 8 KB halves)
-constexpr int KV_HALF = KV_BYTES / 2;
 // Warpgroup 0: softmax of query tile 0, warpgroup 1: tile 1 (one thread per
 // query row); warpgroup 2: TMA warp, MMA warp and two idle warps.  setmaxnreg
 // moves registers from warpgroup 2 to the softmax warpgroups.
@@ -66,8 +68,11 @@ constexpr int S_COL = 0, O_COL = 256;
 constexpr int SMEM_BYTES = 1024 + 2 * Q_BYTES + (KS + VS) * KV_BYTES + 512;
 constexpr float kRescaleThreshold = 8.0f;
 // Pairs of a row whose exponentials take the polynomial (bit k: pair
-// positions k mod 16); the rest go to the MUFU.
-constexpr unsigned kPolyPairs = 0x8080;
+// positions k mod 16); the rest go to the MUFU.  Measured best: 2 of 16 for
+// the one-CTA kernel, 5 of 16 for the CTA pair (whose tensor-core side is
+// faster, so the softmax carries more of the block time).
+constexpr unsigned kPolyPairsSingle = 0x8080;
+constexpr unsigned kPolyPairsPair = 0x9248;
 
 struct Params {
   int seq;
@@ -152,17 +157,29 @@ __device__ __forceinline__ uint32_t cvt_h2(float lo, float hi) {
   return y;
 }
 
+// kPair: a cluster of two CTAs (two SMs) runs every product as one
+// cta_group::2 MMA of M = 256 (each CTA's query tile g is one half).  The B
+// operands are split between the pair, so each CTA stages half of every K
+// block (32 keys) and half of every V block (64 of the 128 dims): per SM, a
+// Q K^T reads 5 KB of shared memory per 32 clocks instead of 6 KB.  The even
+// CTA issues the MMAs; both CTAs' TMA loads complete on its barriers, its
+// commits arrive on both CTAs' barriers, and both CTAs' softmax warps arrive
+// on its p_ready.  CTA r of pair c holds query tiles c*512 + g*256 + r*128.
+template <bool kPair>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap qmap,
                      const __grid_constant__ CUtensorMap kmap,
                      const __grid_constant__ CUtensorMap vmap, const Params p) {
+  constexpr int K_SLOT = kPair ? KV_BYTES / 2 : KV_BYTES;  // two 64-dim halves of 32 or 64 keys
+  constexpr int K_SLOT_HALF = K_SLOT / 2;
+  constexpr int V_SLOT = kPair ? KV_BYTES / 2 : KV_BYTES;  // pair: this CTA's 64 dims of 64 keys
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* qs = smem;  // Q0 then Q1
   uint8_t* ks = qs + 2 * Q_BYTES;
-  uint8_t* vs = ks + KS * KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + VS * KV_BYTES);
+  uint8_t* vs = ks + KS * K_SLOT;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + VS * V_SLOT);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
   uint64_t* k_empty = k_full + KS;
@@ -179,7 +196,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x / 32;
   const uint32_t lane = lane_id();
   const int head = blockIdx.y;
-  const int q0 = blockIdx.x * 2 * BQ;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  // first query of tile g: q0 + g * tstride
+  const int q0 = kPair ? (int)(blockIdx.x >> 1) * 4 * BQ + (int)rank * BQ : (int)blockIdx.x * 2 * BQ;
+  constexpr int tstride = kPair ? 2 * BQ : BQ;
+  const bool leader = !kPair || rank == 0;
   const int nkv = (p.seq + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
@@ -194,7 +215,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int i = 0; i < 4; ++i) {
       bar_init(&s_full[i], 1);
-      bar_init(&p_ready[i], 4);
+      bar_init(&p_ready[i], kPair ? 8 : 4);
       bar_init(&pv_done[i], 1);
     }
     bar_init(drain, 1);
@@ -203,13 +224,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     fence_barrier_init();
   }
   if (warp == WARP_MMA) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair) cluster_sync_all();  // barrier inits and TMEM of both CTAs visible to the pair
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Cluster addresses of the even CTA's barriers (pair loads and remote arrives).
+  auto lead_bar = [&](uint64_t* b) -> uint32_t { return mapa_shared(smem_u32(b), 0); };
 
   if (warp >= 8) {
   regs_dec<kAuxRegs>();
@@ -218,10 +247,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      bar_arrive_expect_tx(q_full, 2 * Q_BYTES);
+      constexpr int ncta = kPair ? 2 : 1;
+      if (leader) bar_arrive_expect_tx(q_full, ncta * 2 * Q_BYTES);
       for (int g = 0; g < 2; ++g) {
-        tma_load_3d(qs + g * Q_BYTES, &qmap, q_full, 0, q0 + g * BQ, head);
-        tma_load_3d(qs + g * Q_BYTES + Q_HALF, &qmap, q_full, 64, q0 + g * BQ, head);
+        for (int h = 0; h < 2; ++h) {
+          if constexpr (kPair)
+            tma_load_3d_pair(qs + g * Q_BYTES + h * Q_HALF, &qmap, lead_bar(q_full), h * 64,
+                             q0 + g * tstride, head);
+          else
+            tma_load_3d(qs + g * Q_BYTES + h * Q_HALF, &qmap, q_full, h * 64, q0 + g * tstride, head);
+        }
       }
       bool ok = true;
       for (int j = 0; j < nkv && ok; ++j) {
@@ -230,17 +265,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
-        bar_arrive_expect_tx(&k_full[sk], KV_BYTES);
-        tma_load_3d(ks + sk * KV_BYTES, &kmap, &k_full[sk], 0, j * BKV, head);
-        tma_load_3d(ks + sk * KV_BYTES + KV_HALF, &kmap, &k_full[sk], 64, j * BKV, head);
+        if (leader) bar_arrive_expect_tx(&k_full[sk], ncta * K_SLOT);
+        for (int h = 0; h < 2; ++h) {
+          if constexpr (kPair)  // this CTA's 32 keys of the block
+            tma_load_3d_pair(ks + sk * K_SLOT + h * K_SLOT_HALF, &kmap, lead_bar(&k_full[sk]), h * 64,
+                             j * BKV + (int)rank * (BKV / 2), head);
+          else
+            tma_load_3d(ks + sk * K_SLOT + h * K_SLOT_HALF, &kmap, &k_full[sk], h * 64, j * BKV, head);
+        }
         const int sv = j % VS;
         if (!wait_bar(&v_empty[sv], ((j / VS) & 1) ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
           ok = false;
           break;
         }
-        bar_arrive_expect_tx(&v_full[sv], KV_BYTES);
-        tma_load_3d(vs + sv * KV_BYTES, &vmap, &v_full[sv], 0, j * BKV, head);
-        tma_load_3d(vs + sv * KV_BYTES + KV_HALF, &vmap, &v_full[sv], 64, j * BKV, head);
+        if (leader) bar_arrive_expect_tx(&v_full[sv], ncta * V_SLOT);
+        if constexpr (kPair) {  // this CTA's 64 dims of the block
+          tma_load_3d_pair(vs + sv * V_SLOT, &vmap, lead_bar(&v_full[sv]), (int)rank * 64, j * BKV,
+                           head);
+        } else {
+          tma_load_3d(vs + sv * V_SLOT, &vmap, &v_full[sv], 0, j * BKV, head);
+          tma_load_3d(vs + sv * V_SLOT + V_SLOT / 2, &vmap, &v_full[sv], 64, j * BKV, head);
+        }
       }
       if (!ok) {
         const unsigned long long t0 = globaltimer_ns();
@@ -248,10 +293,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    __syncwarp();
+    if constexpr (kPair) cluster_sync_all();
   } else if (warp == WARP_MMA) {
     if (elect_one()) {
-      constexpr uint32_t idesc_s = make_idesc_f16(BQ, BKV, 0, 0, 0);   // K-major A and B
-      constexpr uint32_t idesc_o = make_idesc_f16(BQ, HD, 0, 0, 1);    // B (V) MN-major
+    if (leader) {
+      constexpr int MM = kPair ? 2 * BQ : BQ;
+      constexpr uint32_t idesc_s = make_idesc_f16(MM, BKV, 0, 0, 0);   // K-major A and B
+      constexpr uint32_t idesc_o = make_idesc_f16(MM, HD, 0, 0, 1);    // B (V) MN-major
+      auto commit = [&](uint64_t* b) {
+        if constexpr (kPair)
+          tc_commit_pair(b, 0x3);
+        else
+          tc_commit(b);
+      };
       bool ok = wait_bar(q_full, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA);
       // S_g(j) = Q_g K_j^T into S_{g, j&1}; the K stage is released after the
       // second tile's product.
@@ -262,17 +317,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(qs + g * Q_BYTES);
-        const uint32_t k_addr = smem_u32(ks + sk * KV_BYTES);
+        const uint32_t k_addr = smem_u32(ks + sk * K_SLOT);
         const uint32_t d = tmem + S_COL + g * 128 + (j & 1) * BKV;
 #pragma unroll
         for (int k16 = 0; k16 < HD / 16; ++k16) {
           const uint32_t qo = (k16 >> 2) * Q_HALF + (k16 & 3) * 32;
-          const uint32_t ko = (k16 >> 2) * KV_HALF + (k16 & 3) * 32;
-          mma_ss(d, make_smem_desc(q_addr + qo, 16, 1024), make_smem_desc(k_addr + ko, 16, 1024),
-                 idesc_s, k16 > 0 ? 1u : 0u);
+          const uint32_t ko = (k16 >> 2) * K_SLOT_HALF + (k16 & 3) * 32;
+          const uint64_t qd = make_smem_desc(q_addr + qo, 16, 1024);
+          const uint64_t kd = make_smem_desc(k_addr + ko, 16, 1024);
+          if constexpr (kPair)
+            mma_ss_pair(d, qd, kd, idesc_s, k16 > 0 ? 1u : 0u);
+          else
+            mma_ss(d, qd, kd, idesc_s, k16 > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[g * 2 + (j & 1)]);
-        if (g == 1) tc_commit(&k_empty[sk]);
+        commit(&s_full[g * 2 + (j & 1)]);
+        if (g == 1) commit(&k_empty[sk]);
         return true;
       };
       // O_g += P_g(j) V_j with P_g(j) over the first 32 columns of S_{g, j&1};
@@ -286,16 +345,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             !wait_bar(&v_full[sv], (j / VS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
           return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(vs + sv * KV_BYTES);
+        const uint32_t v_addr = smem_u32(vs + sv * V_SLOT);
 #pragma unroll
         for (int k16 = 0; k16 < BKV / 16; ++k16) {
-          // 16 keys per step: rows k16*16.. of both 64-dim halves (LBO = half stride).
-          mma_ts(tmem + O_COL + g * HD, tmem + S_COL + g * 128 + b * BKV + k16 * 8,
-                 make_smem_desc(v_addr + k16 * 16 * 128, KV_HALF, 1024), idesc_o,
-                 (j > 0 || k16 > 0) ? 1u : 0u);
+          // 16 keys per step: rows k16*16.. of the 64-dim halves (LBO = half
+          // stride; the pair's CTAs hold one half each).
+          const uint32_t a = tmem + S_COL + g * 128 + b * BKV + k16 * 8;
+          const uint64_t vd = make_smem_desc(v_addr + k16 * 16 * 128, V_SLOT / 2, 1024);
+          if constexpr (kPair)
+            mma_ts_pair(tmem + O_COL + g * HD, a, vd, idesc_o, (j > 0 || k16 > 0) ? 1u : 0u);
+          else
+            mma_ts(tmem + O_COL + g * HD, a, vd, idesc_o, (j > 0 || k16 > 0) ? 1u : 0u);
         }
-        tc_commit(&pv_done[g * 2 + b]);
-        if (g == 1) tc_commit(&v_empty[sv]);
+        commit(&pv_done[g * 2 + b]);
+        if (g == 1) commit(&v_empty[sv]);
         return true;
       };
       // S runs two blocks ahead of P V: S_g(j + 2) reuses the buffer of
@@ -309,7 +372,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (ok) ok = issue_pv(j, 1);
         if (ok && j + 2 < nkv) ok = issue_s(j + 2, 1);
       }
-      tc_commit(drain);
+      commit(drain);
+    }
+      // Both CTAs of a pair: wait until every MMA has completed (the commit
+      // above arrives on the drain barrier of each CTA).
       const uint32_t da = smem_u32(drain);
       const unsigned long long t0 = globaltimer_ns();
       while (!bar_try_wait(da, 0)) {
@@ -320,20 +386,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     __syncwarp();
-    // Free TMEM once every softmax warp has finished reading it (the roles
-    // never rejoin, so that each keeps its own register budget).
-    const uint32_t sd = smem_u32(sm_done);
-    const unsigned long long t1 = globaltimer_ns();
-    bool done = bar_try_wait(sd, 0);
-    while (!__all_sync(0xffffffffu, done)) {
-      if (globaltimer_ns() - t1 > kWaitLimitNs) {
-        if (p.err && lane == 0) atomicCAS(p.err, 0, DEV_ERR_TIMEOUT_MMA);
-        break;
+    if constexpr (kPair) {
+      // Every warp of both CTAs ends at this cluster barrier, after its last
+      // MMA, remote arrive and TMEM access.
+      cluster_sync_all();
+      tc_fence_after();
+      tmem_dealloc_pair(tmem, TMEM_COLS);
+    } else {
+      // Free TMEM once every softmax warp has finished reading it (the roles
+      // never rejoin, so that each keeps its own register budget).
+      const uint32_t sd = smem_u32(sm_done);
+      const unsigned long long t1 = globaltimer_ns();
+      bool done = bar_try_wait(sd, 0);
+      while (!__all_sync(0xffffffffu, done)) {
+        if (globaltimer_ns() - t1 > kWaitLimitNs) {
+          if (p.err && lane == 0) atomicCAS(p.err, 0, DEV_ERR_TIMEOUT_MMA);
+          break;
+        }
+        done = bar_try_wait(sd, 0);
       }
-      done = bar_try_wait(sd, 0);
+      tc_fence_after();
+      tmem_dealloc(tmem, TMEM_COLS);
     }
-    tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+  } else {
+    if constexpr (kPair) cluster_sync_all();  // warps 10-11
   }
   } else {
     regs_inc<kSoftmaxRegs>();
@@ -427,7 +503,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int c = ch * 16 + i;
           const unsigned long long x2 = fma2(pack2(s[2 * c], s[2 * c + 1]), sc2, nm2);
           float a, b;
-          if ((kPolyPairs >> i) & 1) {
+          if (((kPair ? kPolyPairsPair : kPolyPairsSingle) >> i) & 1) {
             ex2_poly2(x2, a, b);
           } else {
             float x0, x1;
@@ -448,7 +524,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) bar_arrive(&p_ready[g * 2 + buf]);
+      if (lane == 0) {
+        if constexpr (kPair)
+          bar_arrive_remote(lead_bar(&p_ready[g * 2 + buf]));
+        else
+          bar_arrive(&p_ready[g * 2 + buf]);
+      }
     }
     if (ok) {
       const bool good =
@@ -457,7 +538,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (__all_sync(0xffffffffu, good)) {
         tc_fence_after();
         const float inv_l = 1.0f / l;
-        const int q = q0 + g * BQ + row;
+        const int q = q0 + g * tstride + row;
         __half* base = p.out;
         if (p.routes.n > 0) {
           int r = 0;
@@ -489,7 +570,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) bar_arrive(sm_done);
+    if constexpr (kPair)
+      cluster_sync_all();
+    else if (lane == 0)
+      bar_arrive(sm_done);
   }
 }
 
@@ -516,9 +600,13 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
   if (ld_out < (long long)n_heads * head_dim || (ld_out % 8) != 0 ||
       (reinterpret_cast<uintptr_t>(out) & 15) != 0)
     return fail(-1, "attention: out must be 16-byte aligned with ld_out % 8 == 0 and >= heads*128");
+  // BONSAI_ATTN=single selects the one-CTA form (the tests run both); the
+  // CTA-pair form is the default.
+  const char* form = getenv("BONSAI_ATTN");
+  const bool pair = !(form && std::strcmp(form, "single") == 0);
   CUtensorMap qm, km, vm;
   int rc = encode_tmap_heads(&qm, q, n_heads, seq, head_dim, attn::BQ);
-  if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim, attn::BKV);
+  if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim, pair ? attn::BKV / 2 : attn::BKV);
   if (!rc) rc = encode_tmap_heads(&vm, v, n_heads, seq, head_dim, attn::BKV);
   if (rc) return rc;
   attn::Params p{};
@@ -534,23 +622,41 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
     // setmaxnreg.inc waits until the block's launch allocation can supply
     // the registers: refuse to launch unless the kernel was built with the
     // per-thread count the split above assumes.
-    cudaFuncAttributes fa{};
-    cudaError_t e = cudaFuncGetAttributes(&fa, attn::attention_kernel);
-    if (e != cudaSuccess) return cuda_status(e, "attention function attributes");
-    if (fa.numRegs != attn::kLaunchRegs)
-      return fail(-2, "attention: kernel built with " + std::to_string(fa.numRegs) +
-                          " registers per thread, the register split needs " +
-                          std::to_string(attn::kLaunchRegs));
-    e = cudaFuncSetAttribute(attn::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             attn::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_status(e, "attention set smem attribute");
+    for (auto kern : {attn::attention_kernel<false>, attn::attention_kernel<true>}) {
+      cudaFuncAttributes fa{};
+      cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+      if (e != cudaSuccess) return cuda_status(e, "attention function attributes");
+      if (fa.numRegs != attn::kLaunchRegs)
+        return fail(-2, "attention: kernel built with " + std::to_string(fa.numRegs) +
+                            " registers per thread, the register split needs " +
+                            std::to_string(attn::kLaunchRegs));
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_status(e, "attention set smem attribute");
+    }
     attr = true;
   }
-  dim3 grid((seq + 2 * attn::BQ - 1) / (2 * attn::BQ), n_heads);
   ProfScope prof("attention", 4.0 * (double)seq * seq * head_dim * n_heads,
                  4.0 * (double)seq * n_heads * head_dim * 2, st);
-  attn::attention_kernel<<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, st>>>(qm, km, vm, p);
-  return launch_status("attention_kernel launch");
+  if (!pair) {
+    dim3 grid((seq + 2 * attn::BQ - 1) / (2 * attn::BQ), n_heads);
+    attn::attention_kernel<false><<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, st>>>(qm, km, vm, p);
+    return launch_status("attention_kernel launch");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr_c[1];
+  attr_c[0].id = cudaLaunchAttributeClusterDimension;
+  attr_c[0].val.clusterDim.x = 2;
+  attr_c[0].val.clusterDim.y = 1;
+  attr_c[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (unsigned)((seq + 4 * attn::BQ - 1) / (4 * attn::BQ)), (unsigned)n_heads);
+  cfg.blockDim = dim3(attn::NUM_THREADS);
+  cfg.dynamicSmemBytes = attn::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr_c;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn::attention_kernel<true>, qm, km, vm, p);
+  if (e != cudaSuccess) return cuda_status(e, "attention pair launch");
+  return launch_status("attention pair launch");
 }
 
 }  // namespace bonsai

@@ -283,6 +283,16 @@ __device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, ui
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
+// Pair MMA with A from TMEM: D (both CTAs' TMEM) (+)= A (each CTA's own
+// rows, from its TMEM at a_tmem) * B^T, B rows split between the two CTAs'
+// shared memory at the same offsets.
+__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
 // Arrive on the mbarrier at this offset in every CTA of `mask` once the pair
 // MMAs issued so far complete.
 __device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t mask) {

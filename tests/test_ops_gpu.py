@@ -29,6 +29,14 @@ def _assert_block_tol(got, ref, what):
     assert c >= 0.9999 and err <= 1e-2 * rms, f"{what}: cos={c:.6f} maxabs={err:.3e} rms={rms:.3e}"
 
 
+@pytest.fixture(params=["pair", "single"])
+def attn_form(request, monkeypatch):
+    """Both forms of the attention kernel: CTA pair (the default) and one CTA
+    (BONSAI_ATTN=single)."""
+    monkeypatch.setenv("BONSAI_ATTN", request.param)
+    return request.param
+
+
 def _attn_gpu(q, k, v, scale):
     """q, k, v f32 [seq][H][128] numpy -> GPU output f32 [seq][H*128]."""
     import torch
@@ -43,8 +51,9 @@ def _attn_gpu(q, k, v, scale):
     return out.float().cpu().numpy()
 
 
-@pytest.mark.parametrize("seq,H", [(128, 1), (200, 2), (333, 3), (1280, 2), (77, 1), (64, 1), (65, 2), (1, 1), (191, 1)])
-def test_attention_vs_oracle(gpu, seq, H):
+@pytest.mark.parametrize("seq,H", [(128, 1), (200, 2), (333, 3), (1280, 2), (77, 1), (64, 1), (65, 2),
+                                   (1, 1), (191, 1), (513, 2), (1100, 1)])
+def test_attention_vs_oracle(gpu, attn_form, seq, H):
     rng = np.random.default_rng(seq * 10 + H)
     q, k, v = (rng.standard_normal((seq, H, 128)).astype(np.float32) for _ in range(3))
     scale = 1.0 / np.sqrt(128.0)
@@ -53,7 +62,7 @@ def test_attention_vs_oracle(gpu, seq, H):
     _assert_block_tol(got, ref, f"attention seq={seq} H={H}")
 
 
-def test_attention_large_logits_rescale(gpu):
+def test_attention_large_logits_rescale(gpu, attn_form):
     """Rows whose max grows across key tiles exercise the lazy O rescale."""
     rng = np.random.default_rng(5)
     seq, H = 640, 2
@@ -65,7 +74,7 @@ def test_attention_large_logits_rescale(gpu):
     _assert_block_tol(_attn_gpu(q, k, v, scale), O.attention(q, k, v, scale), "attention rescale")
 
 
-def test_attention_config2_full_size(gpu):
+def test_attention_config2_full_size(gpu, attn_form):
     """BASELINE config 2 shape (H=24, D=128, L=4352 = 256 text + 4096 image),
     against a torch fp32 softmax attention on the same f16 inputs."""
     import torch
