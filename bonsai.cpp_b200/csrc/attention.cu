@@ -582,6 +582,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 int encode_tmap_heads(CUtensorMap* map, const void* base, int n_heads, int seq, int head_dim,
                       int box_rows);
 
+namespace {
+cudaLaunchConfig_t attn_pair_config(cudaLaunchAttribute* attr) {
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(attn::NUM_THREADS);
+  cfg.dynamicSmemBytes = attn::SMEM_BYTES;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Whether at least one cluster of two attention CTAs can be resident (the
+// pair form is used only then).
+bool attn_pair_fits() {
+  static int fits = -1;
+  if (fits < 0) {
+    fits = 0;
+    if (cudaFuncSetAttribute(attn::attention_kernel<true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             attn::SMEM_BYTES) == cudaSuccess) {
+      cudaLaunchAttribute attr[1];
+      cudaLaunchConfig_t cfg = attn_pair_config(attr);
+      cfg.gridDim = dim3(2);
+      int c = 0;
+      if (cudaOccupancyMaxActiveClusters(&c, attn::attention_kernel<true>, &cfg) == cudaSuccess)
+        fits = c > 0 ? 1 : 0;
+    }
+    cudaGetLastError();
+  }
+  return fits == 1;
+}
+}  // namespace
+
 int launch_attention(const __half* q, const __half* k, const __half* v, int n_heads, int seq,
                      int head_dim, float scale, __half* out, long long ld_out, cudaStream_t st,
                      const RowRoutes* routes) {
@@ -601,9 +637,9 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
       (reinterpret_cast<uintptr_t>(out) & 15) != 0)
     return fail(-1, "attention: out must be 16-byte aligned with ld_out % 8 == 0 and >= heads*128");
   // BONSAI_ATTN=single selects the one-CTA form (the tests run both); the
-  // CTA-pair form is the default.
+  // CTA-pair form is the default where a cluster of two fits (checked once).
   const char* form = getenv("BONSAI_ATTN");
-  const bool pair = !(form && std::strcmp(form, "single") == 0);
+  const bool pair = !(form && std::strcmp(form, "single") == 0) && attn_pair_fits();
   CUtensorMap qm, km, vm;
   int rc = encode_tmap_heads(&qm, q, n_heads, seq, head_dim, attn::BQ);
   if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim, pair ? attn::BKV / 2 : attn::BKV);
@@ -642,18 +678,10 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
     attn::attention_kernel<false><<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, st>>>(qm, km, vm, p);
     return launch_status("attention_kernel launch");
   }
-  cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr_c[1];
-  attr_c[0].id = cudaLaunchAttributeClusterDimension;
-  attr_c[0].val.clusterDim.x = 2;
-  attr_c[0].val.clusterDim.y = 1;
-  attr_c[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = attn_pair_config(attr_c);
   cfg.gridDim = dim3(2 * (unsigned)((seq + 4 * attn::BQ - 1) / (4 * attn::BQ)), (unsigned)n_heads);
-  cfg.blockDim = dim3(attn::NUM_THREADS);
-  cfg.dynamicSmemBytes = attn::SMEM_BYTES;
   cfg.stream = st;
-  cfg.attrs = attr_c;
-  cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, attn::attention_kernel<true>, qm, km, vm, p);
   if (e != cudaSuccess) return cuda_status(e, "attention pair launch");
   return launch_status("attention pair launch");

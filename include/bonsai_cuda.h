@@ -201,7 +201,10 @@ int bonsai_ln_modulate_f32(const float* x, int rows, int dim, const float* shift
  * GGML_PREC_F32: src/diffuser_graph.cpp:403-416, :506-519).
  * q, k, v: f16 head-major [n_heads][seq][head_dim] (head_dim = 128).
  * out: f16 token-major [seq][ld_out] with head h at columns h*head_dim.
- * scale: softmax scale (the reference uses 1/sqrt(head_dim)). */
+ * scale: softmax scale (the reference uses 1/sqrt(head_dim)).
+ * Runs as clusters of two CTAs where they fit; the environment variable
+ * BONSAI_ATTN=single selects the one-CTA kernel (results equal within the
+ * tolerance, not bit-identical). */
 int bonsai_joint_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int n_heads,
                            int seq, int head_dim, float scale, uint16_t* out, long long ld_out,
                            void* stream);

@@ -62,6 +62,24 @@ def test_attention_vs_oracle(gpu, attn_form, seq, H):
     _assert_block_tol(got, ref, f"attention seq={seq} H={H}")
 
 
+def test_attention_default_is_the_pair_form(gpu, monkeypatch):
+    """On a B200 the default launch is the CTA-pair kernel: its results differ
+    in the last bits from the one-CTA form's (5/16 vs 2/16 of the
+    exponentials on the polynomial) while both meet the tolerance."""
+    rng = np.random.default_rng(11)
+    seq, H = 700, 2
+    q, k, v = (rng.standard_normal((seq, H, 128)).astype(np.float32) for _ in range(3))
+    scale = 1.0 / np.sqrt(128.0)
+    monkeypatch.delenv("BONSAI_ATTN", raising=False)
+    pair = _attn_gpu(q, k, v, scale)
+    monkeypatch.setenv("BONSAI_ATTN", "single")
+    single = _attn_gpu(q, k, v, scale)
+    ref = O.attention(q, k, v, scale)
+    _assert_block_tol(pair, ref, "attention default form")
+    _assert_block_tol(single, ref, "attention single form")
+    assert not np.array_equal(pair, single)
+
+
 def test_attention_large_logits_rescale(gpu, attn_form):
     """Rows whose max grows across key tiles exercise the lazy O rescale."""
     rng = np.random.default_rng(5)
