@@ -76,6 +76,12 @@ __global__ void f32_to_f16_scalar_kernel(const float* __restrict__ src, __half* 
 }
 }  // namespace
 
+int device_slot() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d & 63;
+}
+
 void set_error(const std::string& msg) { g_last_error = msg; }
 int fail(int code, const std::string& msg) {
   g_last_error = msg;

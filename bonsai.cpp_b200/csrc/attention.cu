@@ -6,7 +6,9 @@
 //
 // One CTA = one head x 256 queries, processed as two 128-query tiles that
 // ping-pong on the tensor core: while the softmax warps of one tile work,
-// the MMA thread runs the other tile's P*V and its next Q*K^T.
+// the MMA thread runs the other tile's P*V and its next Q*K^T.  The default
+// launch pairs two such CTAs into a cluster that runs each product as one
+// cta_group::2 MMA (see attention_kernel<true> below).
 //   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1: thread i
 //               owns query row i (TMEM lane i).  Online softmax in the log2
 //               domain with lazy rescaling: the running max only moves (and
@@ -38,6 +40,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 namespace bonsai {
 namespace attn {
@@ -599,9 +602,12 @@ cudaLaunchConfig_t attn_pair_config(cudaLaunchAttribute* attr) {
 // Whether at least one cluster of two attention CTAs can be resident (the
 // pair form is used only then).
 bool attn_pair_fits() {
-  static int fits = -1;
-  if (fits < 0) {
-    fits = 0;
+  static int fits_dev[64] = {};  // 0 unknown, 1 fits, 2 does not
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  int& fits = fits_dev[device_slot()];
+  if (fits == 0) {
+    fits = 2;
     if (cudaFuncSetAttribute(attn::attention_kernel<true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              attn::SMEM_BYTES) == cudaSuccess) {
@@ -610,7 +616,7 @@ bool attn_pair_fits() {
       cfg.gridDim = dim3(2);
       int c = 0;
       if (cudaOccupancyMaxActiveClusters(&c, attn::attention_kernel<true>, &cfg) == cudaSuccess)
-        fits = c > 0 ? 1 : 0;
+        fits = c > 0 ? 1 : 2;
     }
     cudaGetLastError();
   }
@@ -653,7 +659,8 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
   p.ld_out = ld_out;
   if (routes) p.routes = *routes;
   p.err = device_error_word();
-  static bool attr = false;
+  static bool attr_dev[64] = {};
+  bool& attr = attr_dev[device_slot()];
   if (!attr) {
     // setmaxnreg.inc waits until the block's launch allocation can supply
     // the registers: refuse to launch unless the kernel was built with the

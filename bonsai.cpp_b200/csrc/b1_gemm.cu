@@ -888,10 +888,13 @@ B1Kernel forced_kernel() {
 // Largest number of co-resident pair clusters (one per TPC when every SM
 // takes one CTA of the pair kernel); 0 if the query fails.
 int pair_cluster_slots(bool bf16) {
-  static int slots[2] = {-1, -1};
+  struct Slots {
+    int n[2] = {-1, -1};
+  };
+  static Slots slots[64];
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
-  int& n = slots[bf16 ? 1 : 0];
+  int& n = slots[device_slot()].n[bf16 ? 1 : 0];
   if (n >= 0) return n;
   auto k2 = bf16 ? gemm::pair::b1_gemm_pair_kernel<true> : gemm::pair::b1_gemm_pair_kernel<false>;
   n = 0;
@@ -1046,12 +1049,13 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
 
   const int grid = (int)std::min<long long>(tiles1, num_sms());
   auto kern = x_bf16 ? gemm::b1_gemm_kernel<true> : gemm::b1_gemm_kernel<false>;
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[x_bf16 ? 1 : 0]) {
+  static bool attr_set[64][2] = {};
+  bool& attr_done = attr_set[device_slot()][x_bf16 ? 1 : 0];
+  if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          gemm::SMEM_BYTES);
     if (e != cudaSuccess) return cuda_status(e, "b1_gemm set smem attribute");
-    attr_set[x_bf16 ? 1 : 0] = true;
+    attr_done = true;
   }
   ProfScope prof("b1_gemm", 2.0 * tokens * rows_done * (double)w.k_in,
                  (double)tokens * w.k_in * 2 + rows_done * w.k_in * 6 / 32 + out_bytes, st);

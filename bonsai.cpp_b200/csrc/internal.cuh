@@ -33,6 +33,10 @@ long long launch_counter();           // launches counted on this thread so far
 void launch_counter_add(long long n);  // account for kernels replayed from a CUDA graph
 bool profiling_active();              // bonsai_profile_start() in effect on this thread  // device address of the per-device error word (lazily resolved)
 int num_sms();
+// Index (0..63) of the current CUDA device: per-device caches of launch set-up
+// (shared-memory attributes, cluster occupancy) are kept per device, since a
+// process may drive several GPUs.
+int device_slot();
 
 // ------------------------------------------------------- B1_0 device weights
 // Device layout ("chunked"): the packed reference layout [N][K/32][6 bytes]

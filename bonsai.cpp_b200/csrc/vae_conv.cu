@@ -601,7 +601,8 @@ ConvKernel conv_kernel_choice() {
 
 template <bool kPair>
 int ensure_smem_attr() {
-  static bool done = false;
+  static bool done_dev[64] = {};
+  bool& done = done_dev[device_slot()];
   if (!done) {
     cudaError_t e = cudaFuncSetAttribute(vconv::conv_kernel<kPair>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -614,7 +615,11 @@ int ensure_smem_attr() {
 
 // Clusters of two conv CTAs that can be resident at once (0 if none).
 int conv_pair_slots() {
-  static int n = -1;
+  struct Slots {
+    int n = -1;
+  };
+  static Slots slots[64];
+  int& n = slots[device_slot()].n;
   if (n >= 0) return n;
   n = 0;
   if (ensure_smem_attr<true>()) return n;
