@@ -75,6 +75,20 @@ def step_flops():
 
 
 # ------------------------------------------------------------ CPU reference
+_JSON_FD = None  # the process's original stdout, kept for the JSON lines only
+
+
+def emit_json(obj) -> None:
+    """Write one JSON line to the original stdout.  Everything else that
+    reaches fd 1 (library banners such as NCCL's version line, stray prints)
+    goes to stderr, so stdout carries the JSON line(s) only."""
+    sys.stdout.flush()
+    data = (json.dumps(obj) + "\n").encode()
+    fd = _JSON_FD if _JSON_FD is not None else 1
+    while data:
+        data = data[os.write(fd, data):]
+
+
 class stdout_to_stderr:
     """Send fd 1 to fd 2 for the duration (the reference's kernel prints a
     banner with fprintf(stdout) on first use; bench.py's stdout must carry the
@@ -242,7 +256,7 @@ def run_reference(args):
                          "sample": cs.describe()},
         "e2e": {"value": round(v, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit_json(line)
     return 0
 
 
@@ -472,7 +486,7 @@ def run_bonsai(args):
                                 "kind": cs.kind, "sample": "mean of 2 samples; each " + cs.describe(),
                                 "sample_seconds": round(sample_s, 2)}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit_json(line)
     model.close()
     if dist:
         dist.destroy_process_group()
@@ -512,7 +526,7 @@ def run_configs(args):
     info = {"cpu_threads": threads, "cpu_model": _cpu_model(), "device": torch.cuda.get_device_name(0)}
     R = O.ref()
     if R is None:
-        print(json.dumps({"configs": "unavailable", "why": "oracle/_ref (the reference's b1 kernel) is not built"}))
+        emit_json({"configs": "unavailable", "why": "oracle/_ref (the reference's b1 kernel) is not built"})
         return 0
     fast = ctypes.CDLL(str(ROOT / "oracle/_build/libbonsai_oracle_fast.so"))
     vp, ci, cf = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
@@ -542,7 +556,7 @@ def run_configs(args):
              "cpu_gflops": round(flop / cms / 1e6, 1), **info}
         if extra:
             d.update(extra)
-        print(json.dumps(d), flush=True)
+        emit_json(d)
 
     rng = np.random.default_rng(1234)
     # ---- C1: one double block
@@ -729,7 +743,7 @@ def run_vae(args):
                                 "cores": os.cpu_count() or 1, "kind": "port",
                                 "sample": f"NumPy f32 restatement, 8x8 latent (128^2 image) in "
                                           f"{s_sec:.2f} s, scaled x{scale:.1f} by FLOPs"}
-    print(json.dumps(line), flush=True)
+    emit_json(line)
     return 0
 
 
@@ -753,13 +767,17 @@ def main():
                     help="instead of the step: the Flux VAE decoder at 1024^2 (the next "
                          "pipeline stage), one JSON line")
     args = ap.parse_args()
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     if args.warmup < 3:
         args.warmup = 3
     if args.vae:
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable":
-                              "the reference's VAE decoder runs on ggml, which its tree does not "
-                              "contain (empty llama.cpp submodule); see cpu_baseline of the --vae line"}))
+            emit_json({"impl": "reference", "unavailable":
+                       "the reference's VAE decoder runs on ggml, which its tree does not "
+                       "contain (empty llama.cpp submodule); see cpu_baseline of the --vae line"})
             return 0
         return run_vae(args)
     if args.configs:
