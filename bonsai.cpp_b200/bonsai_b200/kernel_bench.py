@@ -4,14 +4,19 @@
     python -m bonsai_b200.kernel_bench attention L [--heads H] [--reps R]
     python -m bonsai_b200.kernel_bench conv H W CIN COUT [--k 3] [--bf16] [--reps R]
     python -m bonsai_b200.kernel_bench vae LATENT_H LATENT_W [--reps R]
+    python -m bonsai_b200.kernel_bench ln_modulate ROWS [--reps R]
+    python -m bonsai_b200.kernel_bench qk_norm_rope L [--heads H] [--reps R]
 
 gemm: B1_0 GEMM of M tokens x K inputs -> N outputs (f16 store epilogue) on
 seeded random weights/activations; attention: joint attention over L tokens,
 H heads of 128; conv: one VAE decoder convolution (NHWC f16/bf16 in, f32
 out, bias) on the implicit-GEMM kernel; vae: one whole decode of a
 latent_h x latent_w latent (synthetic weights) with the per-kernel time
-split.  Prints one line: mean time per call over R calls after 3
-warm-up calls (CUDA events on the current stream) and the TFLOP/s.
+split; ln_modulate: LayerNorm + modulate of f32 [ROWS][3072] into f16
+(bytes ROWS*3072*6); qk_norm_rope: Q/K RMSNorm + RoPE in place on f16
+[H][L][128] (bytes H*L*128*4).  Prints one line: mean time per call over R
+calls after 3 warm-up calls (CUDA events on the current stream) and the
+TFLOP/s (GB/s for the two HBM-bound kernels).
 """
 from __future__ import annotations
 
@@ -60,7 +65,15 @@ def main(argv=None) -> int:
     vae.add_argument("lh", type=int)
     vae.add_argument("lw", type=int)
     vae.add_argument("--reps", type=int, default=5)
+    ln = sub.add_parser("ln_modulate")
+    ln.add_argument("rows", type=int)
+    ln.add_argument("--reps", type=int, default=20)
+    qk = sub.add_parser("qk_norm_rope")
+    qk.add_argument("L", type=int)
+    qk.add_argument("--heads", type=int, default=48)
+    qk.add_argument("--reps", type=int, default=20)
     args = ap.parse_args(argv)
+    nbytes = 0.0
 
     import numpy as np
     import torch
@@ -93,6 +106,28 @@ def main(argv=None) -> int:
         ms = e["ms"] / e["launches"]
         flop = 2.0 * args.H * args.W * args.cin * args.cout * args.k * args.k
         desc = f"conv {args.H}x{args.W} {args.cin}->{args.cout} k={args.k} {'bf16' if args.bf16 else 'f16'}"
+    elif args.op == "ln_modulate":
+        R = args.rows
+        x = torch.randn(R, 3072, device="cuda")
+        sh = torch.randn(3072, device="cuda")
+        sc = torch.randn(3072, device="cuda")
+        y = torch.empty(R, 3072, device="cuda", dtype=torch.float16)
+        ms = _time(lambda: bb.check(bb.lib().bonsai_ln_modulate(
+            x.data_ptr(), R, 3072, sh.data_ptr(), sc.data_ptr(), 1e-6, y.data_ptr(), 3072,
+            bb.stream_ptr()), "bonsai_ln_modulate"), args.reps)
+        flop, nbytes = 0.0, R * 3072 * 6.0
+        desc = f"ln_modulate rows={R} dim=3072"
+    elif args.op == "qk_norm_rope":
+        H, L = args.heads, args.L
+        qkt = torch.randn(H, L, 128, device="cuda").half()
+        w = torch.ones(128, device="cuda")
+        cs = torch.rand(L, 64, device="cuda")
+        sn = torch.rand(L, 64, device="cuda")
+        ms = _time(lambda: bb.check(bb.lib().bonsai_qk_norm_rope(
+            qkt.data_ptr(), H, L, 128, w.data_ptr(), w.data_ptr(), 0, 1e-6, cs.data_ptr(),
+            sn.data_ptr(), bb.stream_ptr()), "bonsai_qk_norm_rope"), args.reps)
+        flop, nbytes = 0.0, H * L * 128 * 4.0
+        desc = f"qk_norm_rope heads={H} L={L}"
     elif args.op == "vae":
         import json
         v = bb.Vae(args.lh, args.lw, seed=1)
@@ -120,7 +155,9 @@ def main(argv=None) -> int:
         flop = 4.0 * L * L * 128 * H
         desc = f"attention L={L} heads={H}"
     err = bb.device_error()
-    print(f"{desc}: {ms * 1e3:.1f} us/call, {flop / (ms / 1e3) / 1e12:.1f} TFLOP/s, device_error={err}")
+    rate = (f"{nbytes / (ms / 1e3) / 1e9:.0f} GB/s" if nbytes else
+            f"{flop / (ms / 1e3) / 1e12:.1f} TFLOP/s")
+    print(f"{desc}: {ms * 1e3:.1f} us/call, {rate}, device_error={err}")
     return 0 if err == 0 else 1
 
 
