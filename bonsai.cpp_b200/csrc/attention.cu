@@ -70,6 +70,9 @@ constexpr int TMEM_COLS = 512;
 constexpr int S_COL = 0, O_COL = 256;
 constexpr int SMEM_BYTES = 1024 + 2 * Q_BYTES + (KS + VS) * KV_BYTES + 512;
 constexpr float kRescaleThreshold = 8.0f;
+// Row-sum bound of a block computed against the running max: above it the
+// block is redone with its own max (2^15: every P then fits f16).
+constexpr float kSpeculativeSumLimit = 32768.0f;
 // Pairs of a row whose exponentials take the polynomial (bit k: pair
 // positions k mod 16); the rest go to the MUFU.  Measured best: 2 of 16 for
 // the one-CTA kernel, 5 of 16 for the CTA pair (whose tensor-core side is
@@ -134,13 +137,16 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 // mantissa bits of t) and f in [-0.5, 0.5]; 2^f by a degree-3 polynomial
 // (coefficients from a Remez exchange on the relative error, max 7.5e-5,
 // below the f16 rounding of P); 2^n added to the exponent field.  x is
-// clamped at -126 so that n + the exponent of 2^f stays >= 0; results below
-// 2^-126 are not needed (P is rounded to f16).
+// clamped to [-126, 126] so that n + the exponent of 2^f stays a valid
+// exponent: results below 2^-126 are not needed (P is rounded to f16), and a
+// large x (a block computed against a stale running max) still gives a large
+// finite P, which the row-sum check catches.
 constexpr float kRoundShift = 12582912.0f;  // 1.5 * 2^23
 __device__ __forceinline__ void ex2_poly2(unsigned long long x2, float& a, float& b) {
   float x0, x1;
   unpack2(x2, x0, x1);
-  const unsigned long long xc = pack2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const unsigned long long xc =
+      pack2(fminf(fmaxf(x0, -126.0f), 126.0f), fminf(fmaxf(x1, -126.0f), 126.0f));
   const unsigned long long t = add2(xc, pack2(kRoundShift, kRoundShift));
   const unsigned long long r = add2(t, pack2(-kRoundShift, -kRoundShift));
   const unsigned long long f = fma2(r, pack2(-1.0f, -1.0f), xc);
@@ -453,37 +459,70 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int c = 0; c < BKV; ++c)
           if (kbase + c >= p.seq) s[c] = -INFINITY;
       }
-      // Row max as 8 independent chains, then a tree.
-      float m8[8];
+      // Row max as 8 independent chains, then a tree (log2 domain).
+      auto row_max = [&]() -> float {
+        float m8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = fmaxf(s[i], s[8 + i]);
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(s[i], s[8 + i]);
 #pragma unroll
-      for (int c = 16; c < BKV; c += 16) {
+        for (int c = 16; c < BKV; c += 16) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = max3f(m8[i], s[c + i], s[c + 8 + i]);
-      }
-      float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
-      mx *= p.scale_log2;
-      float alpha = 1.0f;
-      if (j == 0) {
-        m = mx;
-      } else if (mx > m + kRescaleThreshold) {
-        alpha = ex2(m - mx);
-        m = mx;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-        // O_g is rescaled once P_g(j - 1) V_{j-1} has completed (it may still
-        // be in flight: S runs ahead of P V).  P_g(j) V_j waits for this
-        // block's p_ready, so nothing else writes O_g meanwhile.
-        const int pb = (j - 1) & 1;
-        bool good2 = wait_bar(&pv_done[g * 2 + pb], ((j - 1) >> 1) & 1, abort_flag, p.err,
-                              DEV_ERR_TIMEOUT_SOFTMAX);
-        if (!__all_sync(0xffffffffu, good2)) {
-          ok = false;
-          break;
+          for (int i = 0; i < 8; ++i) m8[i] = max3f(m8[i], s[c + i], s[c + 8 + i]);
         }
-        tc_fence_after();
-        {
+        return max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]),
+                     fmaxf(m8[6], m8[7])) * p.scale_log2;
+      };
+      // P = 2^(s * scale - mref) into the first half of this S buffer; returns
+      // the row sum of P (f32, before the f16 rounding).
+      auto exps = [&](float mref) -> float {
+        unsigned long long rs2[4] = {0ull, 0ull, 0ull, 0ull};
+        const unsigned long long sc2 = pack2(p.scale_log2, p.scale_log2);
+        const unsigned long long nm2 = pack2(-mref, -mref);
+#pragma unroll
+        for (int ch = 0; ch < BKV / 32; ++ch) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int c = ch * 16 + i;
+            const unsigned long long x2 = fma2(pack2(s[2 * c], s[2 * c + 1]), sc2, nm2);
+            float a, b;
+            if (((kPair ? kPolyPairsPair : kPolyPairsSingle) >> i) & 1) {
+              ex2_poly2(x2, a, b);
+            } else {
+              float x0, x1;
+              unpack2(x2, x0, x1);
+              a = ex2(x0);
+              b = ex2(x1);
+            }
+            rs2[c & 3] = add2(rs2[c & 3], pack2(a, b));
+            pk[i] = cvt_h2(a, b);
+          }
+          tmem_st16(s_addr + ch * 16, pk);
+        }
+        float rsv[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) unpack2(rs2[i], rsv[2 * i], rsv[2 * i + 1]);
+        return ((rsv[0] + rsv[1]) + (rsv[2] + rsv[3])) + ((rsv[4] + rsv[5]) + (rsv[6] + rsv[7]));
+      };
+      float alpha = 1.0f;
+      float rs = 0.0f;
+      // This block's max; the running max moves (and O_g is rescaled) only
+      // when it exceeds it by more than kRescaleThreshold.  False on timeout.
+      auto rescale_step = [&]() -> bool {
+        const float mx = row_max();
+        if (mx > m + kRescaleThreshold) {
+          alpha = ex2(m - mx);
+          m = mx;
+        }
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+          // O_g is rescaled once P_g(j - 1) V_{j-1} has completed (it may
+          // still be in flight: S runs ahead of P V).  P_g(j) V_j waits for
+          // this block's p_ready, so nothing else writes O_g meanwhile.
+          const int pb = (j - 1) & 1;
+          bool good2 = wait_bar(&pv_done[g * 2 + pb], ((j - 1) >> 1) & 1, abort_flag, p.err,
+                                DEV_ERR_TIMEOUT_SOFTMAX);
+          if (!__all_sync(0xffffffffu, good2)) return false;
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
@@ -494,35 +533,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st32(o_addr + c * 32, r);
           }
         }
+        return true;
+      };
+      // CTA pair: from the second block on, the exponentials are first taken
+      // against the running max, without this block's max.  Every P is <=
+      // the row sum, so a row sum <= 2^15 means every P fits f16 (and is as
+      // precise there as any other value); only when some row's sum exceeds
+      // it (a block max more than ~9 above the running max, rare after the
+      // first blocks) is the block redone the usual way.  One copy of the
+      // exponential code serves both passes.  (The one-CTA form measured
+      // slower this way and keeps the max first.)
+      constexpr bool kSpeculative = kPair;
+      if (j == 0) {
+        m = row_max();
+      } else if (!kSpeculative && !rescale_step()) {
+        ok = false;
+        break;
       }
-      unsigned long long rs2[4] = {0ull, 0ull, 0ull, 0ull};
-      const unsigned long long sc2 = pack2(p.scale_log2, p.scale_log2);
-      const unsigned long long nm2 = pack2(-m, -m);
-#pragma unroll
-      for (int ch = 0; ch < BKV / 32; ++ch) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c = ch * 16 + i;
-          const unsigned long long x2 = fma2(pack2(s[2 * c], s[2 * c + 1]), sc2, nm2);
-          float a, b;
-          if (((kPair ? kPolyPairsPair : kPolyPairsSingle) >> i) & 1) {
-            ex2_poly2(x2, a, b);
-          } else {
-            float x0, x1;
-            unpack2(x2, x0, x1);
-            a = ex2(x0);
-            b = ex2(x1);
-          }
-          rs2[c & 3] = add2(rs2[c & 3], pack2(a, b));
-          pk[i] = cvt_h2(a, b);
+#pragma unroll 1
+      for (int pass = 0; pass < 2; ++pass) {
+        rs = exps(m);
+        if (!kSpeculative || j == 0 || pass == 1 ||
+            !__any_sync(0xffffffffu, !(rs <= kSpeculativeSumLimit)))
+          break;
+        if (!rescale_step()) {
+          ok = false;
+          break;
         }
-        tmem_st16(s_addr + ch * 16, pk);
+        tmem_wait_st();  // the first pass's P stores land before they are overwritten
       }
-      float rsv[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) unpack2(rs2[i], rsv[2 * i], rsv[2 * i + 1]);
-      const float rs = ((rsv[0] + rsv[1]) + (rsv[2] + rsv[3])) + ((rsv[4] + rsv[5]) + (rsv[6] + rsv[7]));
+      if (!ok) break;
       l = l * alpha + rs;
       tmem_wait_st();
       tc_fence_before();
