@@ -64,7 +64,7 @@ def test_attention_vs_oracle(gpu, attn_form, seq, H):
 
 def test_attention_default_is_the_pair_form(gpu, monkeypatch):
     """On a B200 the default launch is the CTA-pair kernel: its results differ
-    in the last bits from the one-CTA form's (5/16 vs 2/16 of the
+    in the last bits from the one-CTA form's (4/16 vs 2/16 of the
     exponentials on the polynomial) while both meet the tolerance."""
     rng = np.random.default_rng(11)
     seq, H = 700, 2
