@@ -63,8 +63,10 @@ def peaks():
     return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
 
 
-def step_flops():
+def step_flops(L=None, IMG=None):
     """Algorithmic FLOPs of one step (GEMM 2*M*N*K, attention 4*L^2*D*H)."""
+    L = L or globals()["L"]
+    IMG = IMG or globals()["IMG"]
     attn = 4.0 * L * L * HD * HEADS
     dbl = 2.0 * L * H * (3 * H + H + MLP) + 2.0 * L * MLP * H + attn
     sgl = 2.0 * L * H * (3 * H + MLP) + 2.0 * L * (H + MLP) * H + attn
@@ -111,18 +113,19 @@ class CpuSample:
 
     One double block and one single block at the full token count
     (L = 4608), with the reference's own b1_linear_f32_f32 (AVX2 build in
-    oracle/_ref, all host threads) on 1/row_frac of each linear's output
-    rows, attention for `heads` of the 24 heads, and the remaining ops
+    oracle/_ref, all host threads) on every output row of each linear,
+    attention for `heads` of the 24 heads, and the remaining ops
     (LayerNorm-modulate, Q/K RMSNorm + RoPE, GELU) in full through the CPU
     restatement of the ggml built-ins.  Each part's time is scaled by the
     work it skipped, then ms/step = 19 * double + 38 * single + edges.
-    The bench line's cpu_baseline uses every output row and 4 heads (about
-    10-20 s of CPU work on a 16-core host); the --impl reference arm times a
-    lighter sample per step so that its K + W steps finish in minutes.
+    Both the bench line's cpu_baseline and the --impl reference arm use
+    every output row and 4 heads (about 5-10 s of CPU work per sample on a
+    16-core host); the reference kernel runs on a persistent worker pool
+    (oracle/ref_bridge.cpp), as ggml's CPU backend does.
     """
 
-    def __init__(self, threads: int, row_frac: int = 1, heads: int = 4):
-        self.ROW_FRAC = row_frac
+    def __init__(self, threads: int, heads: int = 4):
+        self.ROW_FRAC = 1
         self.heads = heads
         import ctypes
         from oracle import pyoracle as O
@@ -169,7 +172,8 @@ class CpuSample:
         return self.w[key]
 
     def _lin(self, tokens, K, N, row_frac=None):
-        """Time the reference B1 kernel on N/row_frac rows; return the full-N estimate (s)."""
+        """Time the reference B1 kernel on N/row_frac rows (all rows unless given);
+        return the full-N estimate (s)."""
         O = self.O
         n = max(1, N // (row_frac or self.ROW_FRAC))
         w = self._packed(n, K)
@@ -218,8 +222,9 @@ class CpuSample:
         sgl = self._ln(L) + self._qk() + self._attn() + self._gelu(L)
         sgl += self._lin(L, H, 3 * H + MLP) + self._lin(L, H + MLP, H)
         # one token x 1.05 M modulation rows: sampled at 1/16 of the rows (a
-        # full-size packed copy would be 0.6 GB of host memory)
-        mods = self._lin(1, H, DEPTH * 12 * H + SINGLE * 3 * H, row_frac=max(16, self.ROW_FRAC))
+        # full-size packed copy would be 0.6 GB of host memory; a GEMV of one
+        # token is a small share of the step either way)
+        mods = self._lin(1, H, DEPTH * 12 * H + SINGLE * 3 * H, row_frac=16)
         edges = self._lin(TXT, CTX, H)  # text embedder (dominant edge op), B1-rate proxy
         ms = 1000.0 * (DEPTH * dbl + SINGLE * sgl + mods + edges)
         return ms, time.perf_counter() - t_start
@@ -232,13 +237,33 @@ class CpuSample:
                 f"of the ggml built-ins); scaled to 19 double + 38 single blocks + modulation + edges")
 
 
+def step_config(world: int, split: bool = False, exchange: str = "fused") -> dict:
+    """The bench line's `config`, identical in both arms for the same N."""
+    if split:
+        par = (f"head/row split over {world} GPUs, exchanges fused into the producing kernels "
+               "over peer memory (CUDA IPC), one-element all-reduce per phase for ordering"
+               if exchange == "fused" else
+               f"head/row split over {world} GPUs (NCCL all-gather + all-to-all per block)")
+    else:
+        par = f"dp{world} (one image per GPU, no collective)"
+    return {"workload": WORKLOAD_2048 if split else WORKLOAD,
+            "global_batch": 1 if split else world, "img_tokens": IMG, "txt_tokens": TXT,
+            "parallelism": par,
+            "l2": "inputs larger than L2: every step streams all 2.2 GB of B1_0 weights"}
+
+
 def run_reference(args):
+    """--impl reference: the reference's CPU path on this host's cores, one
+    bounded sample per step -- the same sample as the GPU arm's cpu_baseline
+    leg (one double + one single block at L = 4608, every output row of every
+    B1_0 linear through the reference's own kernel, 4 of 24 attention heads),
+    scaled to the 57 blocks + modulation + edges.  Only rank 0 works."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
     with stdout_to_stderr():
-        cs = CpuSample(threads, row_frac=16, heads=1)
+        cs = CpuSample(threads)
         for _ in range(args.warmup):
             cs.run()
         vals = []
@@ -251,9 +276,10 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 1),
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": WORKLOAD, "parallelism": "host threads", "l2": "n/a (CPU)"},
+        "config": step_config(args.gpus),
         "cpu_baseline": {"value": round(v, 1), "unit": "ms", "cores": threads, "kind": cs.kind,
-                         "sample": cs.describe()},
+                         "sample": f"mean of {args.steps} samples; each " + cs.describe(),
+                         "spread_ms": [round(min(vals), 1), round(max(vals), 1)]},
         "e2e": {"value": round(v, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit_json(line)
@@ -305,6 +331,126 @@ class ClockSampler:
         reasons = sorted({names[j] for r in rows for j in range(4) if r[5 + j].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def measure_split_2048(args, rank: int, world: int, dist) -> dict:
+    """BASELINE config 5(b) beside the headline: one 2048^2 image (16384 image +
+    512 text tokens, all 57 blocks) split by heads and token rows over the
+    `world` GPUs of this run (one GPU: the plain step), outside the headline's
+    timed region.  Every rank calls it (it takes collective steps).
+
+    ms_per_step: device time of `split_steps` steps (CUDA events on the
+    launching stream, barrier + synchronize on both sides, max over ranks).
+    e2e_ms: the same with the step's inputs copied in from pinned host memory
+    and the prediction copied back, inside the timed region.  phase_ms: one
+    more step with a CUDA-event pair around every phase and exchange, summed
+    per stage (max over ranks); on one GPU the phases run unsplit, without
+    exchanges.  parity_vs_unsplit (N > 1): rank 0 runs the unpartitioned
+    forward of the same model on the same inputs and compares (cos, max-abs /
+    RMS)."""
+    import torch
+    import bonsai_b200 as bb
+    from bonsai_b200 import headsplit
+    img_n, grid = 16384, 128
+    m = bb.Dit(bb.PRESET_FLUX1, img_n, TXT, grid, grid, seed=1234)
+    if world > 1:
+        m.set_partition(rank, world)
+        if args.exchange == "fused":
+            headsplit.enable_fused(m)
+    rng = np.random.default_rng(2048)  # one shared image on every rank
+    img_h = torch.from_numpy(rng.standard_normal((img_n, IN_CH)).astype(np.float32)).pin_memory()
+    txt_h = torch.from_numpy(rng.standard_normal((TXT, CTX)).astype(np.float32)).pin_memory()
+    pooled_h = torch.from_numpy(rng.standard_normal(POOLED).astype(np.float32)).pin_memory()
+    out_h = torch.empty(img_n, IN_CH).pin_memory()
+    img_d, txt_d, pooled_d = img_h.cuda(), txt_h.cuda(), pooled_h.cuda()
+    out_d = torch.empty(img_n, IN_CH, device="cuda")
+    K, W = args.split_steps, max(3, args.split_warmup)
+    ts = [1000.0 * (1.0 - (i % 4) / 4.0) for i in range(max(K, W))]
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def step(t, timers=None):
+        headsplit.forward(m, img_d, txt_d, pooled_d, t, out_d, timers=timers,
+                          phased=timers is not None)
+
+    def timed(fn):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(K):
+            fn(ts[i])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / K)
+
+    for i in range(W):
+        step(ts[i])
+    torch.cuda.synchronize()
+    assert bb.device_error() == 0
+    ms = timed(step)
+
+    def step_host(t):  # pinned host inputs in, prediction out, inside the timed region
+        img_d.copy_(img_h, non_blocking=True)
+        txt_d.copy_(txt_h, non_blocking=True)
+        pooled_d.copy_(pooled_h, non_blocking=True)
+        step(t)
+        out_h.copy_(out_d, non_blocking=True)
+        stream.synchronize()
+    ms_e2e = timed(step_host)
+
+    timers = []
+    barrier()
+    torch.cuda.synchronize()
+    step(ts[0], timers)
+    torch.cuda.synchronize()
+    pt = headsplit.phase_times(timers)
+    # every rank ran the same stages, so the key set (and the order of the
+    # reductions below) is the same on all ranks
+    phase_ms = {k: round(max_over_ranks(pt[k]), 3) for k in sorted(pt)}
+    assert bb.device_error() == 0
+
+    res = {"n_gpus": world, "ms_per_step": round(ms, 3), "e2e_ms": round(ms_e2e, 3),
+           "steps": K, "warmup": W, "img_tokens": img_n, "txt_tokens": TXT,
+           "exchange": (args.exchange if world > 1 else "none (one GPU: the plain step)"),
+           "images_per_s": round(1000.0 / ms, 3),
+           "step_tflops": round(step_flops(img_n + TXT, img_n) / (ms / 1e3) / 1e12, 1),
+           "phase_ms": phase_ms,
+           "phase_ms_note": "one extra step, a CUDA-event pair around every phase and exchange "
+                            "call, summed per stage, max over ranks"}
+    step(ts[0])
+    torch.cuda.synchronize()
+    split_out = out_d.clone()
+    if world > 1:
+        parity = None
+        if rank == 0:  # the unpartitioned forward of the same weights on the same inputs
+            m.set_partition(0, 1)
+            ref = torch.empty_like(out_d)
+            m.forward(img_d, txt_d, pooled_d, ts[0], ref)
+            torch.cuda.synchronize()
+            g, r = split_out.double().flatten(), ref.double().flatten()
+            parity = {"cos": round(float(g @ r / (g.norm() * r.norm())), 8),
+                      "maxabs_rms": float((g - r).abs().max() / r.pow(2).mean().sqrt()),
+                      "vs": "unpartitioned bonsai_dit_forward of the same model on rank 0"}
+        barrier()
+        res["parity_vs_unsplit"] = parity
+    else:
+        res["parity_vs_unsplit"] = {"note": "one GPU: the split is the unpartitioned step"}
+    res["output_finite"] = bool(torch.isfinite(split_out).all().item())
+    assert bb.device_error() == 0
+    m.close()
+    return res
 
 
 def run_bonsai(args):
@@ -441,16 +587,7 @@ def run_bonsai(args):
         "warmup": W, "ms_per_step": round(ms, 3), "higher_is_better": False,
         "scaling": "strong" if split else "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": WORKLOAD_2048 if split else WORKLOAD,
-                   "global_batch": 1 if split else world, "img_tokens": IMG,
-                   "txt_tokens": TXT,
-                   "parallelism": ((f"head/row split over {world} GPUs, exchanges fused into the "
-                                    "producing kernels over peer memory (CUDA IPC), one-element "
-                                    "all-reduce per phase for ordering"
-                                    if args.exchange == "fused" else
-                                    f"head/row split over {world} GPUs (NCCL all-gather + all-to-all per block)")
-                                   if split else f"dp{world} (one image per GPU, no collective)"),
-                   "l2": "inputs larger than L2: every step streams all 2.2 GB of B1_0 weights"},
+        "config": step_config(world, split, args.exchange),
         "images_per_s": round((1 if split else world) * 1000.0 / ms, 3),
         "step_tflops": round(step_flops() / (ms / 1e3) / 1e12 * (1 if split else world), 1),
         "roofline": {"bound": "tensor", "kernel": "b1_gemm", "achieved": round(gemm_tf, 1),
@@ -485,9 +622,11 @@ def run_bonsai(args):
         line["cpu_baseline"] = {"value": round(cpu_ms, 1), "unit": "ms", "cores": threads,
                                 "kind": cs.kind, "sample": "mean of 2 samples; each " + cs.describe(),
                                 "sample_seconds": round(sample_s, 2)}
+    model.close()
+    if not split and not args.no_split:
+        line["split_2048"] = measure_split_2048(args, rank, world, dist)
     if rank == 0:
         emit_json(line)
-    model.close()
     if dist:
         dist.destroy_process_group()
     return 0
@@ -760,6 +899,12 @@ def main():
     ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
                     help="--workload 2048 on N > 1 GPUs: exchanges fused into the kernels over "
                          "peer memory (default) or NCCL collectives between the phases")
+    ap.add_argument("--no-split", action="store_true",
+                    help="skip the 2048^2 head/row-split measurement (split_2048) that every "
+                         "default run adds beside the headline")
+    ap.add_argument("--split-steps", type=int, default=10,
+                    help="timed steps of the split_2048 measurement")
+    ap.add_argument("--split-warmup", type=int, default=3)
     ap.add_argument("--configs", action="store_true",
                     help="instead of the step: BASELINE configs 1-3, GPU vs the reference CPU "
                          "path, one JSON line per config")

@@ -21,7 +21,7 @@ and the data moves between the phases in one of two ways:
     the rows of `xm` (phase 0 -> 1) and an all-to-all of the attention output
     in `cat` (every rank holds its heads' columns for every row and needs
     every head's columns for its own rows).
-The reference has no multi-device path (SURVEY: single process).
+The reference has no multi-device path: it runs in one process on one device.
 """
 from __future__ import annotations
 
@@ -70,35 +70,84 @@ def _order(token: torch.Tensor, group) -> None:
     dist.all_reduce(token, group=group)
 
 
-def forward(model, img, txt, pooled, t: float, out, group=None) -> None:
+class _Span:
+    """Records a (name, start, end) pair of CUDA events on the current stream
+    into `timers` around a block of issued work (no-op when timers is None)."""
+
+    def __init__(self, timers, name):
+        self.timers, self.name = timers, name
+
+    def __enter__(self):
+        if self.timers is not None:
+            self.e0 = torch.cuda.Event(enable_timing=True)
+            self.e0.record()
+        return self
+
+    def __exit__(self, *exc):
+        if self.timers is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            self.timers.append((self.name, self.e0, e1))
+
+
+def phase_times(timers) -> dict:
+    """Sum the event pairs recorded by forward(timers=...) per name (ms);
+    call after the stream has been synchronised."""
+    out = {}
+    for name, e0, e1 in timers:
+        out[name] = out.get(name, 0.0) + e0.elapsed_time(e1)
+    return out
+
+
+def forward(model, img, txt, pooled, t: float, out, group=None, timers=None,
+            phased: bool = False) -> None:
     """One denoise-step forward of a partitioned bonsai_b200.Dit.  img/txt/
     pooled are the full inputs (device tensors) on every rank; out
-    [img_tokens][in_ch] receives the full prediction on every rank."""
-    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+    [img_tokens][in_ch] receives the full prediction on every rank.
+
+    timers: optional list; a (name, start event, end event) triple is
+    appended for every stage -- "edges" (begin + end), "phase0", "phase1",
+    "phase2", and the exchanges ("order" for the fused form's ordering
+    all-reduce, "xm_gather" / "cat_exchange" for the NCCL form, "hidden_gather")
+    -- for a per-phase breakdown (phase_times).  phased: on one rank, run the
+    phase entry points instead of the replayed step graph (same result; used
+    for the one-GPU breakdown)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1 and not phased and timers is None:
         model.forward(img, txt, pooled, t, out)  # one rank: the plain (graph-replayed) step
         return
-    rank = dist.get_rank(group)
-    world = dist.get_world_size(group)
+    rank = dist.get_rank(group) if world > 1 else 0
     L = model.L
     C = H + model.mlp
     xm = model.buffer("xm", torch.float16, (L, H))
     cat = model.buffer("cat", torch.float16, (L, C))
     hidden = model.buffer("hidden", torch.float32, (L, H))
-    fused = getattr(model, "fused_exchange", False)
+    fused = world > 1 and getattr(model, "fused_exchange", False)
     token = torch.zeros(1, dtype=torch.int32, device="cuda") if fused else None
-    model.begin(img, txt, pooled, t)
+    with _Span(timers, "edges"):
+        model.begin(img, txt, pooled, t)
     for kind, n in ((0, model.depth), (1, model.depth_single)):
         for i in range(n):
-            model.phase(kind, i, 0)
+            with _Span(timers, "phase0"):
+                model.phase(kind, i, 0)
             if fused:
-                _order(token, group)
-            else:
-                gather_rows_inplace(xm, rank, world, group)
-            model.phase(kind, i, 1)
+                with _Span(timers, "order"):
+                    _order(token, group)
+            elif world > 1:
+                with _Span(timers, "xm_gather"):
+                    gather_rows_inplace(xm, rank, world, group)
+            with _Span(timers, "phase1"):
+                model.phase(kind, i, 1)
             if fused:
-                _order(token, group)
-            else:
-                heads_to_rows(cat, H, rank, world, group)
-            model.phase(kind, i, 2)
-    gather_rows_inplace(hidden, rank, world, group)
-    model.end(out)
+                with _Span(timers, "order"):
+                    _order(token, group)
+            elif world > 1:
+                with _Span(timers, "cat_exchange"):
+                    heads_to_rows(cat, H, rank, world, group)
+            with _Span(timers, "phase2"):
+                model.phase(kind, i, 2)
+    if world > 1:
+        with _Span(timers, "hidden_gather"):
+            gather_rows_inplace(hidden, rank, world, group)
+    with _Span(timers, "edges"):
+        model.end(out)

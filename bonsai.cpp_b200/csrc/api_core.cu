@@ -45,12 +45,32 @@ DeviceInfo& dev_info() {
   return di;
 }
 
-// Scratch f16 copy of the f32 activations used by bonsai_b1_linear_f32.
+// Scratch f16 copy of the f32 activations used by bonsai_b1_linear_f32, one
+// per (device, stream) of the calling thread: calls on different streams
+// never share a buffer, so one stream's call cannot overwrite the copy that
+// another stream's GEMM is still reading, and a buffer is grown or freed only
+// in the order of its own stream.  `done` is recorded after every use and
+// waited on by the next one, which keeps a buffer safe even when a destroyed
+// stream's handle is reused by a new stream while the old work still runs.
 struct Scratch {
+  int device = -1;
+  cudaStream_t stream = nullptr;
   void* ptr = nullptr;
   size_t bytes = 0;
+  cudaEvent_t done = nullptr;
 };
-thread_local Scratch g_scratch[64];
+thread_local std::vector<Scratch> g_scratch;
+
+Scratch* scratch_for(int device, cudaStream_t st) {
+  for (auto& s : g_scratch)
+    if (s.device == device && s.stream == st) return &s;
+  Scratch s;
+  s.device = device;
+  s.stream = st;
+  if (cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  g_scratch.push_back(s);
+  return &g_scratch.back();
+}
 
 __global__ void f32_to_f16_kernel(const float* __restrict__ src, __half* __restrict__ dst,
                                   long long n) {
@@ -151,6 +171,11 @@ int launch_f32_to_f16(const float* src, __half* dst, long long n, cudaStream_t s
 
 using namespace bonsai;
 
+#define RC_CUDA(call, what)                                \
+  do {                                                     \
+    const cudaError_t _e = (call);                         \
+    if (_e != cudaSuccess) return cuda_status(_e, (what)); \
+  } while (0)
 
 extern "C" {
 
@@ -186,10 +211,15 @@ int bonsai_shutdown(void) {
   int d = 0;
   cudaGetDevice(&d);
   const cudaError_t e = cudaDeviceSynchronize();
-  Scratch& sc = g_scratch[d & 63];
-  if (sc.ptr) {
-    cudaFree(sc.ptr);
-    sc = Scratch{};
+  for (size_t i = 0; i < g_scratch.size();) {
+    Scratch& sc = g_scratch[i];
+    if (sc.device != d) {
+      ++i;
+      continue;
+    }
+    if (sc.ptr) cudaFree(sc.ptr);
+    if (sc.done) cudaEventDestroy(sc.done);
+    g_scratch.erase(g_scratch.begin() + i);
   }
   for (auto& r : g_prof) {
     cudaEventDestroy(r.e0);
@@ -335,6 +365,11 @@ int bonsai_b1_gemm(const uint16_t* x, long long ldx, int tokens, bonsai_b1_t h, 
   if (tokens == 0) return 0;
   if (!out) return fail(BONSAI_ERR_ARG, "b1_gemm: null output");
   const B1Weight& w = h->w;
+  int dev = 0;
+  RC_CUDA(cudaGetDevice(&dev), "b1_gemm: cudaGetDevice");
+  if (dev != w.device)
+    return fail(BONSAI_ERR_ARG, "b1_gemm: the weight lives on device " + std::to_string(w.device) +
+                                    ", the current device is " + std::to_string(dev));
   EpiSeg seg;
   seg.row_begin = 0;
   seg.row_end = w.n_rows;
@@ -364,21 +399,31 @@ int bonsai_b1_linear_f32(const float* act, int tokens, bonsai_b1_t h, float* out
   if (tokens == 0) return 0;  // empty batch: nothing to do (pointers may be null)
   if (!act || !out) return fail(BONSAI_ERR_ARG, "b1_linear_f32: null tensor");
   const B1Weight& w = h->w;
+  int dev = 0;
+  RC_CUDA(cudaGetDevice(&dev), "b1_linear_f32: cudaGetDevice");
+  if (dev != w.device)
+    return fail(BONSAI_ERR_ARG, "b1_linear_f32: the weight lives on device " +
+                                    std::to_string(w.device) + ", the current device is " +
+                                    std::to_string(dev));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // f16 copy of the activations; K is padded to a multiple of 8 so that
   // the TMA row pitch is 16-byte aligned (K % 32 == 0 already guarantees it).
   const long long n = (long long)tokens * w.k_in;
-  Scratch& sc = g_scratch[w.device & 63];
+  Scratch* sc = scratch_for(dev, st);
+  if (!sc) return fail(BONSAI_ERR_CUDA, "b1_linear_f32: scratch event creation failed");
+  // the previous use of this buffer (in this stream's order, or of a stream
+  // that had the same handle) has finished before it is overwritten or freed
+  RC_CUDA(cudaStreamWaitEvent(st, sc->done, 0), "b1_linear_f32: wait for the scratch");
   const size_t need = (size_t)n * sizeof(__half);
-  if (sc.bytes < need) {
-    if (sc.ptr) cudaFreeAsync(sc.ptr, st);
-    sc.ptr = nullptr;
-    sc.bytes = 0;
-    cudaError_t e = cudaMallocAsync(&sc.ptr, need, st);
+  if (sc->bytes < need) {
+    if (sc->ptr) cudaFreeAsync(sc->ptr, st);
+    sc->ptr = nullptr;
+    sc->bytes = 0;
+    cudaError_t e = cudaMallocAsync(&sc->ptr, need, st);
     if (e != cudaSuccess) return fail(BONSAI_ERR_NOMEM, "b1_linear_f32: scratch allocation failed");
-    sc.bytes = need;
+    sc->bytes = need;
   }
-  int rc = launch_f32_to_f16(act, static_cast<__half*>(sc.ptr), n, st);
+  int rc = launch_f32_to_f16(act, static_cast<__half*>(sc->ptr), n, st);
   if (rc) return rc;
   EpiSeg seg;
   seg.mode = EPI_F32;
@@ -386,7 +431,9 @@ int bonsai_b1_linear_f32(const float* act, int tokens, bonsai_b1_t h, float* out
   seg.row_end = w.n_rows;
   seg.dst = out;
   seg.ld = w.n_rows;
-  return launch_b1_gemm(sc.ptr, w.k_in, tokens, w, &seg, 1, false, st);
+  rc = launch_b1_gemm(sc->ptr, w.k_in, tokens, w, &seg, 1, false, st);
+  if (rc) return rc;
+  return cuda_status(cudaEventRecord(sc->done, st), "b1_linear_f32: record the scratch's use");
 }
 
 }  // extern "C"

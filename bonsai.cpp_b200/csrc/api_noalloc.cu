@@ -3,9 +3,9 @@
 //
 // bonsai_b1_linear_f32 keeps an f16 copy of the activations in a scratch
 // buffer that it grows with cudaMallocAsync.  Some hosts cannot allow that:
-// a ggml-style backend whose graph allocator owns every device byte, code
-// that records the call into a CUDA graph, or a latency-critical loop where
-// an allocation (and the synchronisation it may cause) is not acceptable.
+// a ggml-style backend whose graph allocator owns every device byte, or a
+// latency-critical loop where an allocation (and the synchronisation it may
+// cause) is not acceptable.
 // This entry point instead uses one fixed array that lives in the library's
 // device image: kNoAllocMaxElems f16 values (8 MiB), which every GPU that
 // loads the library keeps reserved until the process exits.
@@ -66,6 +66,12 @@ extern "C" int bonsai_b1_linear_f32_noalloc(const float* act, int tokens, bonsai
   __half* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != w.device)
+    return fail(BONSAI_ERR_ARG, "b1_linear_f32_noalloc: the weight lives on device " +
+                                    std::to_string(w.device) + ", the current device is " +
+                                    std::to_string(dev));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // Every element the GEMM reads (tokens x in_dim) is written here first, so
   // nothing is left over from an earlier call's contents.

@@ -111,23 +111,27 @@ int bonsai_b1_shape(bonsai_b1_t w, int* out_dim, int* in_dim);
  *   out[t][r] = sum_blk scale[r][blk] * sum_i (bit ? +act : -act)
  * act: f32 [tokens][in_dim]; out: f32 [tokens][out_dim].
  * The activations are rounded to f16 for the tensor cores (f32
- * accumulation).  Uses an internal scratch buffer for the f16 copy of act,
- * grown on demand with cudaMallocAsync on the given stream. */
+ * accumulation).  The f16 copy of act lives in a scratch buffer the library
+ * keeps per (calling thread, device, stream), grown on demand with
+ * cudaMallocAsync on that stream and released by bonsai_shutdown: calls on
+ * different streams never share a buffer, so they may overlap on the GPU.
+ * The weight must live on the current device (BONSAI_ERR_ARG otherwise). */
 int bonsai_b1_linear_f32(const float* act, int tokens, bonsai_b1_t w, float* out, void* stream);
 
 /* Same operation as bonsai_b1_linear_f32, for callers that cannot let the
  * library allocate device memory (no counterpart in the reference).  Hosts
  * that own every device byte through their own allocator (a ggml graph
- * allocator), code being recorded into a CUDA graph, or loops that must not
- * block on an allocation use this form: it calls no cudaMalloc/cudaFree or
- * allocating library routine.  The f16 copy of act lives in one fixed
- * 8 MiB device array inside the library (tokens * in_dim <= 4,194,304
- * elements; larger calls return BONSAI_ERR_UNSUPPORTED), which every GPU that
- * loads the library keeps until the process exits.  The first call on a
- * device looks up that array's device address (cudaGetSymbolAddress) with the
- * device current: make that first call before any stream capture.  All calls
- * share the one array, so calls that may overlap on the GPU (different
- * streams, or different host threads on one device) race: serialise them. */
+ * allocator) or loops that must not block on an allocation use this form:
+ * it calls no cudaMalloc/cudaFree or allocating library routine.  The f16
+ * copy of act lives in one fixed 8 MiB device array inside the library
+ * (tokens * in_dim <= 4,194,304 elements; larger calls return
+ * BONSAI_ERR_UNSUPPORTED), which every GPU that loads the library keeps until
+ * the process exits.  The first call on a device looks up that array's device
+ * address (cudaGetSymbolAddress) with the device current: make that first
+ * call before any stream capture.  All calls share the one array, so calls
+ * that may overlap on the GPU (different streams, or different host threads
+ * on one device) race: serialise them.  The weight must live on the current
+ * device (BONSAI_ERR_ARG otherwise). */
 int bonsai_b1_linear_f32_noalloc(const float* act, int tokens, bonsai_b1_t w, float* out,
                                  void* stream);
 

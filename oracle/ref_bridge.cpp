@@ -8,6 +8,8 @@
 #include "diffuser_types.h"
 #include "b1_0_kernel.h"
 
+#include <condition_variable>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -16,15 +18,97 @@ bool g_bonsai_debug = false;  // defined by the reference's drivers (src/diffuse
 }
 
 namespace {
-void run_threads(ggml_custom_op_t fn, ggml_tensor* dst, int nth, void* ud) {
-  if (nth <= 1) {
-    fn(dst, 0, 1, ud);
-    return;
+// A persistent worker pool, as ggml's CPU backend keeps one for the whole
+// graph: the workers are created once and reused by every call, so a call's
+// cost is the kernel's own work and not the creation of nth threads.  The
+// calling thread runs ith = 0 itself; workers 1 .. nth-1 run the rest.
+class Pool {
+ public:
+  ~Pool() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      quit_ = true;
+      ++gen_;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
   }
-  std::vector<std::thread> ts;
-  ts.reserve(nth);
-  for (int i = 0; i < nth; ++i) ts.emplace_back(fn, dst, i, nth, ud);
-  for (auto& t : ts) t.join();
+  void run(ggml_custom_op_t fn, ggml_tensor* dst, int nth, void* ud) {
+    if (nth <= 1) {
+      fn(dst, 0, 1, ud);
+      return;
+    }
+    std::lock_guard<std::mutex> call(call_mu_);  // one call at a time
+    grow(nth - 1);
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      fn_ = fn;
+      dst_ = dst;
+      ud_ = ud;
+      nth_ = nth;
+      pending_ = nth - 1;
+      ++gen_;
+    }
+    cv_.notify_all();
+    fn(dst, 0, nth, ud);
+    std::unique_lock<std::mutex> lk(mu_);
+    done_cv_.wait(lk, [&] { return pending_ == 0; });
+  }
+
+ private:
+  // Called with call_mu_ held, before the call's generation is published: a
+  // new worker starts from the current generation and so joins that call.
+  void grow(int n) {
+    while ((int)workers_.size() < n) {
+      const int ith = (int)workers_.size() + 1;
+      unsigned long long g0;
+      {
+        std::lock_guard<std::mutex> lk(mu_);
+        g0 = gen_;
+      }
+      workers_.emplace_back([this, ith, g0] { loop(ith, g0); });
+    }
+  }
+  void loop(int ith, unsigned long long seen) {
+    for (;;) {
+      ggml_custom_op_t fn;
+      ggml_tensor* dst;
+      void* ud;
+      int nth;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return gen_ != seen; });
+        seen = gen_;
+        if (quit_) return;
+        fn = fn_;
+        dst = dst_;
+        ud = ud_;
+        nth = nth_;
+      }
+      if (ith >= nth) continue;
+      fn(dst, ith, nth, ud);
+      std::lock_guard<std::mutex> lk(mu_);
+      if (--pending_ == 0) done_cv_.notify_one();
+    }
+  }
+  std::mutex call_mu_, mu_;
+  std::condition_variable cv_, done_cv_;
+  std::vector<std::thread> workers_;
+  ggml_custom_op_t fn_ = nullptr;
+  ggml_tensor* dst_ = nullptr;
+  void* ud_ = nullptr;
+  int nth_ = 0, pending_ = 0;
+  unsigned long long gen_ = 0;
+  bool quit_ = false;
+};
+
+Pool& pool() {
+  static Pool p;
+  return p;
+}
+
+void run_threads(ggml_custom_op_t fn, ggml_tensor* dst, int nth, void* ud) {
+  pool().run(fn, dst, nth, ud);
 }
 }  // namespace
 

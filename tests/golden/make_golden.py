@@ -1,9 +1,10 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Run in a container that has the reference checkout (default /root/reference)
+Run where the reference checkout is readable; its directory is given by
+--ref or the BONSAI_REF_DIR environment variable (one of them is required)
 and the reference's C kernels built into oracle/_ref (make -C oracle):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>
 
 Every output value comes from the reference itself:
   * b1_kat.npz       - the literal 64-weight row of the reference's B1_0
@@ -27,6 +28,7 @@ without needing the reference.
 from __future__ import annotations
 
 import argparse
+import os
 import ast
 import ctypes
 import importlib.util
@@ -62,7 +64,9 @@ def kat_row(ref: Path) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("BONSAI_REF_DIR"),
+                    required="BONSAI_REF_DIR" not in os.environ,
+                    help="the reference checkout (default: $BONSAI_REF_DIR)")
     args = ap.parse_args()
     ref = Path(args.ref)
 

@@ -1,10 +1,11 @@
 """Generate the Flux VAE decoder fixtures from the reference's own PyTorch
 decoder.
 
-Run in a container that has the reference checkout (default /root/reference)
+Run where the reference checkout is readable; its directory is given by
+--ref or the BONSAI_REF_DIR environment variable (one of them is required)
 and torch:
 
-    python tests/golden/make_vae_golden.py [--ref /root/reference]
+    python tests/golden/make_vae_golden.py --ref <reference checkout>
 
 For each latent size (h, w) it builds the reference's FluxDecoder
 (tests/run_vae.py), loads the seeded synthetic checkpoint of
@@ -20,6 +21,7 @@ loader, which is not used here; a stub stands in when the package is absent.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import sys
 import types
@@ -58,7 +60,9 @@ def load_run_vae(ref: Path):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("BONSAI_REF_DIR"),
+                    required="BONSAI_REF_DIR" not in os.environ,
+                    help="the reference checkout (default: $BONSAI_REF_DIR)")
     args = ap.parse_args()
     import torch
 

@@ -132,3 +132,29 @@ def test_b1_gemm_epilogues(gpu, kernel):
     g_, v_ = ref[:, : N // 2], ref[:, N // 2:]
     torch.testing.assert_close(osw.float(), torch.nn.functional.silu(g_) * v_, rtol=4e-3, atol=4e-3)
     torch.cuda.synchronize()
+
+
+def test_b1_linear_f32_two_streams_interleaved(gpu):
+    """The drop-in linear's f16 scratch is per (thread, device, stream): calls
+    of growing size issued alternately on two streams from one host thread,
+    with nothing synchronised between them, give the results of the same
+    calls run one after another on one stream (same kernels, same bits)."""
+    import torch
+    rng = np.random.default_rng(77)
+    K, N = 3072, 1024
+    w = bb.B1Weight(bb.random_b1_packed(N, K, rng), N, K)
+    sizes = [96, 640, 1500, 2900, 4100, 6200]  # every call grows its stream's scratch
+    acts = [torch.from_numpy(rng.standard_normal((T, K)).astype(np.float32)).cuda() for T in sizes]
+    outs = [torch.full((T, N), float("nan"), device="cuda") for T in sizes]
+    refs = [torch.empty(T, N, device="cuda") for T in sizes]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for i, (a, o) in enumerate(zip(acts, outs)):
+        bb.b1_linear_f32(a, w, o, stream=streams[i % 2])
+    torch.cuda.synchronize()
+    for a, r in zip(acts, refs):
+        bb.b1_linear_f32(a, w, r)
+    torch.cuda.synchronize()
+    for o, r in zip(outs, refs):
+        assert torch.equal(o, r)
+    w.free()

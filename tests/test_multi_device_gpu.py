@@ -46,3 +46,31 @@ def test_two_devices_one_process(gpu):
         bb.init(0)
     assert np.array_equal(g0, g1)
     assert np.array_equal(a0, a1)
+
+
+def test_weight_on_another_device_is_rejected(gpu):
+    """A B1_0 weight uploaded on device 0 and used while device 1 is current
+    is an argument error for the drop-in linears, not a launch against memory
+    of another GPU."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    L = bb.lib()
+    rng = np.random.default_rng(5)
+    K, N, T = 256, 128, 16
+    torch.cuda.set_device(0)
+    bb.init(0)
+    w = bb.B1Weight(bb.random_b1_packed(N, K, rng), N, K)
+    try:
+        torch.cuda.set_device(1)
+        bb.init(1)
+        act = torch.zeros(T, K, device="cuda")
+        out = torch.zeros(T, N, device="cuda")
+        for fn in (L.bonsai_b1_linear_f32, L.bonsai_b1_linear_f32_noalloc):
+            rc = fn(act.data_ptr(), T, w.handle, out.data_ptr(), bb.stream_ptr())
+            assert rc == -1 and b"lives on device 0" in L.bonsai_last_error()
+        torch.cuda.synchronize()
+    finally:
+        torch.cuda.set_device(0)
+        bb.init(0)
+        w.free()

@@ -1,6 +1,6 @@
 """bonsai_b1_linear_f32_noalloc: the B1_0 linear for callers that cannot let
-the library allocate (their allocator owns all device memory, or the call is
-being recorded into a CUDA graph, or an allocation's stall is not allowed).
+the library allocate (their allocator owns all device memory, or an
+allocation's stall is not allowed).
 
 It must give the same result as the allocating drop-in bonsai_b1_linear_f32,
 call after call (its fixed scratch array keeps the previous call's contents),
