@@ -45,6 +45,7 @@ SIGNATURES = {
     "bonsai_shutdown": (_c_int, []),
     "bonsai_count_nonfinite": (_c_int, [_vp, _c_ll, ctypes.POINTER(_c_ll), _vp]),
     "bonsai_launch_count": (_c_ll, []),
+    "bonsai_debug_stall_next_gemm": (_c_int, []),
     "bonsai_profile_start": (_c_int, []),
     "bonsai_profile_stop": (_c_int, [ctypes.c_char_p, _c_int]),
     "bonsai_b1_upload": (_c_int, [_vp, _c_int, _c_int, _c_int, ctypes.POINTER(_vp)]),

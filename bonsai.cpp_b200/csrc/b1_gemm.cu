@@ -82,6 +82,10 @@ struct Params {
   int nseg;
   EpiSeg seg[kMaxSegs];
   int* err;
+  // Test hook (bonsai_debug_stall_next_gemm): the load warp issues nothing,
+  // so every other role's first bounded wait expires and the kernel unwinds
+  // through its abort path with no copy or MMA in flight.  0 in normal use.
+  int idle_loads;
 };
 
 __device__ __forceinline__ float tanh_hw(float x) {
@@ -168,7 +172,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int k_blocks = p.k_blocks;
 
   if (warp == WARP_TMA) {
-    if (elect_one()) {
+    if (elect_one() && !p.idle_loads) {
       tma_prefetch_desc(&xmap);
       uint32_t it = 0;
       bool ok = true;
@@ -934,6 +938,9 @@ int launch_b1_unretile(const B1Weight& w, uint8_t* dev_packed, cudaStream_t st) 
   return launch_status("b1_unretile_kernel launch");
 }
 
+// Set by bonsai_debug_stall_next_gemm, consumed by the next launch on the thread.
+thread_local bool g_stall_next_gemm = false;
+
 int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, const EpiSeg* segs,
                    int nseg, bool x_bf16, cudaStream_t st, const TileSel* sel) {
   if (tokens < 0) return fail(-1, "b1_gemm: negative token count");
@@ -970,7 +977,11 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
   constexpr double kPairTileCost = 1.63;
   bool use_pair = false;
   const B1Kernel force = forced_kernel();
-  if (force == B1Kernel::Pair) {
+  const bool stall = g_stall_next_gemm;  // test hook: this launch runs the one-CTA kernel idle
+  g_stall_next_gemm = false;
+  if (stall) {
+    use_pair = false;
+  } else if (force == B1Kernel::Pair) {
     if (slots < 1) return fail(-3, "b1_gemm: the pair kernel cannot be scheduled on this device");
     use_pair = true;
   } else if (force == B1Kernel::Auto && slots >= 1) {
@@ -1046,6 +1057,7 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
   p.nseg = nseg;
   for (int i = 0; i < nseg; ++i) p.seg[i] = segs[i];
   p.err = device_error_word();
+  p.idle_loads = stall ? 1 : 0;
 
   const int grid = (int)std::min<long long>(tiles1, num_sms());
   auto kern = x_bf16 ? gemm::b1_gemm_kernel<true> : gemm::b1_gemm_kernel<false>;
@@ -1064,3 +1076,8 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
 }
 
 }  // namespace bonsai
+
+extern "C" int bonsai_debug_stall_next_gemm(void) {
+  bonsai::g_stall_next_gemm = true;
+  return 0;
+}

@@ -77,6 +77,16 @@ int bonsai_shutdown(void);
  * (src/b1_0_kernel.h:45-69, :195-198) with a value the caller can test. */
 int bonsai_count_nonfinite(const float* x, long long n, long long* count, void* stream);
 
+/* Testing hook for the bounded waits that replace the reference's abort()
+ * (src/b1_0_kernel.h:193-198): the next B1_0 GEMM launched by the calling
+ * thread runs the one-CTA kernel with its load warp idle, so every other role
+ * waits on a barrier that nothing completes.  Each wait gives up after its
+ * 2 s limit, the kernel records a DEV_ERR_TIMEOUT_* code in the device error
+ * word and returns through its abort path (nothing is in flight: no copy was
+ * issued and no MMA started), leaving the context usable.  Read (and clear)
+ * the code with bonsai_device_error().  The launch's output is not written. */
+int bonsai_debug_stall_next_gemm(void);
+
 /* Number of kernel launches this library has issued on the current thread
  * since the last call (launch accounting for benchmarks); resets to 0. */
 long long bonsai_launch_count(void);

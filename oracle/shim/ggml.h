@@ -4,8 +4,11 @@
  * src/diffuser_types.h) unmodified.  It is test infrastructure for the CPU
  * oracle: it provides the tensor struct fields those kernels read
  * (ne, nb, src, data), IEEE fp16 -> fp32 conversion, and a ggml_custom_4d
- * that only records the node (the bridge in ref_bridge.cpp runs the
- * callback itself on a thread pool, as ggml's CPU backend does).
+ * that builds the custom node in a small fixed arena of the context -- its
+ * shape, sources, callback, task count and user-data pointer, which real
+ * ggml keeps among the node's op parameters -- or returns NULL without a
+ * context (the bridge in ref_bridge.cpp runs the callbacks itself on a
+ * thread pool, as ggml's CPU backend does).
  * The real ggml lives in the reference's empty llama.cpp submodule.
  */
 #pragma once
@@ -21,7 +24,7 @@
 
 enum ggml_type { GGML_TYPE_F32 = 0, GGML_TYPE_F16 = 1, GGML_TYPE_I8 = 24 };
 
-struct ggml_context;  // opaque; never dereferenced by the kernels
+typedef void (*ggml_custom_op_t)(struct ggml_tensor* dst, int ith, int nth, void* userdata);
 
 struct ggml_tensor {
   enum ggml_type type;
@@ -29,9 +32,17 @@ struct ggml_tensor {
   size_t nb[GGML_MAX_DIMS];
   struct ggml_tensor* src[GGML_MAX_SRC];
   void* data;
+  /* custom-op parameters of a node made by ggml_custom_4d */
+  ggml_custom_op_t op_fun;
+  int op_n_tasks;
+  void* op_userdata;
 };
 
-typedef void (*ggml_custom_op_t)(struct ggml_tensor* dst, int ith, int nth, void* userdata);
+#define GGML_SHIM_MAX_NODES 64
+struct ggml_context {
+  struct ggml_tensor nodes[GGML_SHIM_MAX_NODES];
+  int n_nodes;
+};
 
 static inline int64_t ggml_nelements(const struct ggml_tensor* t) {
   return t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3];
@@ -65,13 +76,22 @@ static inline float ggml_fp16_to_fp32(uint16_t h) {
   return f;
 }
 
-/* Records nothing: the oracle bridge invokes the callback directly. */
+/* The custom node: f32/f16 output of shape {ne0..ne3} with sources args,
+ * whose data the caller provides; NULL without a context or when the arena
+ * is full or n_args exceeds GGML_MAX_SRC. */
 static inline struct ggml_tensor* ggml_custom_4d(struct ggml_context* ctx, enum ggml_type type,
                                                  int64_t ne0, int64_t ne1, int64_t ne2,
                                                  int64_t ne3, struct ggml_tensor** args,
                                                  int n_args, ggml_custom_op_t fun, int n_tasks,
                                                  void* userdata) {
-  (void)ctx; (void)type; (void)ne0; (void)ne1; (void)ne2; (void)ne3;
-  (void)args; (void)n_args; (void)fun; (void)n_tasks; (void)userdata;
-  return NULL;
+  if (!ctx || ctx->n_nodes >= GGML_SHIM_MAX_NODES || n_args > GGML_MAX_SRC) return NULL;
+  struct ggml_tensor* t = &ctx->nodes[ctx->n_nodes++];
+  memset(t, 0, sizeof(*t));
+  t->type = type;
+  t->ne[0] = ne0; t->ne[1] = ne1; t->ne[2] = ne2; t->ne[3] = ne3;
+  for (int i = 0; i < n_args; ++i) t->src[i] = args[i];
+  t->op_fun = fun;
+  t->op_n_tasks = n_tasks;
+  t->op_userdata = userdata;
+  return t;
 }

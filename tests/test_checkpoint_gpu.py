@@ -249,3 +249,54 @@ def test_load_gguf_container(gpu, tmp_path):
     finally:
         src.close()
         dst.close()
+
+
+@pytest.fixture(scope="module")
+def converter_files(tmp_path_factory):
+    """The files the reference's converters write (byte-identical, checked
+    against their SHA-256 in tests/golden/klein_ckpt.json)."""
+    import json
+    from pathlib import Path
+    import klein_ckpt as kc
+    gold = json.loads((Path(__file__).resolve().parent / "golden" / "klein_ckpt.json").read_text())
+    d = tmp_path_factory.mktemp("converted")
+    sd = kc.make_state_dict(gold["seed"])
+    out = {"safetensors": d / "flux2_4b_1bit.safetensors", "gguf": d / "flux2_4b_1bit.gguf"}
+    kc.write_packed_safetensors(sd, out["safetensors"])
+    kc.write_gguf(sd, out["gguf"])
+    del sd
+    for kind, p in out.items():
+        assert kc.sha256(p) == gold["files"][kind]["sha256"], f"{kind} differs from the converter's"
+    return out
+
+
+def test_load_reference_converter_outputs(gpu, converter_files):
+    """Load the packed safetensors and the GGUF that the reference's
+    converters write (convert_to_b1_0_packed.py, convert_to_b1_0.py) and run
+    one forward of each; compare with the CPU oracle reading the same file's
+    tensors through the safetensors library under the reference loader's
+    names (src/diffuser.cpp:88-186), independently of the engine's loader."""
+    import torch
+    from oracle import pyoracle as O
+    import klein_ckpt as kc
+    rng = np.random.default_rng(12)
+    outs = {}
+    for kind in ("safetensors", "gguf"):
+        m = _klein(seed=999)  # random weights, all replaced by the load
+        try:
+            m.load_safetensors(converter_files[kind])
+            img, txt = _inputs(m, seed=12)
+            out = torch.empty(m.img, m.in_ch, device="cuda")
+            m.forward(img, txt, None, 500.0, out)
+            outs[kind] = out.cpu().numpy()
+            if kind == "safetensors":
+                fw = kc.FileWeights(converter_files[kind], m)
+                ref = O.dit_forward(fw, img.cpu().numpy(), txt.cpu().numpy(), None, 500.0)
+        finally:
+            m.close()
+    assert bb.device_error() == 0
+    np.testing.assert_array_equal(outs["gguf"], outs["safetensors"])
+    g, r = outs["safetensors"].astype(np.float64).ravel(), ref.astype(np.float64).ravel()
+    cos = float(g @ r / (np.linalg.norm(g) * np.linalg.norm(r)))
+    rel = float(np.abs(g - r).max() / np.sqrt(np.mean(r ** 2)))
+    assert cos >= 0.9999 and rel <= 1e-2, (cos, rel)
