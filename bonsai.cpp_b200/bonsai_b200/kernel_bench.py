@@ -1,6 +1,7 @@
 """Time one kernel of the step in isolation (and give ncu a small, fixed case).
 
-    python -m bonsai_b200.kernel_bench gemm M K N [--kernel auto|pair|single] [--reps R]
+    python -m bonsai_b200.kernel_bench gemm M K N [--kernel auto|pair|single]
+                                       [--epi f16|f32|gelu|resid] [--flush] [--reps R]
     python -m bonsai_b200.kernel_bench attention L [--heads H] [--reps R]
     python -m bonsai_b200.kernel_bench conv H W CIN COUT [--k 3] [--bf16] [--reps R]
     python -m bonsai_b200.kernel_bench vae LATENT_H LATENT_W [--reps R]
@@ -48,6 +49,13 @@ def main(argv=None) -> int:
     g.add_argument("K", type=int)
     g.add_argument("N", type=int)
     g.add_argument("--kernel", choices=["auto", "pair", "single"], default="auto")
+    g.add_argument("--epi", choices=["f16", "f32", "gelu", "resid"], default="f16",
+                   help="epilogue: f16 / f32 store, GELU-tanh -> f16, or the gate-residual "
+                        "f32 read-modify-write of the out-projection / MLP-out linears")
+    g.add_argument("--flush", action="store_true",
+                   help="write a 256 MB buffer before every call, so the weights and "
+                        "activations come from DRAM as in the step (which streams 2.2 GB "
+                        "of weights) instead of from the 126 MB L2")
     g.add_argument("--reps", type=int, default=10)
     a = sub.add_parser("attention")
     a.add_argument("L", type=int)
@@ -85,10 +93,29 @@ def main(argv=None) -> int:
             os.environ["BONSAI_B1_KERNEL"] = args.kernel
         w = bb.B1Weight(bb.random_b1_packed(args.N, args.K, np.random.default_rng(1)), args.N, args.K)
         x = torch.randn(args.M, args.K, device="cuda").half()
-        out = torch.empty(args.M, args.N, device="cuda", dtype=torch.float16)
-        ms = _time(lambda: bb.b1_gemm(x, w, bb.BONSAI_EPI_F16, out), args.reps)
+        mode, odt = {"f16": (bb.BONSAI_EPI_F16, torch.float16), "f32": (bb.BONSAI_EPI_F32, torch.float32),
+                     "gelu": (bb.BONSAI_EPI_GELU, torch.float16),
+                     "resid": (bb.BONSAI_EPI_RESID, torch.float32)}[args.epi]
+        out = torch.zeros(args.M, args.N, device="cuda", dtype=odt)
+        gate = torch.full((args.N,), 1e-3, device="cuda") if args.epi == "resid" else None
+        flush = torch.empty(64 << 20, device="cuda") if args.flush else None
+
+        def call():
+            if flush is not None:
+                flush.zero_()
+            bb.b1_gemm(x, w, mode, out, gate=gate)
+        if flush is None:
+            ms = _time(call, args.reps)
+        else:  # the GEMM alone, timed by the library's per-launch events
+            _time(call, 1)
+            bb.profile_start()
+            for _ in range(args.reps):
+                call()
+            e = bb.profile_stop()["b1_gemm"]
+            ms = e["ms"] / e["launches"]
         flop = 2.0 * args.M * args.N * args.K
-        desc = f"gemm M={args.M} K={args.K} N={args.N} kernel={args.kernel}"
+        desc = (f"gemm M={args.M} K={args.K} N={args.N} kernel={args.kernel} epi={args.epi}"
+                + (" flushed" if flush is not None else ""))
     elif args.op == "conv":
         td = torch.bfloat16 if args.bf16 else torch.float16
         x = torch.randn(args.H, args.W, args.cin, device="cuda").to(td)
