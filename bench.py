@@ -419,6 +419,7 @@ def measure_split_2048(args, rank: int, world: int, dist) -> dict:
     # every rank ran the same stages, so the key set (and the order of the
     # reductions below) is the same on all ranks
     phase_ms = {k: round(max_over_ranks(pt[k]), 3) for k in sorted(pt)}
+    phase_ms_min = {k: round(-max_over_ranks(-pt[k]), 3) for k in sorted(pt)}
     assert bb.device_error() == 0
 
     res = {"n_gpus": world, "ms_per_step": round(ms, 3), "e2e_ms": round(ms_e2e, 3),
@@ -426,9 +427,10 @@ def measure_split_2048(args, rank: int, world: int, dist) -> dict:
            "exchange": (args.exchange if world > 1 else "none (one GPU: the plain step)"),
            "images_per_s": round(1000.0 / ms, 3),
            "step_tflops": round(step_flops(img_n + TXT, img_n) / (ms / 1e3) / 1e12, 1),
-           "phase_ms": phase_ms,
+           "phase_ms": phase_ms, "phase_ms_min_rank": phase_ms_min,
            "phase_ms_note": "one extra step, a CUDA-event pair around every phase and exchange "
-                            "call, summed per stage, max over ranks"}
+                            "call, summed per stage; phase_ms = max over ranks, "
+                            "phase_ms_min_rank = min over ranks (the spread is load imbalance)"}
     step(ts[0])
     torch.cuda.synchronize()
     split_out = out_d.clone()

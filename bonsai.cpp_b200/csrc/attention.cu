@@ -88,6 +88,14 @@ struct Params {
   long long ld_out;
   RowRoutes routes;  // routes.n == 0: every row through out
   int* err;
+  // Key split: the keys of a head are cut into kv_split ranges of
+  // kv_chunk blocks of 64 (the last one shorter), each taken by its own
+  // CTA (pair); kv_split > 1 writes each range's normalised partial output
+  // and the log2 of its exponential sum instead of `out`, and
+  // combine_kernel merges them.
+  int kv_split, kv_chunk;
+  float* part_o;    // [kv_split][seq][n_heads * 128]
+  float* part_lse;  // [kv_split][n_heads][seq]
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -174,7 +182,11 @@ __device__ __forceinline__ uint32_t cvt_h2(float lo, float hi) {
 // CTA issues the MMAs; both CTAs' TMA loads complete on its barriers, its
 // commits arrive on both CTAs' barriers, and both CTAs' softmax warps arrive
 // on its p_ready.  CTA r of pair c holds query tiles c*512 + g*256 + r*128.
-template <bool kPair>
+//
+// kSplit: the CTA (pair) takes one range of the head's keys and writes
+// partials (Params::kv_split > 1); the unsplit instantiation keeps the key
+// offset a compile-time zero.
+template <bool kPair, bool kSplit>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap qmap,
                      const __grid_constant__ CUtensorMap kmap,
@@ -206,11 +218,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t lane = lane_id();
   const int head = blockIdx.y;
   const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  // Unit = (query block, key range): query block qb, key range ksplit.
+  const int unit = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ksplit = kSplit ? unit % p.kv_split : 0;
+  const int qb = kSplit ? unit / p.kv_split : unit;
   // first query of tile g: q0 + g * tstride
-  const int q0 = kPair ? (int)(blockIdx.x >> 1) * 4 * BQ + (int)rank * BQ : (int)blockIdx.x * 2 * BQ;
+  const int q0 = kPair ? qb * 4 * BQ + (int)rank * BQ : qb * 2 * BQ;
   constexpr int tstride = kPair ? 2 * BQ : BQ;
   const bool leader = !kPair || rank == 0;
-  const int nkv = (p.seq + BKV - 1) / BKV;
+  // key blocks [j0, j0 + nkv) of 64 keys (the host guarantees nkv >= 1)
+  const int j0 = kSplit ? ksplit * p.kv_chunk : 0;
+  const int nkv = kSplit ? min((p.seq + BKV - 1) / BKV - j0, p.kv_chunk) : (p.seq + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
     bar_init(q_full, 1);
@@ -278,9 +296,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int h = 0; h < 2; ++h) {
           if constexpr (kPair)  // this CTA's 32 keys of the block
             tma_load_3d_pair(ks + sk * K_SLOT + h * K_SLOT_HALF, &kmap, lead_bar(&k_full[sk]), h * 64,
-                             j * BKV + (int)rank * (BKV / 2), head);
+                             (j0 + j) * BKV + (int)rank * (BKV / 2), head);
           else
-            tma_load_3d(ks + sk * K_SLOT + h * K_SLOT_HALF, &kmap, &k_full[sk], h * 64, j * BKV, head);
+            tma_load_3d(ks + sk * K_SLOT + h * K_SLOT_HALF, &kmap, &k_full[sk], h * 64,
+                        (j0 + j) * BKV, head);
         }
         const int sv = j % VS;
         if (!wait_bar(&v_empty[sv], ((j / VS) & 1) ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
@@ -289,11 +308,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (leader) bar_arrive_expect_tx(&v_full[sv], ncta * V_SLOT);
         if constexpr (kPair) {  // this CTA's 64 dims of the block
-          tma_load_3d_pair(vs + sv * V_SLOT, &vmap, lead_bar(&v_full[sv]), (int)rank * 64, j * BKV,
-                           head);
+          tma_load_3d_pair(vs + sv * V_SLOT, &vmap, lead_bar(&v_full[sv]), (int)rank * 64,
+                           (j0 + j) * BKV, head);
         } else {
-          tma_load_3d(vs + sv * V_SLOT, &vmap, &v_full[sv], 0, j * BKV, head);
-          tma_load_3d(vs + sv * V_SLOT + V_SLOT / 2, &vmap, &v_full[sv], 64, j * BKV, head);
+          tma_load_3d(vs + sv * V_SLOT, &vmap, &v_full[sv], 0, (j0 + j) * BKV, head);
+          tma_load_3d(vs + sv * V_SLOT + V_SLOT / 2, &vmap, &v_full[sv], 64, (j0 + j) * BKV, head);
         }
       }
       if (!ok) {
@@ -453,7 +472,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           s[32 + i] = __uint_as_float(r1[i]);
         }
       }
-      const int kbase = j * BKV;
+      const int kbase = (j0 + j) * BKV;
       if (kbase + BKV > p.seq) {
 #pragma unroll
         for (int c = 0; c < BKV; ++c)
@@ -582,6 +601,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const float inv_l = 1.0f / l;
         const int q = q0 + g * tstride + row;
+        if (kSplit) {
+          // this key range's O / l (f32) and log2 of its exponential sum
+          float* po = p.part_o + ((size_t)ksplit * p.seq + q) * ((size_t)p.n_heads * HD) +
+                      (size_t)head * HD;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(o_addr + c * 32, r);
+            tmem_wait_ld();
+            if (q < p.seq) {
+              float4* d4 = reinterpret_cast<float4*>(po + c * 32);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                d4[i] = make_float4(__uint_as_float(r[4 * i]) * inv_l, __uint_as_float(r[4 * i + 1]) * inv_l,
+                                    __uint_as_float(r[4 * i + 2]) * inv_l,
+                                    __uint_as_float(r[4 * i + 3]) * inv_l);
+            }
+          }
+          if (q < p.seq)
+            p.part_lse[((size_t)ksplit * p.n_heads + head) * p.seq + q] = m + __log2f(l);
+        } else {
         __half* base = p.out;
         if (p.routes.n > 0) {
           int r = 0;
@@ -609,6 +649,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
         if (p.routes.n > 0) __threadfence_system();  // peer stores ordered before the kernel's end
+        }
       }
     }
     tc_fence_before();
@@ -618,6 +659,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     else if (lane == 0)
       bar_arrive(sm_done);
   }
+}
+
+// Merges the kv_split partial outputs of each (query row, head): with
+// lse_s = log2 of range s's exponential sum, out = sum_s 2^(lse_s - lse) O_s
+// where lse = log2 sum_s 2^lse_s (the ranges' softmax weights).  One thread
+// per 8 dims of one (row, head); f16 stores to out, or to the row's owner
+// under routes (as the attention epilogue does).
+__global__ void combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                               int kv_split, int seq, int n_heads, __half* out, long long ld_out,
+                               RowRoutes routes) {
+  const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  const long long total = (long long)seq * n_heads * (HD / 8);
+  if (idx >= total) return;
+  const int d8 = (int)(idx % (HD / 8));
+  const int h = (int)((idx / (HD / 8)) % n_heads);
+  const int q = (int)(idx / ((long long)(HD / 8) * n_heads));
+  float mx = -INFINITY;
+  for (int sp = 0; sp < kv_split; ++sp)
+    mx = fmaxf(mx, part_lse[((size_t)sp * n_heads + h) * seq + q]);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float wsum = 0.f;
+  const size_t row_stride = (size_t)n_heads * HD;
+  for (int sp = 0; sp < kv_split; ++sp) {
+    const float w = exp2f(part_lse[((size_t)sp * n_heads + h) * seq + q] - mx);
+    wsum += w;
+    const float4* src = reinterpret_cast<const float4*>(part_o + ((size_t)sp * seq + q) * row_stride +
+                                                        (size_t)h * HD + d8 * 8);
+    const float4 a = src[0], b = src[1];
+    acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
+    acc[4] += w * b.x; acc[5] += w * b.y; acc[6] += w * b.z; acc[7] += w * b.w;
+  }
+  const float inv = 1.0f / wsum;
+  __half* base = out;
+  if (routes.n > 0) {
+    int r = 0;
+    while (r + 1 < routes.n && q >= routes.row_bound[r + 1]) ++r;
+    base = routes.outs[r];
+  }
+  uint32_t hv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 h2 = __floats2half2_rn(acc[2 * i] * inv, acc[2 * i + 1] * inv);
+    hv[i] = *reinterpret_cast<const uint32_t*>(&h2);
+  }
+  *reinterpret_cast<uint4*>(base + (size_t)q * ld_out + (size_t)h * HD + d8 * 8) =
+      make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  if (routes.n > 0) __threadfence_system();  // peer stores ordered before the kernel's end
 }
 
 }  // namespace attn
@@ -639,28 +727,59 @@ cudaLaunchConfig_t attn_pair_config(cudaLaunchAttribute* attr) {
   return cfg;
 }
 
-// Whether at least one cluster of two attention CTAs can be resident (the
-// pair form is used only then).
-bool attn_pair_fits() {
-  static int fits_dev[64] = {};  // 0 unknown, 1 fits, 2 does not
+// How many clusters of two attention CTAs can be resident at once (0: the
+// pair form cannot run and the one-CTA form is used).
+int attn_pair_slots() {
+  static int slots_dev[64];
+  static bool known[64] = {};
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
-  int& fits = fits_dev[device_slot()];
-  if (fits == 0) {
-    fits = 2;
-    if (cudaFuncSetAttribute(attn::attention_kernel<true>,
+  const int d = device_slot();
+  if (!known[d]) {
+    known[d] = true;
+    slots_dev[d] = 0;
+    if (cudaFuncSetAttribute(attn::attention_kernel<true, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              attn::SMEM_BYTES) == cudaSuccess) {
       cudaLaunchAttribute attr[1];
       cudaLaunchConfig_t cfg = attn_pair_config(attr);
       cfg.gridDim = dim3(2);
       int c = 0;
-      if (cudaOccupancyMaxActiveClusters(&c, attn::attention_kernel<true>, &cfg) == cudaSuccess)
-        fits = c > 0 ? 1 : 2;
+      if (cudaOccupancyMaxActiveClusters(&c, attn::attention_kernel<true, false>, &cfg) == cudaSuccess)
+        slots_dev[d] = c > 0 ? c : 0;
     }
     cudaGetLastError();
   }
-  return fits == 1;
+  return slots_dev[d];
+}
+
+// Key split for a launch of `units` equal work units (clusters or CTAs) on
+// `slots` resident ones, nkv key blocks per head: the units run in
+// ceil(units / slots) waves, so when they fill the last wave poorly (the
+// multi-GPU head split leaves 3 heads of 33 query blocks per GPU: 99
+// clusters on 74 slots, two waves for 1.34 waves of work) cutting every
+// unit's keys into s ranges gives ceil(s * units / slots) / s waves of whole
+// units.  A split is used only where it saves at least 10% of the wave time
+// and every range keeps >= 16 blocks (the partials and their merge cost a
+// few percent of a range).  BONSAI_ATTN_SPLIT=n forces n ranges (tests).
+// Returns the number of key ranges; *chunk = blocks per range.
+int choose_kv_split(long long units, int slots, int nkv, int* chunk) {
+  int want = 1;
+  if (const char* e = getenv("BONSAI_ATTN_SPLIT")) {
+    want = std::max(1, atoi(e));
+  } else if (slots > 0) {
+    auto waves = [&](int sp) { return (double)((units * sp + slots - 1) / slots) / sp; };
+    const double w1 = waves(1);
+    double best = w1;
+    for (int sp = 2; sp <= 4; ++sp)
+      if (nkv / sp >= 16 && waves(sp) <= 0.9 * w1 && waves(sp) < best - 1e-9) {
+        best = waves(sp);
+        want = sp;
+      }
+  }
+  want = std::min(want, nkv);
+  *chunk = (nkv + want - 1) / want;
+  return (nkv + *chunk - 1) / *chunk;  // no empty range
 }
 }  // namespace
 
@@ -685,7 +804,8 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
   // BONSAI_ATTN=single selects the one-CTA form (the tests run both); the
   // CTA-pair form is the default where a cluster of two fits (checked once).
   const char* form = getenv("BONSAI_ATTN");
-  const bool pair = !(form && std::strcmp(form, "single") == 0) && attn_pair_fits();
+  const int pair_slots = attn_pair_slots();
+  const bool pair = !(form && std::strcmp(form, "single") == 0) && pair_slots > 0;
   CUtensorMap qm, km, vm;
   int rc = encode_tmap_heads(&qm, q, n_heads, seq, head_dim, attn::BQ);
   if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim, pair ? attn::BKV / 2 : attn::BKV);
@@ -705,7 +825,8 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
     // setmaxnreg.inc waits until the block's launch allocation can supply
     // the registers: refuse to launch unless the kernel was built with the
     // per-thread count the split above assumes.
-    for (auto kern : {attn::attention_kernel<false>, attn::attention_kernel<true>}) {
+    for (auto kern : {attn::attention_kernel<false, false>, attn::attention_kernel<true, false>,
+                      attn::attention_kernel<false, true>, attn::attention_kernel<true, true>}) {
       cudaFuncAttributes fa{};
       cudaError_t e = cudaFuncGetAttributes(&fa, kern);
       if (e != cudaSuccess) return cuda_status(e, "attention function attributes");
@@ -718,20 +839,58 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
     }
     attr = true;
   }
-  ProfScope prof("attention", 4.0 * (double)seq * seq * head_dim * n_heads,
-                 4.0 * (double)seq * n_heads * head_dim * 2, st);
-  if (!pair) {
-    dim3 grid((seq + 2 * attn::BQ - 1) / (2 * attn::BQ), n_heads);
-    attn::attention_kernel<false><<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, st>>>(qm, km, vm, p);
-    return launch_status("attention_kernel launch");
+  // work units of the unsplit launch and the key split
+  const int nkv = (seq + attn::BKV - 1) / attn::BKV;
+  const long long qblocks = pair ? (seq + 4 * attn::BQ - 1) / (4 * attn::BQ)
+                                 : (seq + 2 * attn::BQ - 1) / (2 * attn::BQ);
+  int chunk = nkv;
+  p.kv_split = choose_kv_split(qblocks * n_heads, pair ? pair_slots : num_sms(), nkv, &chunk);
+  p.kv_chunk = chunk;
+  void* part = nullptr;
+  if (p.kv_split > 1) {
+    // partial outputs + their log2 sums, stream-ordered, freed after the merge
+    const size_t o_bytes = (size_t)p.kv_split * seq * n_heads * attn::HD * sizeof(float);
+    const size_t l_bytes = (size_t)p.kv_split * n_heads * seq * sizeof(float);
+    cudaError_t e = cudaMallocAsync(&part, o_bytes + l_bytes, st);
+    if (e != cudaSuccess) return fail(-6, "attention: partial-output allocation failed");
+    p.part_o = static_cast<float*>(part);
+    p.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(part) + o_bytes);
   }
-  cudaLaunchAttribute attr_c[1];
-  cudaLaunchConfig_t cfg = attn_pair_config(attr_c);
-  cfg.gridDim = dim3(2 * (unsigned)((seq + 4 * attn::BQ - 1) / (4 * attn::BQ)), (unsigned)n_heads);
-  cfg.stream = st;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn::attention_kernel<true>, qm, km, vm, p);
-  if (e != cudaSuccess) return cuda_status(e, "attention pair launch");
-  return launch_status("attention pair launch");
+  int rc2 = 0;
+  {
+    ProfScope prof("attention", 4.0 * (double)seq * seq * head_dim * n_heads,
+                   4.0 * (double)seq * n_heads * head_dim * 2, st);
+    if (!pair) {
+      dim3 grid((unsigned)(qblocks * p.kv_split), n_heads);
+      if (p.kv_split > 1)
+        attn::attention_kernel<false, true><<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, st>>>(qm, km, vm, p);
+      else
+        attn::attention_kernel<false, false><<<grid, attn::NUM_THREADS, attn::SMEM_BYTES, st>>>(qm, km, vm, p);
+      rc2 = launch_status("attention_kernel launch");
+    } else {
+      cudaLaunchAttribute attr_c[1];
+      cudaLaunchConfig_t cfg = attn_pair_config(attr_c);
+      cfg.gridDim = dim3(2 * (unsigned)(qblocks * p.kv_split), (unsigned)n_heads);
+      cfg.stream = st;
+      const cudaError_t e =
+          p.kv_split > 1 ? cudaLaunchKernelEx(&cfg, attn::attention_kernel<true, true>, qm, km, vm, p)
+                         : cudaLaunchKernelEx(&cfg, attn::attention_kernel<true, false>, qm, km, vm, p);
+      rc2 = e != cudaSuccess ? cuda_status(e, "attention pair launch")
+                             : launch_status("attention pair launch");
+    }
+  }
+  if (p.kv_split > 1) {
+    if (rc2 == 0) {
+      ProfScope prof("attention_combine", 0.0,
+                     (double)seq * n_heads * attn::HD * (4.0 * p.kv_split + 2.0), st);
+      const long long threads = (long long)seq * n_heads * (attn::HD / 8);
+      attn::combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+          p.part_o, p.part_lse, p.kv_split, seq, n_heads, out, ld_out, p.routes);
+      rc2 = launch_status("attention combine launch");
+    }
+    cudaFreeAsync(part, st);
+  }
+  return rc2;
 }
 
 }  // namespace bonsai

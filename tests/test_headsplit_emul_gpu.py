@@ -111,3 +111,30 @@ def test_headsplit_emulated_matches_forward(gpu, monkeypatch, world, kernel, fus
         rel = float((g - r).abs().max() / r.pow(2).mean().sqrt())
         assert cos >= 0.99999 and rel <= 1e-3, (world, kernel, fused, rank, cos, rel)
     assert bb.device_error() == 0
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_headsplit_emulated_with_key_split(gpu, monkeypatch, fused):
+    """World 8 (3 heads per rank, the layout whose attention the launcher
+    splits by key range at 2048^2) with the key split forced on at this small
+    size: the merged partial outputs reach every rank's cat, directly or
+    routed to the row owners (fused)."""
+    import torch
+    preset = bb.PRESET_FLUX1
+    ref_m = bb.Dit(preset, IMG_H * IMG_W, TXT, IMG_H, IMG_W, depth=1, depth_single=1, seed=5)
+    try:
+        img, txt, pooled = _inputs(ref_m)
+        ref = torch.empty(ref_m.img, ref_m.in_ch, device="cuda")
+        ref_m.forward(img, txt, pooled, 600.0, ref)
+        torch.cuda.synchronize()
+    finally:
+        ref_m.close()
+    monkeypatch.setenv("BONSAI_ATTN_SPLIT", "3")  # 5 key blocks -> ranges of 2, 2 and 1
+    outs = _emulated_forward(preset, 8, img, txt, pooled, 600.0, fused=fused)
+    r = ref.double().flatten()
+    for rank, o in enumerate(outs):
+        g = o.double().flatten()
+        cos = float(g @ r / (g.norm() * r.norm()))
+        rel = float((g - r).abs().max() / r.pow(2).mean().sqrt())
+        assert cos >= 0.99999 and rel <= 1e-3, (fused, rank, cos, rel)
+    assert bb.device_error() == 0

@@ -132,3 +132,34 @@ def test_attention_long_sequence_with_redo(gpu, attn_form, L):
         del s
         got = out[:, h * hd:(h + 1) * hd].float()
         _check(got.cpu().numpy(), ref.cpu().numpy(), f"attention L={L} head {h} ({attn_form})")
+
+
+@pytest.mark.parametrize("L,nh,split", [(1000, 2, 2), (1000, 2, 3), (4608, 3, 2), (16896, 3, 2),
+                                        (333, 1, 4)])
+def test_attention_key_split(gpu, attn_form, monkeypatch, L, nh, split):
+    """The key-range split (BONSAI_ATTN_SPLIT forces it; the launcher picks
+    it for the 2048^2 head split on 8 GPUs): each range's normalised partial
+    and log2 exponential sum, merged, against torch fp32 -- ragged last
+    ranges and ragged last key blocks included."""
+    import torch
+    monkeypatch.setenv("BONSAI_ATTN_SPLIT", str(split))
+    hd = 128
+    g = torch.Generator(device="cuda").manual_seed(L + split)
+    q, k, v = (torch.randn(nh, L, hd, device="cuda", generator=g) for _ in range(3))
+    q[0, : L // 2, 0] += 6.0          # a planted block (redo path) inside one range
+    b1 = (L // 3 // 64) * 64
+    k[0, b1:b1 + 64, 0] = 30.0
+    q, k, v = q.half(), k.half(), v.half()
+    out = torch.full((L, nh * hd), float("nan"), device="cuda", dtype=torch.float16)
+    scale = hd ** -0.5
+    bb.check(bb.lib().bonsai_joint_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), nh, L, hd,
+                                             scale, out.data_ptr(), out.stride(0), bb.stream_ptr()),
+             "attention")
+    torch.cuda.synchronize()
+    assert bb.device_error() == 0
+    for h in range(nh):
+        s = (q[h].float() @ k[h].float().t()) * scale
+        ref = torch.softmax(s, -1) @ v[h].float()
+        del s
+        got = out[:, h * hd:(h + 1) * hd].float()
+        _check(got.cpu().numpy(), ref.cpu().numpy(), f"attention split={split} L={L} head {h} ({attn_form})")
