@@ -754,28 +754,24 @@ int attn_pair_slots() {
 }
 
 // Key split for a launch of `units` equal work units (clusters or CTAs) on
-// `slots` resident ones, nkv key blocks per head: the units run in
-// ceil(units / slots) waves, so when they fill the last wave poorly (the
-// multi-GPU head split leaves 3 heads of 33 query blocks per GPU: 99
-// clusters on 74 slots, two waves for 1.34 waves of work) cutting every
-// unit's keys into s ranges gives ceil(s * units / slots) / s waves of whole
-// units.  A split is used only where it saves at least 10% of the wave time
-// and every range keeps >= 16 blocks (the partials and their merge cost a
-// few percent of a range).  BONSAI_ATTN_SPLIT=n forces n ranges (tests).
-// Returns the number of key ranges; *chunk = blocks per range.
+// `slots` resident ones, nkv key blocks per head.  A launch that fills at
+// most half of the GPU in a single wave (one or two heads at a long
+// sequence) leaves SMs idle for its whole duration: cutting every unit's keys
+// into s ranges (units * s <= slots) runs it in about 1/s of the time.  Where
+// the units already take more than one wave the split does not pay: on 3
+// heads x 16896 tokens (99 clusters on 74 slots) two ranges measured 450 us
+// against 438 us unsplit -- the part-filled last wave runs at a higher clock
+// than the full ones, and every range adds its pipeline start, f32 partial
+// stores and the merge.  Every range keeps >= 16 key blocks.
+// BONSAI_ATTN_SPLIT=n forces n ranges (tests).  Returns the number of key
+// ranges; *chunk = blocks per range.
 int choose_kv_split(long long units, int slots, int nkv, int* chunk) {
   int want = 1;
   if (const char* e = getenv("BONSAI_ATTN_SPLIT")) {
     want = std::max(1, atoi(e));
   } else if (slots > 0) {
-    auto waves = [&](int sp) { return (double)((units * sp + slots - 1) / slots) / sp; };
-    const double w1 = waves(1);
-    double best = w1;
     for (int sp = 2; sp <= 4; ++sp)
-      if (nkv / sp >= 16 && waves(sp) <= 0.9 * w1 && waves(sp) < best - 1e-9) {
-        best = waves(sp);
-        want = sp;
-      }
+      if (units * sp <= slots && nkv / sp >= 16) want = sp;
   }
   want = std::min(want, nkv);
   *chunk = (nkv + want - 1) / want;

@@ -118,7 +118,10 @@ def test_headsplit_emulated_with_key_split(gpu, monkeypatch, fused):
     """World 8 (3 heads per rank, the layout whose attention the launcher
     splits by key range at 2048^2) with the key split forced on at this small
     size: the merged partial outputs reach every rank's cat, directly or
-    routed to the row owners (fused)."""
+    routed to the row owners (fused).  The split changes the attention's
+    rounding (each range's P is rounded against its own maximum), so the bar
+    is the attention's parity bar, not the bit-level agreement of the
+    unsplit partition."""
     import torch
     preset = bb.PRESET_FLUX1
     ref_m = bb.Dit(preset, IMG_H * IMG_W, TXT, IMG_H, IMG_W, depth=1, depth_single=1, seed=5)
@@ -136,5 +139,5 @@ def test_headsplit_emulated_with_key_split(gpu, monkeypatch, fused):
         g = o.double().flatten()
         cos = float(g @ r / (g.norm() * r.norm()))
         rel = float((g - r).abs().max() / r.pow(2).mean().sqrt())
-        assert cos >= 0.99999 and rel <= 1e-3, (fused, rank, cos, rel)
+        assert cos >= 0.9999 and rel <= 1e-2, (fused, rank, cos, rel)
     assert bb.device_error() == 0
