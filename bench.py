@@ -47,11 +47,12 @@ WORKLOAD_2048 = ("flux1-schnell DiT denoise step @2048^2: 19 double + 38 single 
                  "L = 512 text + 16384 image tokens, one image split across the GPUs")
 
 
-# DRAM traffic of the B1_0 GEMM (dram__bytes_read.sum + dram__bytes_write.sum),
-# summed over the 229 b1_gemm launches of one flux1 1024^2 step and divided by
-# 229: one ncu capture of this bench on one B200 (one pass per launch), kept in
-# profiles/b1_gemm_dram_flux1_1024.md.  It applies to the default workload only.
-GEMM_DRAM_BYTES_PER_LAUNCH = 116.53e6
+# DRAM traffic of the B1_0 GEMM (dram__bytes_read.sum + dram__bytes_write.sum)
+# per launch of the flux1 1024^2 step: one ncu capture of one launch of each
+# of the step's ten GEMM shapes (kernel_bench, L2 flushed before the launch),
+# weighted by the shapes' launch counts (profiles/b1_gemm_dram_flux1_1024.md).
+# It applies to the default workload only.
+GEMM_DRAM_BYTES_PER_LAUNCH = 115.82e6
 
 
 def peaks():
@@ -598,7 +599,8 @@ def run_bonsai(args):
                      "peak_kind": f"{pk['source']} sustained bf16 (dense GEMM under the power cap)",
                      "frac_of_burst": round(gemm_tf / pk["bf16"], 4),
                      "traffic": None if split else GEMM_DRAM_BYTES_PER_LAUNCH,
-                     "traffic_unit": "bytes per launch (mean over the step's launches, ncu)",
+                     "traffic_unit": "bytes per launch (ncu, one launch per GEMM shape of the step, "
+                                     "weighted by launch count)",
                      "algorithmic_bytes": round(g["bytes"] / g["launches"]) if g else None,
                      "measured": "sum of 2*M*N*K over every b1_gemm launch / sum of their "
                                  "CUDA-event durations, over a second pass of the K steps"},
