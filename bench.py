@@ -241,10 +241,15 @@ class CpuSample:
 def step_config(world: int, split: bool = False, exchange: str = "fused") -> dict:
     """The bench line's `config`, identical in both arms for the same N."""
     if split:
-        par = (f"head/row split over {world} GPUs, exchanges fused into the producing kernels "
-               "over peer memory (CUDA IPC), one-element all-reduce per phase for ordering"
-               if exchange == "fused" else
-               f"head/row split over {world} GPUs (NCCL all-gather + all-to-all per block)")
+        par = {"fused": f"head/row split over {world} GPUs, exchanges fused into the producing "
+                        "kernels over peer memory (CUDA IPC), one-element all-reduce per phase "
+                        "for ordering",
+               "scatter": f"head/row split over {world} GPUs, Q/K/V of own rows stored into the "
+                          "heads' owners by the GEMM epilogue and attention rows into the rows' "
+                          "owners, over peer memory (CUDA IPC), one-element all-reduce per phase "
+                          "for ordering",
+               "nccl": f"head/row split over {world} GPUs (NCCL all-gather + all-to-all per "
+                       "block)"}[exchange]
     else:
         par = f"dp{world} (one image per GPU, no collective)"
     return {"workload": WORKLOAD_2048 if split else WORKLOAD,
@@ -356,8 +361,8 @@ def measure_split_2048(args, rank: int, world: int, dist) -> dict:
     m = bb.Dit(bb.PRESET_FLUX1, img_n, TXT, grid, grid, seed=1234)
     if world > 1:
         m.set_partition(rank, world)
-        if args.exchange == "fused":
-            headsplit.enable_fused(m)
+        if args.exchange in ("fused", "scatter"):
+            headsplit.enable_fused(m, scatter_qkv=args.exchange == "scatter")
     rng = np.random.default_rng(2048)  # one shared image on every rank
     img_h = torch.from_numpy(rng.standard_normal((img_n, IN_CH)).astype(np.float32)).pin_memory()
     txt_h = torch.from_numpy(rng.standard_normal((TXT, CTX)).astype(np.float32)).pin_memory()
@@ -481,8 +486,8 @@ def run_bonsai(args):
         from bonsai_b200 import headsplit
         if world > 1:
             model.set_partition(rank, world)
-            if args.exchange == "fused":
-                headsplit.enable_fused(model)
+            if args.exchange in ("fused", "scatter"):
+                headsplit.enable_fused(model, scatter_qkv=args.exchange == "scatter")
 
     rng = np.random.default_rng(1000 + (0 if split else rank))  # split: one shared image
     img_h = torch.from_numpy(rng.standard_normal((IMG, IN_CH)).astype(np.float32)).pin_memory()
@@ -900,9 +905,11 @@ def main():
     ap.add_argument("--workload", choices=["1024", "2048"], default="1024",
                     help="1024: config 4, one image per GPU (data parallel, default); "
                          "2048: config 5(b), one 2048^2 image split by heads/rows across the GPUs")
-    ap.add_argument("--exchange", choices=["fused", "nccl"], default="fused",
-                    help="--workload 2048 on N > 1 GPUs: exchanges fused into the kernels over "
-                         "peer memory (default) or NCCL collectives between the phases")
+    ap.add_argument("--exchange", choices=["fused", "scatter", "nccl"], default="fused",
+                    help="the 2048^2 split on N > 1 GPUs: exchanges fused into the kernels over "
+                         "peer memory (fused: the LN-modulate kernel broadcasts xm rows; scatter: "
+                         "the Q/K/V GEMM stores every head into its owner's buffer) or NCCL "
+                         "collectives between the phases")
     ap.add_argument("--no-split", action="store_true",
                     help="skip the 2048^2 head/row-split measurement (split_2048) that every "
                          "default run adds beside the headline")

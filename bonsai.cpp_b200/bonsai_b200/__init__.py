@@ -83,6 +83,9 @@ SIGNATURES = {
     "bonsai_dit_set_peers": (_c_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), _c_int]),
     "bonsai_dit_ipc_handles": (_c_int, [_vp, _vp]),
     "bonsai_dit_open_peers": (_c_int, [_vp, _vp, _c_int]),
+    "bonsai_dit_set_qkv_peers": (_c_int, [_vp, ctypes.POINTER(_vp), _c_int]),
+    "bonsai_dit_ipc_handle": (_c_int, [_vp, ctypes.c_char_p, _vp]),
+    "bonsai_dit_open_qkv_peers": (_c_int, [_vp, _vp, _c_int]),
     "bonsai_vae_create": (_c_int, [_c_int, _c_int, ctypes.c_ulonglong, ctypes.POINTER(_vp)]),
     "bonsai_vae_destroy": (_c_int, [_vp]),
     "bonsai_vae_load_safetensors": (_c_int, [_vp, ctypes.c_char_p]),
@@ -398,6 +401,26 @@ class Dit:
         xa = (_vp * n)(*xm_ptrs)
         ca = (_vp * n)(*cat_ptrs)
         check(lib().bonsai_dit_set_peers(self.handle, xa, ca, n), "bonsai_dit_set_peers")
+
+    def set_qkv_peers(self, qkv_ptrs):
+        """QKV scatter: every rank's qkv device pointer as seen from this GPU
+        ([rank] = this model's own); None switches back to the xm broadcast."""
+        if qkv_ptrs is None:
+            check(lib().bonsai_dit_set_qkv_peers(self.handle, None, 0), "bonsai_dit_set_qkv_peers")
+            return
+        n = len(qkv_ptrs)
+        check(lib().bonsai_dit_set_qkv_peers(self.handle, (_vp * n)(*qkv_ptrs), n),
+              "bonsai_dit_set_qkv_peers")
+
+    def ipc_handle(self, name: str) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        check(lib().bonsai_dit_ipc_handle(self.handle, name.encode(), buf), "bonsai_dit_ipc_handle")
+        return buf.raw
+
+    def open_qkv_peers(self, handles: bytes, world: int):
+        assert len(handles) == 64 * world
+        check(lib().bonsai_dit_open_qkv_peers(self.handle, handles, world),
+              "bonsai_dit_open_qkv_peers")
 
     def ipc_handles(self) -> bytes:
         buf = ctypes.create_string_buffer(128)

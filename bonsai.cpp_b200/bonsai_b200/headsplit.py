@@ -51,15 +51,23 @@ def heads_to_rows(cat: torch.Tensor, width: int, rank: int, world: int, group=No
     mine.copy_(recv.permute(1, 0, 2))
 
 
-def enable_fused(model, group=None) -> None:
-    """Exchange CUDA IPC handles of every rank's xm / cat and give them to
-    the engine (bonsai_dit_open_peers).  Collective: every rank calls it."""
-    rank = dist.get_rank(group)
-    world = dist.get_world_size(group)
-    mine = torch.frombuffer(bytearray(model.ipc_handles()), dtype=torch.uint8).cuda()
+def _all_gather_bytes(data: bytes, world: int, group) -> bytes:
+    mine = torch.frombuffer(bytearray(data), dtype=torch.uint8).cuda()
     every = torch.empty(world * mine.numel(), dtype=torch.uint8, device="cuda")
     dist.all_gather_into_tensor(every, mine, group=group)
-    model.open_peers(bytes(every.cpu().numpy()), world)
+    return bytes(every.cpu().numpy())
+
+
+def enable_fused(model, group=None, scatter_qkv: bool = False) -> None:
+    """Exchange CUDA IPC handles of every rank's xm / cat and give them to
+    the engine (bonsai_dit_open_peers).  scatter_qkv: also every rank's qkv
+    (bonsai_dit_open_qkv_peers), so that phase 0's Q/K/V GEMM stores each
+    head into its owner's buffer instead of phase 0 broadcasting xm rows.
+    Collective: every rank calls it."""
+    world = dist.get_world_size(group)
+    model.open_peers(_all_gather_bytes(model.ipc_handles(), world, group), world)
+    if scatter_qkv:
+        model.open_qkv_peers(_all_gather_bytes(model.ipc_handle("qkv"), world, group), world)
     model.fused_exchange = True
 
 

@@ -82,6 +82,7 @@ struct Params {
   int nseg;
   EpiSeg seg[kMaxSegs];
   int* err;
+  int fence_sys;  // a segment stores to other GPUs: fence.sys after the epilogue's stores
   // Test hook (bonsai_debug_stall_next_gemm): the load warp issues nothing,
   // so every other role's first bounded wait expires and the kernel unwinds
   // through its abort path with no copy or MMA in flight.  0 in normal use.
@@ -332,6 +333,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int d = rem - h * hd;
         base = ((size_t)(which * sg.heads + h) * sg.seq_total + sg.tok_off) * hd + d;
         stride = (uint32_t)hd;
+        if (sg.route_heads > 0) {  // the head's owner (unrolled select: no dynamic indexing)
+          const int owner = h / sg.route_heads;
+#pragma unroll
+          for (int r = 0; r < kMaxPeers; ++r)
+            if (r == owner) sg.dst = sg.route[r];
+        }
       } else if (mode == EPI_SWIGLU_F16) {
         base = (size_t)sg.col_off + (rr >> 1);
       } else if (mode >= 0) {
@@ -392,6 +399,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) bar_arrive(&dempty[b]);
     }
+    if (p.fence_sys) __threadfence_system();  // peer stores ordered before the kernel's end
   }
 
   __syncthreads();
@@ -439,6 +447,7 @@ struct Params {
   int nseg;
   EpiSeg seg[kMaxSegs];
   int* err;
+  int fence_sys;  // a segment stores to other GPUs: fence.sys after the epilogue's stores
 };
 
 template <bool kBF16>
@@ -650,6 +659,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int d = rem - h * hd;
         base = ((size_t)(which * sg.heads + h) * sg.seq_total + sg.tok_off) * hd + d;
         stride = (uint32_t)hd;
+        if (sg.route_heads > 0) {  // the head's owner (unrolled select: no dynamic indexing)
+          const int owner = h / sg.route_heads;
+#pragma unroll
+          for (int r = 0; r < kMaxPeers; ++r)
+            if (r == owner) sg.dst = sg.route[r];
+        }
       } else if (mode == EPI_SWIGLU_F16) {
         base = (size_t)sg.col_off + (rr >> 1);
       } else if (mode >= 0) {
@@ -709,6 +724,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) bar_arrive_remote(dempty0 + b * 8u);
     }
+    if (p.fence_sys) __threadfence_system();  // peer stores ordered before the kernel's end
   }
 
   tc_fence_before();
@@ -965,6 +981,15 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
     for (int g = 0; g < sel->groups; ++g) fbase[g] = sel->base[g];
   }
   const int nf = fgroups * fcount;
+  bool routed = false;
+  for (int i = 0; i < nseg; ++i) {
+    if (segs[i].route_heads <= 0) continue;
+    if (segs[i].mode != EPI_QKV_F16 || segs[i].heads % segs[i].route_heads != 0)
+      return fail(-1, "b1_gemm: head routing needs a QKV segment whose heads divide by route_heads");
+    for (int r = 0; r < segs[i].heads / segs[i].route_heads; ++r)
+      if (!segs[i].route[r]) return fail(-1, "b1_gemm: null head route");
+    routed = true;
+  }
 
   // Kernel choice: estimated time = waves x tile time, with a 256x256 pair
   // tile (two SMs) taking kPairTileCost 128x128-tile times of one SM (about
@@ -1019,6 +1044,7 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
     q.nseg = nseg;
     for (int i = 0; i < nseg; ++i) q.seg[i] = segs[i];
     q.err = device_error_word();
+    q.fence_sys = routed ? 1 : 0;
     auto k2 = x_bf16 ? gemm::pair::b1_gemm_pair_kernel<true> : gemm::pair::b1_gemm_pair_kernel<false>;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -1057,6 +1083,7 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
   p.nseg = nseg;
   for (int i = 0; i < nseg; ++i) p.seg[i] = segs[i];
   p.err = device_error_word();
+  p.fence_sys = routed ? 1 : 0;
   p.idle_loads = stall ? 1 : 0;
 
   const int grid = (int)std::min<long long>(tiles1, num_sms());

@@ -178,6 +178,14 @@ struct bonsai_dit {
   __half* peer_xm[kMaxPeers] = {};
   __half* peer_cat[kMaxPeers] = {};
   std::vector<void*> ipc_opened;  // peer mappings opened by bonsai_dit_open_peers
+  // QKV scatter (bonsai_dit_set_qkv_peers, fused exchanges only): phase 0
+  // computes q/k/v of this rank's own rows for every head and the GEMM
+  // epilogue stores head h into peer_qkv[h / hl] (its owner's q/k/v buffer),
+  // instead of phase 0 broadcasting xm rows and phase 1 computing the own
+  // heads' q/k/v over every row.
+  bool qkv_scatter = false;
+  __half* peer_qkv[kMaxPeers] = {};
+  std::vector<void*> ipc_opened_qkv;
   // device copies of caller inputs for the host-buffer entry point
   float *in_img = nullptr, *in_txt = nullptr, *in_pooled = nullptr, *out_buf = nullptr;
 };
@@ -287,6 +295,14 @@ EpiSeg seg_qkv(const Cfg& c, int row_end, __half* qkv, int tok_off) {
   s.seq_total = c.L;
   s.tok_off = tok_off;
   s.head_dim = c.hd;
+  return s;
+}
+
+// seg_qkv whose heads go to their owners' q/k/v buffers (QKV scatter).
+EpiSeg seg_qkv_routed(const bonsai_dit* m, int tok_off) {
+  EpiSeg s = seg_qkv(m->c, 3 * m->c.H, m->qkv, tok_off);
+  for (int r = 0; r < m->world; ++r) s.route[r] = m->peer_qkv[r];
+  s.route_heads = m->hl;
   return s;
 }
 
@@ -404,6 +420,20 @@ int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
   // disjoint tokens of qkv until the joint attention: the text chain runs on
   // its own stream, concurrently with the image chain, and is joined back
   // into st before anything that reads both (and at the end of every phase).
+  if (phase == 0 && m->qkv_scatter) {
+    // own rows only: LN-modulate, then q/k/v of every head, each head stored
+    // into its owner's q/k/v buffer by the GEMM epilogue
+    RC(fork_aux(m, st));
+    RC(launch_ln_modulate_f16(m->hidden + (size_t)tx.a * H, tx.n(), H, mt + 0 * H, mt + 1 * H, 1e-6f,
+                              m->xm + (size_t)tx.a * H, H, ts));
+    EpiSeg s = seg_qkv_routed(m, tx.a);
+    RC(launch_b1_gemm(m->xm + (size_t)tx.a * H, H, tx.n(), w.txt_qkv, &s, 1, false, ts));
+    RC(launch_ln_modulate_f16(m->hidden + (size_t)im.a * H, im.n(), H, mi + 0 * H, mi + 1 * H, 1e-6f,
+                              m->xm + (size_t)im.a * H, H, st));
+    s = seg_qkv_routed(m, im.a);
+    RC(launch_b1_gemm(m->xm + (size_t)im.a * H, H, im.n(), w.img_qkv, &s, 1, false, st));
+    return join_aux(m, st);
+  }
   if (phase == 0) {
     RC(fork_aux(m, st));
     RC(launch_ln_modulate_f16_peers(m->hidden + (size_t)tx.a * H, tx.n(), H, mt + 0 * H, mt + 1 * H,
@@ -411,6 +441,18 @@ int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
     RC(launch_ln_modulate_f16_peers(m->hidden + (size_t)im.a * H, im.n(), H, mi + 0 * H, mi + 1 * H,
                                     1e-6f, m->xm + (size_t)im.a * H, H, xm_copies(m, im.a), st));
     return join_aux(m, st);
+  }
+  if (phase == 1 && m->qkv_scatter) {
+    // every row of this rank's heads is in its q/k/v buffer (phase 0 of all ranks)
+    const size_t hs = (size_t)c.L * c.hd;
+    __half* q = m->qkv + (size_t)m->h0 * hs;
+    __half* k = m->qkv + (size_t)(c.heads + m->h0) * hs;
+    __half* v = m->qkv + (size_t)(2 * c.heads + m->h0) * hs;
+    RC(launch_qk_norm_rope(q, k, m->hl, c.L, w.nq_txt, w.nq_img, w.nk_txt, w.nk_img, Lt, 1e-6f,
+                           m->cos_t, m->sin_t, st));
+    const RowRoutes rr = cat_routes(m);
+    return launch_attention(q, k, v, m->hl, c.L, c.hd, 1.0f / sqrtf((float)c.hd),
+                            m->cat + (size_t)m->h0 * c.hd, C, st, &rr);
   }
   if (phase == 1) {
     const TileSel sel = head_tiles(m);
@@ -470,6 +512,31 @@ int single_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
   const int H = c.H, L = c.L, C = c.C();
   const float* md = single_mods(m, i);
   const int rows = m->r1 - m->r0;
+  if (m->qkv_scatter) {
+    const size_t hs = (size_t)L * c.hd;
+    if (phase == 0) {
+      // own rows: LN-modulate, then to_qkv_mlp_proj in one launch -- q/k/v of
+      // every head to the heads' owners, the MLP activation into own cat rows
+      RC(launch_ln_modulate_f16(m->hidden + (size_t)m->r0 * H, rows, H, md, md + H, 1e-6f,
+                                m->xm + (size_t)m->r0 * H, H, st));
+      EpiSeg segs[2];
+      segs[0] = seg_qkv_routed(m, m->r0);
+      segs[1] = seg_of(c.swiglu ? EPI_SWIGLU_F16 : EPI_GELU_F16, 3 * H, 3 * H + c.mlp_in_rows,
+                       m->cat + (size_t)m->r0 * C, C, H, nullptr);
+      return launch_b1_gemm(m->xm + (size_t)m->r0 * H, H, rows, w.proj, segs, 2, false, st);
+    }
+    if (phase == 1) {
+      __half* q = m->qkv + (size_t)m->h0 * hs;
+      __half* k = m->qkv + (size_t)(c.heads + m->h0) * hs;
+      __half* v = m->qkv + (size_t)(2 * c.heads + m->h0) * hs;
+      RC(launch_qk_norm_rope(q, k, m->hl, L, w.nq, w.nq, w.nk, w.nk, L, 1e-6f, m->cos_t, m->sin_t, st));
+      const RowRoutes rr = cat_routes(m);
+      return launch_attention(q, k, v, m->hl, L, c.hd, 1.0f / sqrtf((float)c.hd),
+                              m->cat + (size_t)m->h0 * c.hd, C, st, &rr);
+    }
+    EpiSeg s = seg_of(EPI_RESID_F32, 0, H, m->hidden + (size_t)m->r0 * H, H, 0, md + 2 * H);
+    return launch_b1_gemm(m->cat + (size_t)m->r0 * C, C, rows, w.out, &s, 1, false, st);
+  }
   if (phase == 0)
     return launch_ln_modulate_f16_peers(m->hidden + (size_t)m->r0 * H, rows, H, md, md + H, 1e-6f,
                                         m->xm + (size_t)m->r0 * H, H, xm_copies(m, m->r0), st);
@@ -743,6 +810,7 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
 bonsai_dit::~bonsai_dit() {
   cudaDeviceSynchronize();
   for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
+  for (void* p : ipc_opened_qkv) cudaIpcCloseMemHandle(p);
   if (graph) cudaGraphExecDestroy(graph);
   if (cap_stream) cudaStreamDestroy(cap_stream);
   if (aux) cudaStreamDestroy(aux);
@@ -928,6 +996,7 @@ int bonsai_dit_set_partition(bonsai_dit_t m, int rank, int world) {
   m->hl = c.heads / world;
   m->h0 = rank * m->hl;
   m->fused = false;  // peers belong to a partition: set them again after a change
+  m->qkv_scatter = false;
   if (m->graph) {
     cudaGraphExecDestroy(m->graph);
     m->graph = nullptr;
@@ -939,6 +1008,7 @@ int bonsai_dit_set_peers(bonsai_dit_t m, void* const* xm, void* const* cat, int 
   if (!m) return fail(BONSAI_ERR_ARG, "dit_set_peers: null model");
   if (!xm || !cat) {
     m->fused = false;
+    m->qkv_scatter = false;
     return 0;
   }
   if (world != m->world || world < 2 || world > kMaxPeers)
@@ -972,6 +1042,7 @@ int bonsai_dit_open_peers(bonsai_dit_t m, const void* handles, int world) {
   for (void* p : m->ipc_opened) cudaIpcCloseMemHandle(p);
   m->ipc_opened.clear();
   m->fused = false;
+  m->qkv_scatter = false;
   void* xm[kMaxPeers] = {};
   void* cat[kMaxPeers] = {};
   const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
@@ -990,6 +1061,59 @@ int bonsai_dit_open_peers(bonsai_dit_t m, const void* handles, int world) {
     }
   }
   return bonsai_dit_set_peers(m, xm, cat, world);
+}
+
+int bonsai_dit_set_qkv_peers(bonsai_dit_t m, void* const* qkv, int world) {
+  if (!m) return fail(BONSAI_ERR_ARG, "dit_set_qkv_peers: null model");
+  if (!qkv) {
+    m->qkv_scatter = false;
+    return 0;
+  }
+  if (!m->fused)
+    return fail(BONSAI_ERR_ARG, "dit_set_qkv_peers: set the xm / cat peers first (bonsai_dit_set_peers)");
+  if (world != m->world) return fail(BONSAI_ERR_ARG, "dit_set_qkv_peers: world must match the partition");
+  if (qkv[m->rank] != m->qkv)
+    return fail(BONSAI_ERR_ARG, "dit_set_qkv_peers: entry [rank] must be this model's own qkv");
+  for (int r = 0; r < world; ++r) {
+    if (!qkv[r] || (reinterpret_cast<uintptr_t>(qkv[r]) & 15))
+      return fail(BONSAI_ERR_ARG, "dit_set_qkv_peers: null or misaligned buffer");
+    m->peer_qkv[r] = static_cast<__half*>(qkv[r]);
+  }
+  m->qkv_scatter = true;
+  return 0;
+}
+
+int bonsai_dit_ipc_handle(bonsai_dit_t m, const char* name, void* out) {
+  if (!m || !name || !out) return fail(BONSAI_ERR_ARG, "dit_ipc_handle: null argument");
+  void* ptr = nullptr;
+  RC(bonsai_dit_buffer(m, name, &ptr, nullptr));
+  cudaIpcMemHandle_t h;
+  RC(cuda_status(cudaIpcGetMemHandle(&h, ptr), "dit_ipc_handle"));
+  std::memcpy(out, &h, sizeof(h));
+  return 0;
+}
+
+int bonsai_dit_open_qkv_peers(bonsai_dit_t m, const void* handles, int world) {
+  if (!m || !handles) return fail(BONSAI_ERR_ARG, "dit_open_qkv_peers: null argument");
+  if (world != m->world || world < 2 || world > kMaxPeers)
+    return fail(BONSAI_ERR_ARG, "dit_open_qkv_peers: world must match bonsai_dit_set_partition (2..8)");
+  for (void* p : m->ipc_opened_qkv) cudaIpcCloseMemHandle(p);
+  m->ipc_opened_qkv.clear();
+  m->qkv_scatter = false;
+  void* qkv[kMaxPeers] = {};
+  const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int r = 0; r < world; ++r) {
+    if (r == m->rank) {
+      qkv[r] = m->qkv;
+      continue;
+    }
+    void* p = nullptr;
+    RC(cuda_status(cudaIpcOpenMemHandle(&p, h[r], cudaIpcMemLazyEnablePeerAccess),
+                   "dit_open_qkv_peers: open handle"));
+    m->ipc_opened_qkv.push_back(p);
+    qkv[r] = p;
+  }
+  return bonsai_dit_set_qkv_peers(m, qkv, world);
 }
 
 int bonsai_dit_buffer(bonsai_dit_t m, const char* name, void** ptr, long long* bytes) {

@@ -68,6 +68,8 @@ enum EpiMode : int {
   EPI_SWIGLU_F16 = 5,  // interleaved gate/value rows -> dst f16 silu(g)*v at col_off + (row-row_begin)/2
 };
 
+constexpr int kMaxPeers = 8;
+
 struct EpiSeg {
   int mode = EPI_F32;
   int row_begin = 0, row_end = 0;
@@ -76,6 +78,12 @@ struct EpiSeg {
   int col_off = 0;
   const float* gate = nullptr;
   int heads = 0, seq_total = 0, tok_off = 0, head_dim = 128;
+  // EPI_QKV_F16 only: with route_heads > 0, head h is stored through
+  // route[h / route_heads] (at the same offsets) instead of dst -- each rank's
+  // q/k/v buffer of a head split, peer-mapped -- and the kernel ends with a
+  // system-scope fence after its stores.
+  __half* route[kMaxPeers] = {};
+  int route_heads = 0;
 };
 
 constexpr int kMaxSegs = 2;
@@ -126,7 +134,6 @@ int st_read(StFile& f, const StTensor& t, void* dst, long long bytes);
 // offsets, into copies[0..n) (other GPUs' buffers reached through peer
 // mappings, or other buffers of this GPU).  The kernel ends with a
 // system-scope fence after its stores.
-constexpr int kMaxPeers = 8;
 struct PeerCopies {
   __half* y[kMaxPeers - 1] = {};
   int n = 0;

@@ -321,6 +321,27 @@ int bonsai_dit_ipc_handles(bonsai_dit_t m, void* out);
  * rank's own entry ignored) and set them as peers; the mappings are closed
  * by the next call or bonsai_dit_destroy. */
 int bonsai_dit_open_peers(bonsai_dit_t m, const void* handles, int world);
+/* QKV scatter form of the fused exchanges (after bonsai_dit_set_peers /
+ * bonsai_dit_open_peers): every rank's q/k/v buffer ("qkv") as a device
+ * pointer valid on this GPU (entry [rank] = its own).  Phase 0 then computes
+ * q, k and v of this rank's own token rows for EVERY head, and the GEMM's
+ * epilogue stores head h straight into the q/k/v buffer of the rank that
+ * owns h (the split's all-to-all, fused into the GEMM); phase 0 no longer
+ * stores xm rows into the other ranks, and phase 1 runs only the Q/K norm +
+ * RoPE and the attention of this rank's heads.  Per rank and block this
+ * sends 3 * L/world * 3072 * 2 * (world-1)/world bytes instead of the xm
+ * broadcast's L/world * 3072 * 2 * (world-1), overlapped with the GEMM: fewer
+ * bytes from world = 4 on.  The caller's ordering between the phases is
+ * unchanged.  NULL switches back to the xm broadcast;
+ * bonsai_dit_set_partition and bonsai_dit_set_peers(NULL) do too. */
+int bonsai_dit_set_qkv_peers(bonsai_dit_t m, void* const* qkv, int world);
+/* CUDA IPC handle (64 bytes) of one engine buffer: "hidden", "xm", "cat" or
+ * "qkv" (bonsai_dit_buffer's names). */
+int bonsai_dit_ipc_handle(bonsai_dit_t m, const char* name, void* out);
+/* Open every rank's "qkv" handle (world x 64 bytes, rank-major, this rank's
+ * own entry ignored) and pass them to bonsai_dit_set_qkv_peers; the mappings
+ * are closed by the next call or bonsai_dit_destroy. */
+int bonsai_dit_open_qkv_peers(bonsai_dit_t m, const void* handles, int world);
 /* Device pointer and size of an engine buffer shared with the caller's
  * collectives: "hidden" f32 [L][3072], "xm" f16 [L][3072],
  * "cat" f16 [L][3072 + mlp], "qkv" f16 [3][24][L][128]. */

@@ -8,8 +8,12 @@ models' buffers -- or, fused, by the kernels themselves: each model is given
 the other models' xm / cat as its peers (bonsai_dit_set_peers), so phase 0
 stores its rows into every model's xm and phase 1's attention stores every
 row into its owner's cat, the path a multi-GPU run takes over peer-mapped
-memory.  Every rank's prediction must equal the unpartitioned forward.  World 3 and 8 give 8 and 3 heads per rank, so the Q/K/V weight-tile
-selections have even and odd tile counts; each GEMM kernel is forced in turn.
+memory; in the QKV scatter form each model is also given the other models'
+q/k/v buffers, and phase 0's Q/K/V GEMM over its own rows stores every head
+into its owner's buffer.  Every rank's prediction must equal the
+unpartitioned forward.  World 3 and 8 give 8 and 3 heads per rank, so the
+Q/K/V weight-tile selections have even and odd tile counts; each GEMM kernel
+is forced in turn.
 """
 import numpy as np
 import pytest
@@ -31,7 +35,7 @@ def _inputs(m, seed=3):
     return img, txt, pooled
 
 
-def _emulated_forward(preset, world, img, txt, pooled, t, fused=False):
+def _emulated_forward(preset, world, img, txt, pooled, t, fused=False, scatter=False):
     import torch
     ms = [bb.Dit(preset, IMG_H * IMG_W, TXT, IMG_H, IMG_W, depth=1, depth_single=1, seed=5)
           for _ in range(world)]
@@ -47,6 +51,10 @@ def _emulated_forward(preset, world, img, txt, pooled, t, fused=False):
         if fused:
             for m in ms:
                 m.set_peers([b.data_ptr() for b in xm], [b.data_ptr() for b in cat])
+        if scatter:  # phase 0's Q/K/V GEMM stores each head into its owner's qkv
+            qkv = [m.buffer("qkv", torch.float16, (3 * 24 * L * 128,)) for m in ms]
+            for m in ms:
+                m.set_qkv_peers([b.data_ptr() for b in qkv])
 
         def gather_rows(bufs):
             for r in range(world):
@@ -141,3 +149,39 @@ def test_headsplit_emulated_with_key_split(gpu, monkeypatch, fused):
         rel = float((g - r).abs().max() / r.pow(2).mean().sqrt())
         assert cos >= 0.9999 and rel <= 1e-2, (fused, rank, cos, rel)
     assert bb.device_error() == 0
+
+
+@pytest.mark.parametrize("kernel", ["single", "pair"])
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_headsplit_emulated_qkv_scatter(gpu, monkeypatch, world, kernel):
+    """The QKV scatter form of the fused exchanges (bonsai_dit_set_qkv_peers)
+    equals the unpartitioned forward."""
+    import torch
+    monkeypatch.setenv("BONSAI_B1_KERNEL", kernel)
+    preset = bb.PRESET_FLUX1
+    ref_m = bb.Dit(preset, IMG_H * IMG_W, TXT, IMG_H, IMG_W, depth=1, depth_single=1, seed=5)
+    try:
+        img, txt, pooled = _inputs(ref_m)
+        ref = torch.empty(ref_m.img, ref_m.in_ch, device="cuda")
+        ref_m.forward(img, txt, pooled, 600.0, ref)
+        torch.cuda.synchronize()
+    finally:
+        ref_m.close()
+    outs = _emulated_forward(preset, world, img, txt, pooled, 600.0, fused=True, scatter=True)
+    r = ref.double().flatten()
+    for rank, o in enumerate(outs):
+        g = o.double().flatten()
+        cos = float(g @ r / (g.norm() * r.norm()))
+        rel = float((g - r).abs().max() / r.pow(2).mean().sqrt())
+        assert cos >= 0.99999 and rel <= 1e-3, (world, kernel, rank, cos, rel)
+    assert bb.device_error() == 0
+
+
+def test_qkv_scatter_needs_fused_peers(gpu):
+    m = bb.Dit(bb.PRESET_FLUX1, IMG_H * IMG_W, TXT, IMG_H, IMG_W, depth=1, depth_single=1, seed=5)
+    try:
+        m.set_partition(0, 2)
+        with pytest.raises(bb.BonsaiError, match="set the xm / cat peers first"):
+            m.set_qkv_peers([1 << 20, 2 << 20])
+    finally:
+        m.close()

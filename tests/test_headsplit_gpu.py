@@ -3,9 +3,10 @@
 Spawns two NCCL ranks (one per GPU); each builds the same seeded model, runs
 bonsai_b200.headsplit.forward, and rank 0 compares the prediction with the
 unpartitioned bonsai_dit_forward of an identical model.  Both exchange forms
-run: NCCL collectives between the phases, and the fused form in which the
+run: NCCL collectives between the phases, the fused form in which the
 kernels store into the other GPU's buffers through CUDA IPC mappings
-(headsplit.enable_fused).  Needs >= 2 GPUs (skipped otherwise).
+(headsplit.enable_fused), and its QKV scatter variant (phase 0's Q/K/V GEMM
+stores every head into its owner's buffer).  Needs >= 2 GPUs (skipped otherwise).
 """
 import os
 import socket
@@ -28,7 +29,7 @@ SMALL = dict(img=256, txt=64, grid=16, depth=2, single=2)
 FULL = dict(img=16384, txt=512, grid=128, depth=19, single=38)
 
 
-def _worker(rank, world, port, q, shape, fused):
+def _worker(rank, world, port, q, shape, fused, scatter=False):
     import datetime
     import sys
     from pathlib import Path
@@ -50,7 +51,7 @@ def _worker(rank, world, port, q, shape, fused):
                    depth_single=c["single"], seed=11)
         m.set_partition(rank, world)
         if fused:
-            headsplit.enable_fused(m)
+            headsplit.enable_fused(m, scatter_qkv=scatter)
         rng = np.random.default_rng(3)
         img = torch.from_numpy(rng.standard_normal((m.img, m.in_ch)).astype(np.float32)).cuda()
         txt = torch.from_numpy(rng.standard_normal((m.txt, m.ctx_dim)).astype(np.float32)).cuda()
@@ -77,9 +78,10 @@ def _worker(rank, world, port, q, shape, fused):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fused", [False, True], ids=["nccl", "fused"])
+@pytest.mark.parametrize("fused,scatter", [(False, False), (True, False), (True, True)],
+                         ids=["nccl", "fused", "fused_qkv_scatter"])
 @pytest.mark.parametrize("shape", [SMALL, FULL], ids=["small", "2048sq_full_depth"])
-def test_headsplit_two_gpus_matches_single(shape, fused):
+def test_headsplit_two_gpus_matches_single(shape, fused, scatter):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -87,7 +89,8 @@ def test_headsplit_two_gpus_matches_single(shape, fused):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, shape, fused)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, shape, fused, scatter))
+             for r in range(2)]
     for p in procs:
         p.start()
     results = dict((r, (res, err)) for r, res, err in (q.get(timeout=600) for _ in range(2)))
