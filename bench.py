@@ -238,7 +238,7 @@ class CpuSample:
                 f"of the ggml built-ins); scaled to 19 double + 38 single blocks + modulation + edges")
 
 
-def step_config(world: int, split: bool = False, exchange: str = "fused") -> dict:
+def step_config(world: int, split: bool = False, exchange: str = "scatter") -> dict:
     """The bench line's `config`, identical in both arms for the same N."""
     if split:
         par = {"fused": f"head/row split over {world} GPUs, exchanges fused into the producing "
@@ -905,7 +905,7 @@ def main():
     ap.add_argument("--workload", choices=["1024", "2048"], default="1024",
                     help="1024: config 4, one image per GPU (data parallel, default); "
                          "2048: config 5(b), one 2048^2 image split by heads/rows across the GPUs")
-    ap.add_argument("--exchange", choices=["fused", "scatter", "nccl"], default="fused",
+    ap.add_argument("--exchange", choices=["fused", "scatter", "nccl"], default="scatter",
                     help="the 2048^2 split on N > 1 GPUs: exchanges fused into the kernels over "
                          "peer memory (fused: the LN-modulate kernel broadcasts xm rows; scatter: "
                          "the Q/K/V GEMM stores every head into its owner's buffer) or NCCL "
