@@ -634,6 +634,15 @@ def run_bonsai(args):
     model.close()
     if not split and not args.no_split:
         line["split_2048"] = measure_split_2048(args, rank, world, dist)
+    if world == 1 and not split and not args.no_side:
+        # BASELINE configs 1-3 (GPU and reference CPU path) and the next
+        # pipeline stage, the VAE decode, outside the headline's timed region
+        with stdout_to_stderr():
+            line["configs_1_3"] = measure_configs(args)
+            vae = measure_vae(10, 3, not args.no_cpu_baseline)
+        line["vae_1024"] = {k: vae[k] for k in ("metric", "value", "unit", "steps", "warmup",
+                                                "roofline", "e2e", "clocks", "cpu_baseline",
+                                                "gn_apply_gbs", "gpu_launches") if k in vae}
     if rank == 0:
         emit_json(line)
     if dist:
@@ -652,8 +661,15 @@ def _cpu_model() -> str:
 
 
 def run_configs(args):
-    """--configs: BASELINE configs 1-3 timed on the GPU and with the
-    reference CPU path on all host cores, one JSON line each.
+    """--configs: BASELINE configs 1-3 as JSON lines (see measure_configs)."""
+    for d in measure_configs(args):
+        emit_json(d)
+    return 0
+
+
+def measure_configs(args) -> list:
+    """BASELINE configs 1-3 timed on the GPU and with the reference CPU path
+    on all host cores; one dict per config.
 
     C1 one Flux double block, 256 text + 1024 image tokens (32x32 grid);
     C2 joint attention only, 24 heads x 128, L = 4352;
@@ -674,8 +690,7 @@ def run_configs(args):
     info = {"cpu_threads": threads, "cpu_model": _cpu_model(), "device": torch.cuda.get_device_name(0)}
     R = O.ref()
     if R is None:
-        emit_json({"configs": "unavailable", "why": "oracle/_ref (the reference's b1 kernel) is not built"})
-        return 0
+        return [{"configs": "unavailable", "why": "oracle/_ref (the reference's b1 kernel) is not built"}]
     fast = ctypes.CDLL(str(ROOT / "oracle/_build/libbonsai_oracle_fast.so"))
     vp, ci, cf = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
     fast.orc_set_threads.argtypes = [ci]
@@ -698,13 +713,15 @@ def run_configs(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / K_steps
 
+    results = []
+
     def emit(name, flop, gms, cms, extra=None):
         d = {"config": name, "gpu_ms": round(gms, 4), "cpu_ms": round(cms, 1),
              "speedup": round(cms / gms, 1), "gpu_tflops": round(flop / gms / 1e9, 1),
              "cpu_gflops": round(flop / cms / 1e6, 1), **info}
         if extra:
             d.update(extra)
-        emit_json(d)
+        results.append(d)
 
     rng = np.random.default_rng(1234)
     # ---- C1: one double block
@@ -771,7 +788,7 @@ def run_configs(args):
                 cms = 1000 * (time.perf_counter() - t0)
             emit(f"C3 GEMM M={M} K={Kd} N={N}", 2.0 * M * N * Kd, gms, cms)
         wgt.free()
-    return 0
+    return results
 
 
 def vae_flops(lh: int, lw: int, folded: bool) -> float:
@@ -794,7 +811,14 @@ def vae_flops(lh: int, lw: int, folded: bool) -> float:
 
 
 def run_vae(args):
-    """--vae: the Flux VAE decoder (the stage after the denoise loop in the
+    """--vae: the VAE decode as the bench line (see measure_vae)."""
+    emit_json(measure_vae(args.steps, args.warmup, not args.no_cpu_baseline,
+                          os.environ.get("BONSAI_CLOCK_LOG")))
+    return 0
+
+
+def measure_vae(steps: int, warmup: int, cpu_baseline: bool, clock_log=None) -> dict:
+    """The Flux VAE decoder (the stage after the denoise loop in the
     reference's pipeline, src/vae_decoder.cpp + src/vae_graph.cpp) decoding a
     64 x 64 x 128 encoded latent to a 1024^2 image on one GPU, synthetic
     seeded weights.  value = device-timed ms per decode (latent resident);
@@ -807,7 +831,7 @@ def run_vae(args):
     torch.cuda.init()
     bb.init(0)
     lh = lw = 64
-    K, W = args.steps, args.warmup
+    K, W = steps, max(3, warmup)
     v = bb.Vae(lh, lw, seed=1234)
     rng = np.random.default_rng(7)
     lat_h = torch.from_numpy(rng.uniform(-1, 1, (128, lh, lw)).astype(np.float32)).pin_memory()
@@ -818,7 +842,7 @@ def run_vae(args):
     torch.cuda.synchronize()
     assert bb.device_error() == 0
     stream = torch.cuda.current_stream()
-    clocks = ClockSampler(0, os.environ.get("BONSAI_CLOCK_LOG"))
+    clocks = ClockSampler(0, clock_log)
     clocks.start()
     bb.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -877,7 +901,7 @@ def run_vae(args):
                 "output_finite": bool(finite and np.isfinite(out_np).all())},
     }
     v.close()
-    if not args.no_cpu_baseline:
+    if cpu_baseline:
         from oracle import vae_oracle as vo
         sys.path.insert(0, str(ROOT / "tests"))
         from vae_weights import make_state_dict
@@ -891,8 +915,7 @@ def run_vae(args):
                                 "cores": os.cpu_count() or 1, "kind": "port",
                                 "sample": f"NumPy f32 restatement, 8x8 latent (128^2 image) in "
                                           f"{s_sec:.2f} s, scaled x{scale:.1f} by FLOPs"}
-    emit_json(line)
-    return 0
+    return line
 
 
 def main():
@@ -910,6 +933,9 @@ def main():
                          "peer memory (fused: the LN-modulate kernel broadcasts xm rows; scatter: "
                          "the Q/K/V GEMM stores every head into its owner's buffer) or NCCL "
                          "collectives between the phases")
+    ap.add_argument("--no-side", action="store_true",
+                    help="skip the 1-GPU side measurements (BASELINE configs 1-3 and the VAE "
+                         "decode) that a default 1-GPU run adds to its line")
     ap.add_argument("--no-split", action="store_true",
                     help="skip the 2048^2 head/row-split measurement (split_2048) that every "
                          "default run adds beside the headline")
