@@ -708,6 +708,420 @@ __global__ void combine_kernel(const float* __restrict__ part_o, const float* __
   if (routes.n > 0) __threadfence_system();  // peer stores ordered before the kernel's end
 }
 
+// ------------------------------------------------------------------------
+// attention_pair128_kernel (BONSAI_ATTN=v2): a cluster of two CTAs per head
+// x 256 queries -- one 128-query tile per CTA, every product one
+// cta_group::2 MMA of M = 256 -- with keys in blocks of 128.  Q K^T then has
+// N = 128: per SM and k-step it reads Q (4 KB) and this CTA's 64 keys (2 KB)
+// in 64 clocks, 96 B/clk, under shared memory's 128 B/clk (with 64-key
+// blocks it needs 160 B/clk and waits on shared memory).  The 128 keys of a
+// block feed two independent online softmaxes: warps 0-3 take keys [0, 64)
+// of every block, warps 4-7 keys [64, 128), each half with its own running
+// max, row sum and O accumulator in TMEM (O_a, O_b), merged in the
+// epilogue, so neither half ever waits for the other's max.  S is
+// double-buffered by block parity.  TMEM: S(even) [0,128) S(odd) [128,256)
+// O_a [256,384) O_b [384,512); P of half h (f16 pairs) overwrites the first
+// 32 columns of that half's S.  MMA order: S(0) S(1), then per block j:
+// P_a V_a(j), P_b V_b(j), S(j + 2) -- S(j + 2) reuses the buffer whose P the
+// two products before it have read.
+namespace v2 {
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int HALF = 64;
+constexpr int KS = 4;
+constexpr int VS = 4;
+constexpr int Q_BYTES = BQ * HD * 2;       // 32 KB: two 64-dim halves of 16 KB
+constexpr int Q_HALF = Q_BYTES / 2;
+constexpr int K_SLOT = HALF * HD * 2;      // this CTA's 64 keys x 128 dims: 16 KB
+constexpr int K_SLOT_HALF = K_SLOT / 2;    // 64 keys x 64 dims
+constexpr int V_SLOT = BKV * 64 * 2;       // this CTA's 64 dims x 128 keys: 16 KB
+constexpr int BAR_BYTES = 512;
+constexpr int STAT_BYTES = 4 * BQ * 4;     // (max, sum) of both halves, per row
+constexpr int SMEM_BYTES = 1024 + Q_BYTES + (KS + VS) * K_SLOT + BAR_BYTES + STAT_BYTES;
+constexpr int S_COL = 0, O_COL = 256;
+static_assert(K_SLOT == V_SLOT, "K and V stages share the slot size");
+}  // namespace v2
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attention_pair128_kernel(const __grid_constant__ CUtensorMap qmap,
+                             const __grid_constant__ CUtensorMap kmap,
+                             const __grid_constant__ CUtensorMap vmap, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* qs = smem;
+  uint8_t* ks = qs + v2::Q_BYTES;
+  uint8_t* vs = ks + v2::KS * v2::K_SLOT;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + v2::VS * v2::V_SLOT);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + v2::KS;
+  uint64_t* v_full = k_empty + v2::KS;
+  uint64_t* v_empty = v_full + v2::VS;
+  uint64_t* s_full = v_empty + v2::VS;  // [2] by block parity
+  uint64_t* p_ready = s_full + 2;       // [4] key half * 2 + block parity
+  uint64_t* pv_done = p_ready + 4;      // [4] key half * 2 + block parity
+  uint64_t* drain = pv_done + 4;
+  uint64_t* stat_bar = drain + 1;       // both halves' (max, sum) published
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stat_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* st_m = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + v2::BAR_BYTES);
+  float* st_l = st_m + 2 * v2::BQ;  // st_m / st_l [half][row]
+
+  const int warp = threadIdx.x / 32;
+  const uint32_t lane = lane_id();
+  const int head = blockIdx.y;
+  const uint32_t rank = cluster_ctarank();
+  const int q0 = (int)(blockIdx.x >> 1) * 2 * v2::BQ + (int)rank * v2::BQ;
+  const bool leader = rank == 0;
+  const int nkv = (p.seq + v2::BKV - 1) / v2::BKV;
+
+  if (threadIdx.x == 0) {
+    bar_init(q_full, 1);
+    for (int s = 0; s < v2::KS; ++s) {
+      bar_init(&k_full[s], 1);
+      bar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < v2::VS; ++s) {
+      bar_init(&v_full[s], 1);
+      bar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) bar_init(&s_full[i], 1);
+    for (int i = 0; i < 4; ++i) {
+      bar_init(&p_ready[i], 8);  // 4 warps of the half in each CTA
+      bar_init(&pv_done[i], 1);
+    }
+    bar_init(drain, 1);
+    bar_init(stat_bar, 8 * 32);  // every softmax thread of this CTA
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == WARP_MMA) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // barrier inits and TMEM of both CTAs visible to the pair
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto lead_bar = [&](uint64_t* b) -> uint32_t { return mapa_shared(smem_u32(b), 0); };
+
+  if (warp >= 8) {
+    regs_dec<kAuxRegs>();
+    if (warp == WARP_TMA) {
+      if (elect_one()) {
+        tma_prefetch_desc(&qmap);
+        tma_prefetch_desc(&kmap);
+        tma_prefetch_desc(&vmap);
+        if (leader) bar_arrive_expect_tx(q_full, 2 * v2::Q_BYTES);
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d_pair(qs + h * v2::Q_HALF, &qmap, lead_bar(q_full), h * 64, q0, head);
+        bool ok = true;
+        for (int j = 0; j < nkv && ok; ++j) {
+          const int sk = j % v2::KS;
+          if (!wait_bar(&k_empty[sk], ((j / v2::KS) & 1) ^ 1, abort_flag, p.err,
+                        DEV_ERR_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          if (leader) bar_arrive_expect_tx(&k_full[sk], 2 * v2::K_SLOT);
+          for (int h = 0; h < 2; ++h)  // this CTA's 64 keys of the block, two 64-dim halves
+            tma_load_3d_pair(ks + sk * v2::K_SLOT + h * v2::K_SLOT_HALF, &kmap,
+                             lead_bar(&k_full[sk]), h * 64, j * v2::BKV + (int)rank * v2::HALF,
+                             head);
+          const int sv = j % v2::VS;
+          if (!wait_bar(&v_empty[sv], ((j / v2::VS) & 1) ^ 1, abort_flag, p.err,
+                        DEV_ERR_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          if (leader) bar_arrive_expect_tx(&v_full[sv], 2 * v2::V_SLOT);
+          // this CTA's 64 dims of the block's 128 keys
+          tma_load_3d_pair(vs + sv * v2::V_SLOT, &vmap, lead_bar(&v_full[sv]), (int)rank * 64,
+                           j * v2::BKV, head);
+        }
+        if (!ok) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 1000000ull) {
+          }
+        }
+      }
+      __syncwarp();
+      cluster_sync_all();
+    } else if (warp == WARP_MMA) {
+      if (elect_one()) {
+        if (leader) {
+          constexpr uint32_t idesc_s = make_idesc_f16(2 * v2::BQ, v2::BKV, 0, 0, 0);
+          constexpr uint32_t idesc_o = make_idesc_f16(2 * v2::BQ, HD, 0, 0, 1);  // V MN-major
+          bool ok = wait_bar(q_full, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA);
+          // S(j) = Q K_j^T (N = 128) into S(j & 1); the K stage is released after it.
+          auto issue_s = [&](int j) -> bool {
+            const int sk = j % v2::KS;
+            if (!wait_bar(&k_full[sk], (j / v2::KS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
+              return false;
+            tc_fence_after();
+            const uint32_t q_addr = smem_u32(qs);
+            const uint32_t k_addr = smem_u32(ks + sk * v2::K_SLOT);
+            const uint32_t d = tmem + v2::S_COL + (j & 1) * v2::BKV;
+#pragma unroll
+            for (int k16 = 0; k16 < HD / 16; ++k16) {
+              const uint32_t qo = (k16 >> 2) * v2::Q_HALF + (k16 & 3) * 32;
+              const uint32_t ko = (k16 >> 2) * v2::K_SLOT_HALF + (k16 & 3) * 32;
+              mma_ss_pair(d, make_smem_desc(q_addr + qo, 16, 1024),
+                          make_smem_desc(k_addr + ko, 16, 1024), idesc_s, k16 > 0 ? 1u : 0u);
+            }
+            tc_commit_pair(&s_full[j & 1], 0x3);
+            tc_commit_pair(&k_empty[sk], 0x3);
+            return true;
+          };
+          // O_h += P_h(j) V_h(j): P_h over the first 32 columns of half h of
+          // S(j & 1), V_h = keys [64 h, 64 h + 64) of the V stage; the stage
+          // is released after the second half's product.
+          auto issue_pv = [&](int j, int h) -> bool {
+            const int b = j & 1;
+            if (!wait_bar(&p_ready[h * 2 + b], (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
+              return false;
+            const int sv = j % v2::VS;
+            if (h == 0 &&
+                !wait_bar(&v_full[sv], (j / v2::VS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
+              return false;
+            tc_fence_after();
+            const uint32_t v_addr = smem_u32(vs + sv * v2::V_SLOT) + h * v2::HALF * 128;
+#pragma unroll
+            for (int k16 = 0; k16 < v2::HALF / 16; ++k16) {
+              const uint32_t a = tmem + v2::S_COL + b * v2::BKV + h * v2::HALF + k16 * 8;
+              const uint64_t vd = make_smem_desc(v_addr + k16 * 16 * 128, v2::V_SLOT / 2, 1024);
+              mma_ts_pair(tmem + v2::O_COL + h * HD, a, vd, idesc_o, (j > 0 || k16 > 0) ? 1u : 0u);
+            }
+            tc_commit_pair(&pv_done[h * 2 + b], 0x3);
+            if (h == 1) tc_commit_pair(&v_empty[sv], 0x3);
+            return true;
+          };
+          if (ok) ok = issue_s(0);
+          if (ok && nkv > 1) ok = issue_s(1);
+          for (int j = 0; j < nkv && ok; ++j) {
+            ok = issue_pv(j, 0);
+            if (ok) ok = issue_pv(j, 1);
+            if (ok && j + 2 < nkv) ok = issue_s(j + 2);
+          }
+          tc_commit_pair(drain, 0x3);
+        }
+        // Both CTAs: wait until every MMA has completed (the commit above
+        // arrives on the drain barrier of each CTA).
+        const uint32_t da = smem_u32(drain);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!bar_try_wait(da, 0)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (p.err) atomicCAS(p.err, 0, DEV_ERR_TIMEOUT_MMA);
+            break;
+          }
+        }
+      }
+      __syncwarp();
+      // Every warp of both CTAs ends at this cluster barrier, after its last
+      // MMA, remote arrive and TMEM access.
+      cluster_sync_all();
+      tc_fence_after();
+      tmem_dealloc_pair(tmem, TMEM_COLS);
+    } else {
+      cluster_sync_all();  // warps 10-11
+    }
+  } else {
+    regs_inc<kSoftmaxRegs>();
+    // softmax warps: 0..3 -> keys [0, 64) of every block, 4..7 -> keys [64, 128)
+    const int hf = warp >> 2;
+    const int qd = warp & 3;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t o_addr = tmem + lane_base + v2::O_COL + hf * HD;
+    const int row = qd * 32 + (int)lane;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int buf = j & 1;
+      const uint32_t s_addr = tmem + lane_base + v2::S_COL + buf * v2::BKV + hf * v2::HALF;
+      bool good = wait_bar(&s_full[buf], (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+      if (!__all_sync(0xffffffffu, good)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int kbase = j * v2::BKV + hf * v2::HALF;
+      if (kbase >= p.seq) {
+        // This half of the last block holds no key (seq % 128 <= 64): P = 0,
+        // and the max / sum stay as they are.
+        uint32_t z[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) z[i] = 0u;
+        tmem_st16(s_addr, z);
+        tmem_st16(s_addr + 16, z);
+      } else {
+        float s[v2::HALF];
+        {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(s_addr, r0);
+          tmem_ld32(s_addr + 32, r1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            s[i] = __uint_as_float(r0[i]);
+            s[32 + i] = __uint_as_float(r1[i]);
+          }
+        }
+        if (kbase + v2::HALF > p.seq) {
+#pragma unroll
+          for (int c = 0; c < v2::HALF; ++c)
+            if (kbase + c >= p.seq) s[c] = -INFINITY;
+        }
+        auto row_max = [&]() -> float {
+          float m8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(s[i], s[8 + i]);
+#pragma unroll
+          for (int c = 16; c < v2::HALF; c += 16) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) m8[i] = max3f(m8[i], s[c + i], s[c + 8 + i]);
+          }
+          return max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]),
+                       fmaxf(m8[6], m8[7])) * p.scale_log2;
+        };
+        auto exps = [&](float mref) -> float {
+          unsigned long long rs2[4] = {0ull, 0ull, 0ull, 0ull};
+          const unsigned long long sc2 = pack2(p.scale_log2, p.scale_log2);
+          const unsigned long long nm2 = pack2(-mref, -mref);
+#pragma unroll
+          for (int ch = 0; ch < v2::HALF / 32; ++ch) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int c = ch * 16 + i;
+              const unsigned long long x2 = fma2(pack2(s[2 * c], s[2 * c + 1]), sc2, nm2);
+              float a, b;
+              if ((kPolyPairsPair >> i) & 1) {
+                ex2_poly2(x2, a, b);
+              } else {
+                float x0, x1;
+                unpack2(x2, x0, x1);
+                a = ex2(x0);
+                b = ex2(x1);
+              }
+              rs2[c & 3] = add2(rs2[c & 3], pack2(a, b));
+              pk[i] = cvt_h2(a, b);
+            }
+            tmem_st16(s_addr + ch * 16, pk);
+          }
+          float rsv[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) unpack2(rs2[i], rsv[2 * i], rsv[2 * i + 1]);
+          return ((rsv[0] + rsv[1]) + (rsv[2] + rsv[3])) + ((rsv[4] + rsv[5]) + (rsv[6] + rsv[7]));
+        };
+        float alpha = 1.0f;
+        float rs = 0.0f;
+        auto rescale_step = [&]() -> bool {
+          const float mx = row_max();
+          if (mx > m + kRescaleThreshold) {
+            alpha = ex2(m - mx);
+            m = mx;
+          }
+          if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+            // O_h is rescaled once P_h(j - 1) V_h(j - 1) has completed.
+            const int pb = (j - 1) & 1;
+            bool good2 = wait_bar(&pv_done[hf * 2 + pb], ((j - 1) >> 1) & 1, abort_flag, p.err,
+                                  DEV_ERR_TIMEOUT_SOFTMAX);
+            if (!__all_sync(0xffffffffu, good2)) return false;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld32(o_addr + c * 32, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+              tmem_st32(o_addr + c * 32, r);
+            }
+          }
+          return true;
+        };
+        // Speculative exponentials as in the 64-key pair kernel: from the
+        // second block on, taken against the running max first; a block whose
+        // row sum exceeds 2^15 is redone with its own max.
+        if (j == 0) m = row_max();
+#pragma unroll 1
+        for (int pass = 0; pass < 2; ++pass) {
+          rs = exps(m);
+          if (j == 0 || pass == 1 || !__any_sync(0xffffffffu, !(rs <= kSpeculativeSumLimit)))
+            break;
+          if (!rescale_step()) {
+            ok = false;
+            break;
+          }
+          tmem_wait_st();  // the first pass's P stores land before they are overwritten
+        }
+        if (!ok) break;
+        l = l * alpha + rs;
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive_remote(lead_bar(&p_ready[hf * 2 + buf]));
+    }
+    if (ok) {
+      // Publish this half's (max, sum) per row, then merge both halves.
+      st_m[hf * v2::BQ + row] = m;
+      st_l[hf * v2::BQ + row] = l;
+      bar_arrive(stat_bar);
+      const int lb = (nkv - 1) & 1;
+      const uint32_t lph = ((nkv - 1) >> 1) & 1;
+      const bool good = wait_bar(stat_bar, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX) &&
+                        wait_bar(&pv_done[lb], lph, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX) &&
+                        wait_bar(&pv_done[2 + lb], lph, abort_flag, p.err, DEV_ERR_TIMEOUT_SOFTMAX);
+      if (__all_sync(0xffffffffu, good)) {
+        tc_fence_after();
+        const float ma = st_m[row], mb = st_m[v2::BQ + row];
+        const float mx = fmaxf(ma, mb);
+        const float wa = ex2(ma - mx), wb = ex2(mb - mx);  // 0 for a half that saw no key
+        const float inv_l = 1.0f / (st_l[row] * wa + st_l[v2::BQ + row] * wb);
+        const float ca = wa * inv_l, cb = wb * inv_l;
+        const int q = q0 + row;
+        __half* base = p.out;
+        if (p.routes.n > 0) {
+          int r = 0;
+          while (r + 1 < p.routes.n && q >= p.routes.row_bound[r + 1]) ++r;
+          base = p.routes.outs[r];
+        }
+        // this warp writes dims [64 hf, 64 hf + 64) of its rows
+        __half* dst = base + (size_t)q * p.ld_out + (size_t)head * HD + hf * v2::HALF;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tmem + lane_base + v2::O_COL + hf * v2::HALF + c * 32, ra);
+          tmem_ld32(tmem + lane_base + v2::O_COL + HD + hf * v2::HALF + c * 32, rb);
+          tmem_wait_ld();
+          if (q < p.seq) {
+            uint32_t hv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float x0 = __uint_as_float(ra[2 * i]) * ca + __uint_as_float(rb[2 * i]) * cb;
+              const float x1 =
+                  __uint_as_float(ra[2 * i + 1]) * ca + __uint_as_float(rb[2 * i + 1]) * cb;
+              const __half2 h2 = __floats2half2_rn(x0, x1);
+              hv[i] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(hv[4 * i], hv[4 * i + 1], hv[4 * i + 2], hv[4 * i + 3]);
+          }
+        }
+        if (p.routes.n > 0) __threadfence_system();  // peer stores ordered before the kernel's end
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync_all();
+  }
+}
+
 }  // namespace attn
 
 int encode_tmap_heads(CUtensorMap* map, const void* base, int n_heads, int seq, int head_dim,
@@ -799,14 +1213,29 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
     return fail(-1, "attention: out must be 16-byte aligned with ld_out % 8 == 0 and >= heads*128");
   // BONSAI_ATTN=single selects the one-CTA form (the tests run both); the
   // CTA-pair form is the default where a cluster of two fits (checked once).
+  // Kernel form.  BONSAI_ATTN=single: one CTA per head x 256 queries;
+  // pair (or v1): clusters of two CTAs, 512 queries, 64-key blocks; v2:
+  // clusters of two CTAs, 256 queries, 128-key blocks with two key-half
+  // softmaxes.  Unset: v2 where its smaller work units fill the GPU's waves
+  // enough better to make up for its lower per-SM rate (measured alone:
+  // 1055 / 1242 TFLOP/s for v2 against 1214 / 1356 for the 64-key pair at
+  // L = 4608 / 16896 with 24 heads, 1158 against 1001 with 3 heads at 16896,
+  // the 8-GPU head split's shape), else the 64-key pair.  A forced key split
+  // (BONSAI_ATTN_SPLIT) runs on the 64-key forms.
   const char* form = getenv("BONSAI_ATTN");
   const int pair_slots = attn_pair_slots();
   const bool pair = !(form && std::strcmp(form, "single") == 0) && pair_slots > 0;
-  CUtensorMap qm, km, vm;
-  int rc = encode_tmap_heads(&qm, q, n_heads, seq, head_dim, attn::BQ);
-  if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim, pair ? attn::BKV / 2 : attn::BKV);
-  if (!rc) rc = encode_tmap_heads(&vm, v, n_heads, seq, head_dim, attn::BKV);
-  if (rc) return rc;
+  bool v2form = false;
+  if (pair && form && std::strcmp(form, "v2") == 0) {
+    v2form = true;
+  } else if (pair && !form && !getenv("BONSAI_ATTN_SPLIT")) {
+    constexpr double kV2UnitCost = 0.55;  // a v2 cluster's time per 64-key-pair cluster's
+    const long long u1 = (long long)((seq + 4 * attn::BQ - 1) / (4 * attn::BQ)) * n_heads;
+    const long long u2 = (long long)((seq + 2 * attn::v2::BQ - 1) / (2 * attn::v2::BQ)) * n_heads;
+    const double w1 = (double)((u1 + pair_slots - 1) / pair_slots);
+    const double w2 = kV2UnitCost * (double)((u2 + pair_slots - 1) / pair_slots);
+    v2form = w2 < 0.95 * w1;
+  }
   attn::Params p{};
   p.seq = seq;
   p.n_heads = n_heads;
@@ -815,9 +1244,22 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
   p.ld_out = ld_out;
   if (routes) p.routes = *routes;
   p.err = device_error_word();
+  p.kv_split = 1;
   static bool attr_dev[64] = {};
   bool& attr = attr_dev[device_slot()];
   if (!attr) {
+    {
+      cudaFuncAttributes fa{};
+      cudaError_t e = cudaFuncGetAttributes(&fa, attn::attention_pair128_kernel);
+      if (e != cudaSuccess) return cuda_status(e, "attention function attributes");
+      if (fa.numRegs != attn::kLaunchRegs)
+        return fail(-2, "attention: kernel built with " + std::to_string(fa.numRegs) +
+                            " registers per thread, the register split needs " +
+                            std::to_string(attn::kLaunchRegs));
+      e = cudaFuncSetAttribute(attn::attention_pair128_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, attn::v2::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_status(e, "attention set smem attribute");
+    }
     // setmaxnreg.inc waits until the block's launch allocation can supply
     // the registers: refuse to launch unless the kernel was built with the
     // per-thread count the split above assumes.
@@ -835,6 +1277,29 @@ int launch_attention(const __half* q, const __half* k, const __half* v, int n_he
     }
     attr = true;
   }
+  if (v2form) {
+    CUtensorMap qm, km, vm;
+    int rc = encode_tmap_heads(&qm, q, n_heads, seq, head_dim, attn::v2::BQ);
+    if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim, attn::v2::HALF);
+    if (!rc) rc = encode_tmap_heads(&vm, v, n_heads, seq, head_dim, attn::v2::BKV);
+    if (rc) return rc;
+    ProfScope prof("attention", 4.0 * (double)seq * seq * head_dim * n_heads,
+                   4.0 * (double)seq * n_heads * head_dim * 2, st);
+    cudaLaunchAttribute attr_c[1];
+    cudaLaunchConfig_t cfg = attn_pair_config(attr_c);
+    cfg.gridDim = dim3(2 * (unsigned)((seq + 2 * attn::v2::BQ - 1) / (2 * attn::v2::BQ)),
+                       (unsigned)n_heads);
+    cfg.dynamicSmemBytes = attn::v2::SMEM_BYTES;
+    cfg.stream = st;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, attn::attention_pair128_kernel, qm, km, vm, p);
+    if (e != cudaSuccess) return cuda_status(e, "attention pair128 launch");
+    return launch_status("attention pair128 launch");
+  }
+  CUtensorMap qm, km, vm;
+  int rc = encode_tmap_heads(&qm, q, n_heads, seq, head_dim, attn::BQ);
+  if (!rc) rc = encode_tmap_heads(&km, k, n_heads, seq, head_dim, pair ? attn::BKV / 2 : attn::BKV);
+  if (!rc) rc = encode_tmap_heads(&vm, v, n_heads, seq, head_dim, attn::BKV);
+  if (rc) return rc;
   // work units of the unsplit launch and the key split
   const int nkv = (seq + attn::BKV - 1) / attn::BKV;
   const long long qblocks = pair ? (seq + 4 * attn::BQ - 1) / (4 * attn::BQ)

@@ -29,10 +29,11 @@ def _assert_block_tol(got, ref, what):
     assert c >= 0.9999 and err <= 1e-2 * rms, f"{what}: cos={c:.6f} maxabs={err:.3e} rms={rms:.3e}"
 
 
-@pytest.fixture(params=["pair", "single"])
+@pytest.fixture(params=["pair", "single", "v2"])
 def attn_form(request, monkeypatch):
-    """Both forms of the attention kernel: CTA pair (the default) and one CTA
-    (BONSAI_ATTN=single)."""
+    """Every form of the attention kernel: CTA pair (the default), one CTA
+    (BONSAI_ATTN=single), and the CTA pair with 128-key blocks and two
+    key-half softmaxes (BONSAI_ATTN=v2)."""
     monkeypatch.setenv("BONSAI_ATTN", request.param)
     return request.param
 

@@ -97,7 +97,7 @@ def test_flux1_block_at_step_sequence(gpu, kind):
     _check(got, ref, f"flux1 {kind} block at L=4608 (reference b1 kernel={used})")
 
 
-@pytest.fixture(params=["pair", "single"])
+@pytest.fixture(params=["pair", "single", "v2"])
 def attn_form(request, monkeypatch):
     monkeypatch.setenv("BONSAI_ATTN", request.param)
     return request.param
