@@ -216,9 +216,14 @@ int bonsai_ln_modulate_f32(const float* x, int rows, int dim, const float* shift
  * q, k, v: f16 head-major [n_heads][seq][head_dim] (head_dim = 128).
  * out: f16 token-major [seq][ld_out] with head h at columns h*head_dim.
  * scale: softmax scale (the reference uses 1/sqrt(head_dim)).
- * Runs as clusters of two CTAs where they fit; the environment variable
- * BONSAI_ATTN=single selects the one-CTA kernel (results equal within the
- * tolerance, not bit-identical). */
+ * Runs as clusters of two CTAs where they fit: 512 queries per cluster in
+ * 64-key blocks, or, where its smaller work units fill the GPU's waves
+ * better (few heads at long sequences), 256 queries per cluster in 128-key
+ * blocks.  BONSAI_ATTN=pair | v2 | single forces one form (results equal
+ * within the tolerance, not bit-identical); BONSAI_ATTN_SPLIT=n splits each
+ * head's keys into n ranges merged by a second kernel (used by itself only
+ * for launches that fill at most half of the GPU; partials in stream-ordered
+ * scratch). */
 int bonsai_joint_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int n_heads,
                            int seq, int head_dim, float scale, uint16_t* out, long long ld_out,
                            void* stream);
