@@ -7,8 +7,8 @@
 // starts with a magic number that GPU backends match on (:32, :303).  Here
 // those factory functions -- the reference's code, through the ggml shim in
 // oracle/shim -- build the nodes, and a miniature CUDA backend dispatches each
-// node by its magic to bonsai_b1_linear_f32 / bonsai_rope_2d_f32, exactly as
-// INTEGRATION.md's Level 1 binding does.  The same nodes are then run through
+// node by its magic to bonsai_b1_linear_f32 / bonsai_rope_2d_f32, the way a
+// backend that replaces the two custom ops binds them.  The same nodes are then run through
 // their own CPU callbacks (the reference's kernels, every (ith, nth) slice)
 // and the two results compared:
 //   B1_0 linear: cos >= 0.9999 and max-abs <= 1e-2 * RMS (the device rounds
