@@ -594,7 +594,8 @@ def run_bonsai(args):
         "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": round(ms, 3), "higher_is_better": False,
         "scaling": "strong" if split else "weak",
-        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "vs_baseline": None, "dtype": "f16 operands, f32 accumulate and residual",
+        "data": "synthetic",
         "config": step_config(world, split, args.exchange),
         "images_per_s": round((1 if split else world) * 1000.0 / ms, 3),
         "step_tflops": round(step_flops() / (ms / 1e3) / 1e12 * (1 if split else world), 1),
