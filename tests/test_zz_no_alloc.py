@@ -28,9 +28,13 @@ def test_noalloc_matches_allocating_linear_twice(gpu):
         ref = torch.empty(T, N, device="cuda")
         got = torch.full((T, N), float("nan"), device="cuda")
         bb.b1_linear_f32(act, w, ref)
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
         bb.check(L.bonsai_b1_linear_f32_noalloc(act.data_ptr(), T, w.handle, got.data_ptr(),
                                                 bb.stream_ptr()), "b1_linear_f32_noalloc")
         torch.cuda.synchronize()
+        if i > 0:  # after the first call has loaded the library's kernels on this device
+            assert torch.cuda.mem_get_info()[0] == free_before, "the no-allocation call allocated"
         # same kernels on the same f16-rounded activations: identical up to f32 summation order
         torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-5)
         w.free()
