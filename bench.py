@@ -238,16 +238,19 @@ class CpuSample:
                 f"of the ggml built-ins); scaled to 19 double + 38 single blocks + modulation + edges")
 
 
-def step_config(world: int, split: bool = False, exchange: str = "scatter") -> dict:
+ORDER_DESC = {"flags": "a peer flag barrier per phase for ordering",
+              "nccl": "one-element NCCL all-reduce per phase for ordering"}
+
+
+def step_config(world: int, split: bool = False, exchange: str = "scatter",
+                order: str = "flags") -> dict:
     """The bench line's `config`, identical in both arms for the same N."""
     if split:
         par = {"fused": f"head/row split over {world} GPUs, exchanges fused into the producing "
-                        "kernels over peer memory (CUDA IPC), one-element all-reduce per phase "
-                        "for ordering",
+                        "kernels over peer memory (CUDA IPC), " + ORDER_DESC[order],
                "scatter": f"head/row split over {world} GPUs, Q/K/V of own rows stored into the "
                           "heads' owners by the GEMM epilogue and attention rows into the rows' "
-                          "owners, over peer memory (CUDA IPC), one-element all-reduce per phase "
-                          "for ordering",
+                          "owners, over peer memory (CUDA IPC), " + ORDER_DESC[order],
                "nccl": f"head/row split over {world} GPUs (NCCL all-gather + all-to-all per "
                        "block)"}[exchange]
     else:
@@ -362,7 +365,8 @@ def measure_split_2048(args, rank: int, world: int, dist) -> dict:
     if world > 1:
         m.set_partition(rank, world)
         if args.exchange in ("fused", "scatter"):
-            headsplit.enable_fused(m, scatter_qkv=args.exchange == "scatter")
+            headsplit.enable_fused(m, scatter_qkv=args.exchange == "scatter",
+                                   flag_barrier=args.order == "flags")
     rng = np.random.default_rng(2048)  # one shared image on every rank
     img_h = torch.from_numpy(rng.standard_normal((img_n, IN_CH)).astype(np.float32)).pin_memory()
     txt_h = torch.from_numpy(rng.standard_normal((TXT, CTX)).astype(np.float32)).pin_memory()
@@ -431,6 +435,7 @@ def measure_split_2048(args, rank: int, world: int, dist) -> dict:
     res = {"n_gpus": world, "ms_per_step": round(ms, 3), "e2e_ms": round(ms_e2e, 3),
            "steps": K, "warmup": W, "img_tokens": img_n, "txt_tokens": TXT,
            "exchange": (args.exchange if world > 1 else "none (one GPU: the plain step)"),
+           "order": (ORDER_DESC[args.order] if world > 1 and args.exchange != "nccl" else None),
            "images_per_s": round(1000.0 / ms, 3),
            "step_tflops": round(step_flops(img_n + TXT, img_n) / (ms / 1e3) / 1e12, 1),
            "phase_ms": phase_ms, "phase_ms_min_rank": phase_ms_min,
@@ -487,7 +492,8 @@ def run_bonsai(args):
         if world > 1:
             model.set_partition(rank, world)
             if args.exchange in ("fused", "scatter"):
-                headsplit.enable_fused(model, scatter_qkv=args.exchange == "scatter")
+                headsplit.enable_fused(model, scatter_qkv=args.exchange == "scatter",
+                                       flag_barrier=args.order == "flags")
 
     rng = np.random.default_rng(1000 + (0 if split else rank))  # split: one shared image
     img_h = torch.from_numpy(rng.standard_normal((IMG, IN_CH)).astype(np.float32)).pin_memory()
@@ -596,7 +602,7 @@ def run_bonsai(args):
         "scaling": "strong" if split else "weak",
         "vs_baseline": None, "dtype": "f16 operands, f32 accumulate and residual",
         "data": "synthetic",
-        "config": step_config(world, split, args.exchange),
+        "config": step_config(world, split, args.exchange, args.order),
         "images_per_s": round((1 if split else world) * 1000.0 / ms, 3),
         "step_tflops": round(step_flops() / (ms / 1e3) / 1e12 * (1 if split else world), 1),
         "roofline": {"bound": "tensor", "kernel": "b1_gemm", "achieved": round(gemm_tf, 1),
@@ -934,6 +940,10 @@ def main():
                          "peer memory (fused: the LN-modulate kernel broadcasts xm rows; scatter: "
                          "the Q/K/V GEMM stores every head into its owner's buffer) or NCCL "
                          "collectives between the phases")
+    ap.add_argument("--order", choices=["flags", "nccl"], default="flags",
+                    help="the fused exchanges' ordering of the ranks after phases 0 and 1: the "
+                         "engine's peer flag barrier (bonsai_dit_barrier) or a one-element NCCL "
+                         "all-reduce")
     ap.add_argument("--no-side", action="store_true",
                     help="skip the 1-GPU side measurements (BASELINE configs 1-3 and the VAE "
                          "decode) that a default 1-GPU run adds to its line")

@@ -86,6 +86,9 @@ SIGNATURES = {
     "bonsai_dit_set_qkv_peers": (_c_int, [_vp, ctypes.POINTER(_vp), _c_int]),
     "bonsai_dit_ipc_handle": (_c_int, [_vp, ctypes.c_char_p, _vp]),
     "bonsai_dit_open_qkv_peers": (_c_int, [_vp, _vp, _c_int]),
+    "bonsai_dit_set_flag_peers": (_c_int, [_vp, ctypes.POINTER(_vp), _c_int]),
+    "bonsai_dit_open_flag_peers": (_c_int, [_vp, _vp, _c_int]),
+    "bonsai_dit_barrier": (_c_int, [_vp, _vp]),
     "bonsai_vae_create": (_c_int, [_c_int, _c_int, ctypes.c_ulonglong, ctypes.POINTER(_vp)]),
     "bonsai_vae_destroy": (_c_int, [_vp]),
     "bonsai_vae_load_safetensors": (_c_int, [_vp, ctypes.c_char_p]),
@@ -421,6 +424,17 @@ class Dit:
         assert len(handles) == 64 * world
         check(lib().bonsai_dit_open_qkv_peers(self.handle, handles, world),
               "bonsai_dit_open_qkv_peers")
+
+    def open_flag_peers(self, handles: bytes, world: int):
+        """Every rank's "flags" IPC handle (world x 64 bytes): enables
+        barrier(); order the ranks once (host barrier) before the first."""
+        assert len(handles) == 64 * world
+        check(lib().bonsai_dit_open_flag_peers(self.handle, handles, world),
+              "bonsai_dit_open_flag_peers")
+
+    def barrier(self, stream=None):
+        """Stream-ordered barrier of the partitioned ranks over peer flags."""
+        check(lib().bonsai_dit_barrier(self.handle, stream_ptr(stream)), "bonsai_dit_barrier")
 
     def ipc_handles(self) -> bytes:
         buf = ctypes.create_string_buffer(128)

@@ -58,24 +58,36 @@ def _all_gather_bytes(data: bytes, world: int, group) -> bytes:
     return bytes(every.cpu().numpy())
 
 
-def enable_fused(model, group=None, scatter_qkv: bool = False) -> None:
+def enable_fused(model, group=None, scatter_qkv: bool = False, flag_barrier: bool = True) -> None:
     """Exchange CUDA IPC handles of every rank's xm / cat and give them to
     the engine (bonsai_dit_open_peers).  scatter_qkv: also every rank's qkv
     (bonsai_dit_open_qkv_peers), so that phase 0's Q/K/V GEMM stores each
     head into its owner's buffer instead of phase 0 broadcasting xm rows.
-    Collective: every rank calls it."""
+    flag_barrier: order the ranks between the phases with the engine's peer
+    flag barrier (bonsai_dit_barrier: one small kernel, stores of a counter
+    into every rank's flags over NVLink) instead of a one-element NCCL
+    all-reduce.  Collective: every rank calls it (one process per GPU)."""
     world = dist.get_world_size(group)
     model.open_peers(_all_gather_bytes(model.ipc_handles(), world, group), world)
     if scatter_qkv:
         model.open_qkv_peers(_all_gather_bytes(model.ipc_handle("qkv"), world, group), world)
+    model.flag_barrier = False
+    if flag_barrier:
+        model.open_flag_peers(_all_gather_bytes(model.ipc_handle("flags"), world, group), world)
+        dist.barrier(group=group)  # every rank's flags are zeroed before the first barrier
+        model.flag_barrier = True
     model.fused_exchange = True
 
 
-def _order(token: torch.Tensor, group) -> None:
+def _order(model, token: torch.Tensor, group) -> None:
     """Stream-ordered barrier: the next kernels on this rank start after every
     rank has finished the kernels it issued before (they wrote into this
-    rank's buffers)."""
-    dist.all_reduce(token, group=group)
+    rank's buffers).  The engine's peer flag barrier where enable_fused set
+    it up, else a one-element NCCL all-reduce."""
+    if getattr(model, "flag_barrier", False):
+        model.barrier()
+    else:
+        dist.all_reduce(token, group=group)
 
 
 class _Span:
@@ -140,7 +152,7 @@ def forward(model, img, txt, pooled, t: float, out, group=None, timers=None,
                 model.phase(kind, i, 0)
             if fused:
                 with _Span(timers, "order"):
-                    _order(token, group)
+                    _order(model, token, group)
             elif world > 1:
                 with _Span(timers, "xm_gather"):
                     gather_rows_inplace(xm, rank, world, group)
@@ -148,7 +160,7 @@ def forward(model, img, txt, pooled, t: float, out, group=None, timers=None,
                 model.phase(kind, i, 1)
             if fused:
                 with _Span(timers, "order"):
-                    _order(token, group)
+                    _order(model, token, group)
             elif world > 1:
                 with _Span(timers, "cat_exchange"):
                     heads_to_rows(cat, H, rank, world, group)

@@ -13,6 +13,7 @@
 // first, so the reference's ggml_concat(h_txt, h_img) (:468) is free.
 #include "../../include/bonsai_cuda.h"
 #include "internal.cuh"
+#include "ptx.cuh"
 
 #include <cmath>
 #include <algorithm>
@@ -119,6 +120,10 @@ struct SingleW {
 using namespace bonsai;
 using namespace bonsai::dit;
 
+// Flag words of the peer barrier: [0, kMaxPeers) arrivals, kFlagEpoch own count.
+constexpr int kFlagWords = 64;
+constexpr int kFlagEpoch = 32;
+
 struct bonsai_dit {
   ~bonsai_dit();
   Cfg c;
@@ -186,6 +191,14 @@ struct bonsai_dit {
   bool qkv_scatter = false;
   __half* peer_qkv[kMaxPeers] = {};
   std::vector<void*> ipc_opened_qkv;
+  // Peer flag barrier (bonsai_dit_set_flag_peers / bonsai_dit_barrier): this
+  // rank's flag words (kFlagWords u32, zeroed: [r] = the last barrier rank r
+  // has reached, [kFlagEpoch] = this rank's own barrier count) and every
+  // rank's as seen from this device.
+  unsigned* flags = nullptr;
+  unsigned* peer_flags[kMaxPeers] = {};
+  bool flag_barrier = false;
+  std::vector<void*> ipc_opened_flags;
   // device copies of caller inputs for the host-buffer entry point
   float *in_img = nullptr, *in_txt = nullptr, *in_pooled = nullptr, *out_buf = nullptr;
 };
@@ -597,6 +610,49 @@ int run_single(bonsai_dit* m, int i, cudaStream_t st) {
 
 }  // namespace
 
+// Stream-ordered barrier of the partitioned ranks over peer memory (one
+// process per GPU).  Lane r < world stores this rank's new barrier count into
+// word [rank] of rank r's flags (a system-scope release store: the kernels
+// issued before it on this stream have completed and ended with a
+// system-scope fence after their peer stores), then waits until word [r] of
+// this rank's own flags has reached the same count (acquire loads of local
+// memory; every rank takes the barriers in the same order, so a rank is at
+// most one barrier ahead and counts only grow).  Kernels after it on the
+// stream therefore see everything the other ranks wrote into this GPU's
+// buffers before their own barrier.  The wait gives up after kWaitLimitNs
+// and records DEV_ERR_TIMEOUT_BARRIER (a rank that never arrives).
+struct FlagPeers {
+  unsigned* f[kMaxPeers];
+};
+__global__ void peer_barrier_kernel(FlagPeers peers, unsigned* __restrict__ own, int rank,
+                                    int world, int* err) {
+  const int lane = threadIdx.x;
+  unsigned e = 0;
+  if (lane == 0) {
+    e = own[kFlagEpoch] + 1;
+    own[kFlagEpoch] = e;
+  }
+  e = __shfl_sync(0xffffffffu, e, 0);
+  if (lane < world) {
+    unsigned* dst = peers.f[0];
+#pragma unroll
+    for (int r = 1; r < kMaxPeers; ++r)  // static indices: the pointers stay in parameter space
+      if (r == lane) dst = peers.f[r];
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(dst + rank), "r"(e) : "memory");
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + lane) : "memory");
+      if ((int)(v - e) >= 0) break;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (err) atomicCAS(err, 0, DEV_ERR_TIMEOUT_BARRIER);
+        break;
+      }
+    }
+  }
+  __syncwarp();
+}
+
 extern "C" {
 
 int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
@@ -751,6 +807,9 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->hidden), (size_t)L * H * 4));
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->xm), (size_t)L * H * 2));
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->qkv), (size_t)3 * c.heads * L * c.hd * 2));
+  // its own allocation, so that its IPC handle maps exactly these words
+  RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->flags), kFlagWords * sizeof(unsigned)));
+  RC(cuda_status(cudaMemset(m->flags, 0, kFlagWords * sizeof(unsigned)), "dit_create: flags"));
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->cat), (size_t)L * C * 2));
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->tmp32), (size_t)c.img * H * 4));
   const long long nmods = c.per_block_mod ? m->mod_rows : 15LL * H;
@@ -811,6 +870,7 @@ bonsai_dit::~bonsai_dit() {
   cudaDeviceSynchronize();
   for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
   for (void* p : ipc_opened_qkv) cudaIpcCloseMemHandle(p);
+  for (void* p : ipc_opened_flags) cudaIpcCloseMemHandle(p);
   if (graph) cudaGraphExecDestroy(graph);
   if (cap_stream) cudaStreamDestroy(cap_stream);
   if (aux) cudaStreamDestroy(aux);
@@ -997,6 +1057,7 @@ int bonsai_dit_set_partition(bonsai_dit_t m, int rank, int world) {
   m->h0 = rank * m->hl;
   m->fused = false;  // peers belong to a partition: set them again after a change
   m->qkv_scatter = false;
+  m->flag_barrier = false;
   if (m->graph) {
     cudaGraphExecDestroy(m->graph);
     m->graph = nullptr;
@@ -1116,6 +1177,62 @@ int bonsai_dit_open_qkv_peers(bonsai_dit_t m, const void* handles, int world) {
   return bonsai_dit_set_qkv_peers(m, qkv, world);
 }
 
+int bonsai_dit_set_flag_peers(bonsai_dit_t m, void* const* flags, int world) {
+  if (!m) return fail(BONSAI_ERR_ARG, "dit_set_flag_peers: null model");
+  if (!flags) {
+    m->flag_barrier = false;
+    return 0;
+  }
+  if (world != m->world || world < 2 || world > kMaxPeers)
+    return fail(BONSAI_ERR_ARG, "dit_set_flag_peers: world must match bonsai_dit_set_partition (2..8)");
+  if (flags[m->rank] != m->flags)
+    return fail(BONSAI_ERR_ARG, "dit_set_flag_peers: entry [rank] must be this model's own flags");
+  for (int r = 0; r < world; ++r) {
+    if (!flags[r] || (reinterpret_cast<uintptr_t>(flags[r]) & 15))
+      return fail(BONSAI_ERR_ARG, "dit_set_flag_peers: null or misaligned buffer");
+    m->peer_flags[r] = static_cast<unsigned*>(flags[r]);
+  }
+  // every rank starts counting from zero (the caller orders the ranks after
+  // this call, before the first barrier)
+  RC(cuda_status(cudaMemset(m->flags, 0, kFlagWords * sizeof(unsigned)), "dit_set_flag_peers: reset"));
+  RC(cuda_status(cudaDeviceSynchronize(), "dit_set_flag_peers: reset"));
+  m->flag_barrier = true;
+  return 0;
+}
+
+int bonsai_dit_open_flag_peers(bonsai_dit_t m, const void* handles, int world) {
+  if (!m || !handles) return fail(BONSAI_ERR_ARG, "dit_open_flag_peers: null argument");
+  if (world != m->world || world < 2 || world > kMaxPeers)
+    return fail(BONSAI_ERR_ARG, "dit_open_flag_peers: world must match bonsai_dit_set_partition (2..8)");
+  for (void* p : m->ipc_opened_flags) cudaIpcCloseMemHandle(p);
+  m->ipc_opened_flags.clear();
+  m->flag_barrier = false;
+  void* flags[kMaxPeers] = {};
+  const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int r = 0; r < world; ++r) {
+    if (r == m->rank) {
+      flags[r] = m->flags;
+      continue;
+    }
+    void* p = nullptr;
+    RC(cuda_status(cudaIpcOpenMemHandle(&p, h[r], cudaIpcMemLazyEnablePeerAccess),
+                   "dit_open_flag_peers: open handle"));
+    m->ipc_opened_flags.push_back(p);
+    flags[r] = p;
+  }
+  return bonsai_dit_set_flag_peers(m, flags, world);
+}
+
+int bonsai_dit_barrier(bonsai_dit_t m, void* stream) {
+  if (!m) return fail(BONSAI_ERR_ARG, "dit_barrier: null model");
+  if (!m->flag_barrier) return fail(BONSAI_ERR_ARG, "dit_barrier: set the flag peers first");
+  FlagPeers fp{};
+  for (int r = 0; r < m->world; ++r) fp.f[r] = m->peer_flags[r];
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fp, m->flags, m->rank,
+                                                                       m->world, device_error_word());
+  return launch_status("peer_barrier_kernel launch");
+}
+
 int bonsai_dit_buffer(bonsai_dit_t m, const char* name, void** ptr, long long* bytes) {
   if (!m || !name || !ptr) return fail(BONSAI_ERR_ARG, "dit_buffer: null argument");
   const Cfg& c = m->c;
@@ -1125,6 +1242,7 @@ int bonsai_dit_buffer(bonsai_dit_t m, const char* name, void** ptr, long long* b
   else if (n == "xm") { *ptr = m->xm; b = (long long)c.L * c.H * 2; }
   else if (n == "cat") { *ptr = m->cat; b = (long long)c.L * c.C() * 2; }
   else if (n == "qkv") { *ptr = m->qkv; b = 3LL * c.heads * c.L * c.hd * 2; }
+  else if (n == "flags") { *ptr = m->flags; b = kFlagWords * (long long)sizeof(unsigned); }
   else return fail(BONSAI_ERR_ARG, "dit_buffer: unknown buffer " + n);
   if (bytes) *bytes = b;
   return 0;

@@ -20,6 +20,7 @@ enum : int {
   DEV_ERR_TIMEOUT_PRODUCER = 3,
   DEV_ERR_TIMEOUT_EPILOGUE = 4,
   DEV_ERR_TIMEOUT_SOFTMAX = 5,
+  DEV_ERR_TIMEOUT_BARRIER = 6,  // a rank never reached a peer flag barrier
 };
 
 // A wait that has not completed within this many nanoseconds is treated as

@@ -340,9 +340,31 @@ int bonsai_dit_open_peers(bonsai_dit_t m, const void* handles, int world);
  * unchanged.  NULL switches back to the xm broadcast;
  * bonsai_dit_set_partition and bonsai_dit_set_peers(NULL) do too. */
 int bonsai_dit_set_qkv_peers(bonsai_dit_t m, void* const* qkv, int world);
-/* CUDA IPC handle (64 bytes) of one engine buffer: "hidden", "xm", "cat" or
- * "qkv" (bonsai_dit_buffer's names). */
+/* CUDA IPC handle (64 bytes) of one engine buffer: "hidden", "xm", "cat",
+ * "qkv" or "flags" (bonsai_dit_buffer's names). */
 int bonsai_dit_ipc_handle(bonsai_dit_t m, const char* name, void* out);
+/* Peer flag barrier: the stream-ordered ordering of the ranks after phases 0
+ * and 1 of the fused exchanges, without a collective library.  flags: every
+ * rank's "flags" buffer (64 u32, allocated with the model) as a device
+ * pointer valid on this GPU, entry [rank] = its own.  The call zeroes this
+ * rank's flags and synchronises the device; the caller must then order the
+ * ranks once (e.g. a host barrier) before any rank calls bonsai_dit_barrier.
+ * NULL switches it off; bonsai_dit_set_partition does too. */
+int bonsai_dit_set_flag_peers(bonsai_dit_t m, void* const* flags, int world);
+/* Open the "flags" IPC handles of all ranks (world x 64 bytes, rank-major,
+ * this rank's own entry ignored) and call bonsai_dit_set_flag_peers; the
+ * mappings are closed by the next call or bonsai_dit_destroy. */
+int bonsai_dit_open_flag_peers(bonsai_dit_t m, const void* handles, int world);
+/* Enqueue the barrier on stream: one 32-thread kernel that stores this
+ * rank's barrier count into every rank's flags (system-scope release) and
+ * waits, on its own GPU's memory, until every rank has stored the same
+ * count.  Work enqueued after it sees everything the other ranks wrote into
+ * this GPU's buffers before their barrier.  Every rank must call it the same
+ * number of times, one process per GPU (ranks that share a GPU cannot use
+ * it: their barrier kernels would wait on one another).  A rank that never
+ * arrives makes the wait give up after 2 s with DEV_ERR_TIMEOUT_BARRIER
+ * (bonsai_device_error).  The reference has no multi-device path. */
+int bonsai_dit_barrier(bonsai_dit_t m, void* stream);
 /* Open every rank's "qkv" handle (world x 64 bytes, rank-major, this rank's
  * own entry ignored) and pass them to bonsai_dit_set_qkv_peers; the mappings
  * are closed by the next call or bonsai_dit_destroy. */

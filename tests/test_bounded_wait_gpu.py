@@ -52,3 +52,37 @@ def test_gemm_wait_timeout_is_reported_and_the_context_recovers(gpu):
         assert err < 1e-4, err
     finally:
         w.free()
+
+
+def test_peer_barrier_timeout_is_reported_and_the_context_recovers(gpu):
+    """The peer flag barrier of the split step (bonsai_dit_barrier) waits for
+    every rank's store into this GPU's flags.  Here the model is partitioned
+    as rank 0 of 2 and "rank 1's flags" is a plain device buffer: rank 1 never
+    runs, nothing sets its arrival word, and the wait gives up after its 2 s
+    limit with DEV_ERR_TIMEOUT_BARRIER (6).  The barrier's own store into the
+    stand-in buffer is checked, and the context stays usable."""
+    import ctypes
+    import torch
+    L = bb.lib()
+    assert bb.device_error() == 0
+    m = bb.Dit(bb.PRESET_FLUX1, 64, 32, 8, 8, depth=1, depth_single=1, seed=5)
+    try:
+        m.set_partition(0, 2)
+        own = m.buffer("flags", torch.int32, (64,))
+        fake_peer = torch.zeros(64, dtype=torch.int32, device="cuda")
+        ptrs = (ctypes.c_void_p * 2)(own.data_ptr(), fake_peer.data_ptr())
+        bb.check(L.bonsai_dit_set_flag_peers(m.handle, ptrs, 2), "set_flag_peers")
+        m.barrier()
+        code = bb.device_error()          # synchronises; reads and clears
+        assert code == 6, code
+        assert bb.device_error() == 0
+        assert fake_peer[0].item() == 1   # this rank's arrival at barrier 1 reached the "peer"
+        assert own[0].item() == 1 and own[32].item() == 1  # own arrival word and barrier count
+        # the context is intact: a GPU op after the timed-out wait is correct
+        x = torch.arange(1024, device="cuda", dtype=torch.float32)
+        assert float((x * 2).sum().item()) == 2.0 * 1023 * 1024 / 2
+        # and the barrier is refused until peers are set again
+        bb.check(L.bonsai_dit_set_flag_peers(m.handle, None, 0), "set_flag_peers off")
+        assert L.bonsai_dit_barrier(m.handle, bb.stream_ptr()) != 0
+    finally:
+        m.close()

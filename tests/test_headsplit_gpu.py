@@ -6,7 +6,8 @@ unpartitioned bonsai_dit_forward of an identical model.  Both exchange forms
 run: NCCL collectives between the phases, the fused form in which the
 kernels store into the other GPU's buffers through CUDA IPC mappings
 (headsplit.enable_fused), and its QKV scatter variant (phase 0's Q/K/V GEMM
-stores every head into its owner's buffer).  Needs >= 2 GPUs (skipped otherwise).
+stores every head into its owner's buffer); the fused forms order the ranks
+with the engine's peer flag barrier, and once with a NCCL all-reduce.  Needs >= 2 GPUs (skipped otherwise).
 """
 import os
 import socket
@@ -29,7 +30,7 @@ SMALL = dict(img=256, txt=64, grid=16, depth=2, single=2)
 FULL = dict(img=16384, txt=512, grid=128, depth=19, single=38)
 
 
-def _worker(rank, world, port, q, shape, fused, scatter=False):
+def _worker(rank, world, port, q, shape, fused, scatter=False, flags=True):
     import datetime
     import sys
     from pathlib import Path
@@ -51,7 +52,7 @@ def _worker(rank, world, port, q, shape, fused, scatter=False):
                    depth_single=c["single"], seed=11)
         m.set_partition(rank, world)
         if fused:
-            headsplit.enable_fused(m, scatter_qkv=scatter)
+            headsplit.enable_fused(m, scatter_qkv=scatter, flag_barrier=flags)
         rng = np.random.default_rng(3)
         img = torch.from_numpy(rng.standard_normal((m.img, m.in_ch)).astype(np.float32)).cuda()
         txt = torch.from_numpy(rng.standard_normal((m.txt, m.ctx_dim)).astype(np.float32)).cuda()
@@ -78,10 +79,12 @@ def _worker(rank, world, port, q, shape, fused, scatter=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fused,scatter", [(False, False), (True, False), (True, True)],
-                         ids=["nccl", "fused", "fused_qkv_scatter"])
+@pytest.mark.parametrize("fused,scatter,flags",
+                         [(False, False, False), (True, False, True), (True, True, True),
+                          (True, True, False)],
+                         ids=["nccl", "fused", "fused_qkv_scatter", "fused_qkv_scatter_nccl_order"])
 @pytest.mark.parametrize("shape", [SMALL, FULL], ids=["small", "2048sq_full_depth"])
-def test_headsplit_two_gpus_matches_single(shape, fused, scatter):
+def test_headsplit_two_gpus_matches_single(shape, fused, scatter, flags):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -89,7 +92,7 @@ def test_headsplit_two_gpus_matches_single(shape, fused, scatter):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, shape, fused, scatter))
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, shape, fused, scatter, flags))
              for r in range(2)]
     for p in procs:
         p.start()
