@@ -313,8 +313,9 @@ int bonsai_dit_set_partition(bonsai_dit_t m, int rank, int world);
  * stores its LN-modulated rows into every rank's xm, and phase 1's attention
  * stores each output row into its owner's cat (this rank's head columns):
  * the caller drops the all-gather and the all-to-all and only has to order
- * the ranks after phases 0 and 1 (a stream-ordered barrier, e.g. a one-element
- * NCCL all-reduce), because a rank writes into the others' buffers.  Both
+ * the ranks after phases 0 and 1 (a stream-ordered barrier: bonsai_dit_barrier,
+ * or e.g. a one-element NCCL all-reduce), because a rank writes into the
+ * others' buffers.  Both
  * kernels end with a system-scope fence after their peer stores.  NULL
  * pointers switch back to caller-side exchanges; bonsai_dit_set_partition
  * does too. */
