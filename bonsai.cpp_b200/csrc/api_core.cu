@@ -406,6 +406,9 @@ int bonsai_b1_linear_f32(const float* act, int tokens, bonsai_b1_t h, float* out
                                     std::to_string(w.device) + ", the current device is " +
                                     std::to_string(dev));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // One token: the memory-bound matrix-vector kernel on the f32 activations
+  // (a tensor-core tile would be almost all padding); no scratch.
+  if (tokens == 1 && b1_gemv_supported(w)) return launch_b1_gemv_f32(act, w, out, st);
   // f16 copy of the activations; K is padded to a multiple of 8 so that
   // the TMA row pitch is 16-byte aligned (K % 32 == 0 already guarantees it).
   const long long n = (long long)tokens * w.k_in;

@@ -847,6 +847,67 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
+// ------------------------------------------------------------------------
+// B1_0 GEMV: y[n] = sum_k W[n][k] x[k] for ONE activation row, on the
+// chunked device layout.  A matrix-vector product has no reuse for the
+// tensor cores (a 128-token GEMM tile would be 127/128 padding); it is bound
+// by streaming the 6 bytes per 32 weights from HBM.  Each CTA first builds,
+// in shared memory, a table of signed partial sums of x: for every 32-input
+// group, every 4-bit nibble of its sign word (pair-split order: bit j is
+// input 2j, bit j + 16 input 2j + 1) and every value v of that nibble, the
+// sum over the nibble's four inputs of (bit ? +x : -x).  A row's group sum
+// is then eight table lookups, scaled by the group's f16 scale, which is
+// the reference's sum_i (bit ? +x_i : -x_i) * scale (src/b1_0_kernel.h:
+// 240-287) with x in f32.  Thread r of each 128-thread half handles row r of
+// one 128-row tile; a tile's sign words and scales are read coalesced
+// (128 consecutive u32 per array).  The 16 entries of one nibble's table are
+// consecutive floats, so a warp's lookups into one table hit 16 distinct
+// banks: no conflicts.
+constexpr int kGemvThreads = 256;
+constexpr int kGemvMaxKBlocks = 128;  // table = k_blocks KB of shared memory (K <= 8192)
+
+__global__ void __launch_bounds__(kGemvThreads) b1_gemv_kernel(
+    const float* __restrict__ x, const uint32_t* __restrict__ chunks, int n_rows, int k_in,
+    int n_ftiles, int k_blocks, float* __restrict__ y) {
+  extern __shared__ float lut[];  // [k_blocks][2 groups][8 nibbles][16 values]
+  const int entries = k_blocks * 256;
+  for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+    const int v = e & 15, nib = (e >> 4) & 7, g = (e >> 7) & 1, kb = e >> 8;
+    const int base = kb * 64 + g * 32 + (nib < 4 ? 8 * nib : 8 * (nib - 4) + 1);
+    float sum = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int k = base + 2 * t;
+      const float xv = k < k_in ? x[k] : 0.f;
+      sum += ((v >> t) & 1) ? xv : -xv;
+    }
+    lut[e] = sum;
+  }
+  __syncthreads();
+  const int r = threadIdx.x & 127;
+  for (int ft = blockIdx.x * 2 + (threadIdx.x >> 7); ft < n_ftiles; ft += gridDim.x * 2) {
+    const uint32_t* c = chunks + (size_t)ft * k_blocks * kChunkWords;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int kb = 0; kb < k_blocks; ++kb) {
+      const uint32_t* ck = c + (size_t)kb * kChunkWords;
+      const uint32_t w0 = __ldcs(ck + r), w1 = __ldcs(ck + 128 + r), sc = __ldcs(ck + 256 + r);
+      const float* l0 = lut + kb * 256;
+      const float* l1 = l0 + 128;
+      float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+      for (int nib = 0; nib < 8; ++nib) {
+        p0 += l0[nib * 16 + ((w0 >> (4 * nib)) & 15)];
+        p1 += l1[nib * 16 + ((w1 >> (4 * nib)) & 15)];
+      }
+      acc = fmaf(__half2float(__ushort_as_half((unsigned short)(sc & 0xffffu))), p0, acc);
+      acc = fmaf(__half2float(__ushort_as_half((unsigned short)(sc >> 16))), p1, acc);
+    }
+    const int n = ft * 128 + r;
+    if (n < n_rows) y[n] = acc;
+  }
+}
+
 }  // namespace gemm
 
 // 2-D row-major [rows][cols] 16-bit tensor, box {box_cols, box_rows}, 128B swizzle.
@@ -956,6 +1017,35 @@ int launch_b1_unretile(const B1Weight& w, uint8_t* dev_packed, cudaStream_t st) 
 
 // Set by bonsai_debug_stall_next_gemm, consumed by the next launch on the thread.
 thread_local bool g_stall_next_gemm = false;
+
+bool b1_gemv_supported(const B1Weight& w) {
+  return w.swiglu_from < 0 && w.k_blocks >= 1 && w.k_blocks <= gemm::kGemvMaxKBlocks;
+}
+
+int launch_b1_gemv_f32(const float* x, const B1Weight& w, float* y, cudaStream_t st) {
+  if (!x || !y || !w.chunks) return fail(-1, "b1_gemv: null argument");
+  if (!b1_gemv_supported(w))
+    return fail(-2, "b1_gemv: needs in_dim <= 8192 and a weight without the SwiGLU interleave");
+  const int smem = w.k_blocks * 256 * (int)sizeof(float);
+  static bool attr_dev[64] = {};
+  bool& attr = attr_dev[device_slot()];
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(gemm::b1_gemv_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               gemm::kGemvMaxKBlocks * 256 * (int)sizeof(float));
+    if (e != cudaSuccess) return cuda_status(e, "b1_gemv set smem attribute");
+    attr = true;
+  }
+  // enough CTAs to keep the weight stream in flight on every SM; each builds
+  // its own table once and then walks tiles
+  const int tile_pairs = (w.n_ftiles + 1) / 2;
+  const int grid = std::max(1, std::min(tile_pairs, num_sms() * 4));
+  ProfScope prof("b1_gemv", 2.0 * w.n_rows * (double)w.k_in,
+                 (double)w.k_in * 4 + (double)w.n_rows * w.k_in * 6 / 32 + w.n_rows * 4.0, st);
+  gemm::b1_gemv_kernel<<<grid, gemm::kGemvThreads, smem, st>>>(x, w.chunks, w.n_rows, w.k_in,
+                                                                w.n_ftiles, w.k_blocks, y);
+  return launch_status("b1_gemv_kernel launch");
+}
 
 int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, const EpiSeg* segs,
                    int nseg, bool x_bf16, cudaStream_t st, const TileSel* sel) {

@@ -346,7 +346,11 @@ const float* single_mods(bonsai_dit* m, int i) {
 int compute_mods(bonsai_dit* m, cudaStream_t st) {
   const Cfg& c = m->c;
   RC(launch_silu_f32(m->vec, c.H, m->vec_silu, st));
-  if (c.per_block_mod) {
+  if (c.per_block_mod && b1_gemv_supported(m->mod_all)) {
+    // every block's modulation linear at once: one row of silu(vec), so the
+    // memory-bound B1_0 matrix-vector kernel (f32 activations)
+    RC(launch_b1_gemv_f32(m->vec_silu, m->mod_all, m->mods, st));
+  } else if (c.per_block_mod) {
     RC(launch_f32_to_f16(m->vec_silu, m->vec_silu16, c.H, st));
     EpiSeg s = seg_of(EPI_F32, 0, (int)m->mod_rows, m->mods, m->mod_rows, 0, nullptr);
     RC(launch_b1_gemm(m->vec_silu16, c.H, 1, m->mod_all, &s, 1, false, st));

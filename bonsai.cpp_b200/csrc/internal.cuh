@@ -106,6 +106,12 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w,
                    const EpiSeg* segs, int nseg, bool x_bf16, cudaStream_t st,
                    const TileSel* sel = nullptr);
 
+// B1_0 matrix-vector product for one f32 activation row: y[n] = sum_k
+// W[n][k] x[k] (f32 x and accumulation), memory-bound, no tensor cores.
+// Supported for in_dim <= 8192 and weights without the SwiGLU interleave.
+bool b1_gemv_supported(const B1Weight& w);
+int launch_b1_gemv_f32(const float* x, const B1Weight& w, float* y, cudaStream_t st);
+
 // Retile packed reference bytes (device copy) into the chunked layout.
 int launch_b1_retile(const uint8_t* dev_packed, B1Weight& w, cudaStream_t st);
 // Inverse of launch_b1_retile: device chunks of w back to the packed

@@ -121,7 +121,9 @@ int bonsai_b1_shape(bonsai_b1_t w, int* out_dim, int* in_dim);
  *   out[t][r] = sum_blk scale[r][blk] * sum_i (bit ? +act : -act)
  * act: f32 [tokens][in_dim]; out: f32 [tokens][out_dim].
  * The activations are rounded to f16 for the tensor cores (f32
- * accumulation).  The f16 copy of act lives in a scratch buffer the library
+ * accumulation); a single token (tokens == 1, in_dim <= 8192) instead runs
+ * a memory-bound matrix-vector kernel on the f32 activations, with no
+ * scratch.  The f16 copy of act lives in a scratch buffer the library
  * keeps per (calling thread, device, stream), grown on demand with
  * cudaMallocAsync on that stream and released by bonsai_shutdown: calls on
  * different streams never share a buffer, so they may overlap on the GPU.

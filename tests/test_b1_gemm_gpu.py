@@ -59,13 +59,39 @@ def test_b1_linear_f32_small(gpu, kernel, M, K, N):
     torch.cuda.synchronize()
     got = out.cpu().numpy().astype(np.float64)
     wd = bb.dequant_b1(packed, N, K).astype(np.float64)
-    x16 = x.astype(np.float16).astype(np.float64)
-    exact16 = x16 @ wd.T
-    rms = np.sqrt(np.mean(exact16 ** 2)) + 1e-30
-    assert np.max(np.abs(got - exact16)) <= 1e-4 * rms + 1e-6
     ref32 = x.astype(np.float64) @ wd.T
+    if M == 1:  # one token: the f32 matrix-vector kernel (no f16 rounding of x)
+        assert np.max(np.abs(got - ref32)) <= 1e-5 * np.sqrt(np.mean(ref32 ** 2)) + 1e-7
+    else:
+        x16 = x.astype(np.float16).astype(np.float64)
+        exact16 = x16 @ wd.T
+        rms = np.sqrt(np.mean(exact16 ** 2)) + 1e-30
+        assert np.max(np.abs(got - exact16)) <= 1e-4 * rms + 1e-6
     assert _cos(got, ref32) >= 0.9999
     assert np.max(np.abs(got - ref32)) <= 1e-2 * np.sqrt(np.mean(ref32 ** 2))
+
+
+@pytest.mark.parametrize("K,N", [(32, 1), (96, 200), (3072, 3072), (3072, 9000), (8192, 300),
+                                 (8224, 130)])
+def test_b1_linear_f32_one_token(gpu, K, N):
+    """A single token takes the B1_0 matrix-vector kernel (f32 activations,
+    sign-sum tables; in_dim <= 8192) -- the engine's stacked per-block
+    modulation linear is this shape with N = 1,050,624 -- and beyond 8192
+    inputs the tensor-core GEMM (f16 activations)."""
+    import torch
+    packed, x = _case(1, K, N, 77 + K + N)
+    w = bb.B1Weight(packed, N, K)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.full((1, N), float("nan"), device="cuda", dtype=torch.float32)
+    bb.b1_linear_f32(xd, w, out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    wd = bb.dequant_b1(packed, N, K).astype(np.float64)
+    xr = x.astype(np.float64) if K <= 8192 else x.astype(np.float16).astype(np.float64)
+    ref = xr @ wd.T
+    tol = 1e-5 if K <= 8192 else 1e-4
+    assert np.max(np.abs(got - ref)) <= tol * np.sqrt(np.mean(ref ** 2)) + 1e-7
+    w.free()
 
 
 def test_b1_zero_tokens_is_noop(gpu, kernel):
