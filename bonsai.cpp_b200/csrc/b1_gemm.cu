@@ -440,7 +440,11 @@ struct Params {
   int tokens;
   int n_ttiles, k_blocks;
   int npf;          // weight-tile pairs: selected tiles 2i and 2i+1
-  int num_tiles;    // npf * n_ttiles
+  int num_tiles;    // npf * n_ttiles * ksplit
+  // K split: tile index = (ttile * npf + pf) * ksplit + ks; part ks covers
+  // k-blocks [ks * kchunk, min(k_blocks, (ks + 1) * kchunk)).  ksplit > 1
+  // only with gate-residual segments, whose epilogues then add atomically.
+  int ksplit, kchunk;
   int nf, fcount, fgroups;
   int fbase[kMaxTileGroups];
   const uint32_t* chunks;
@@ -506,12 +510,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = cid; tile < p.num_tiles && ok; tile += ncl) {
-        const int ttile = tile / p.npf;
-        const int pf = tile - ttile * p.npf;
+        const int t2 = tile / p.ksplit;
+        const int kb0 = (tile - t2 * p.ksplit) * p.kchunk;
+        const int kb1 = min(k_blocks, kb0 + p.kchunk);
+        const int ttile = t2 / p.npf;
+        const int pf = t2 - ttile * p.npf;
         const int fidx = min(2 * pf + (int)rank, p.nf - 1);
         const int ftile = sel_ftile(fidx, p.fcount, p.fbase);
         const uint32_t* wsrc = p.chunks + (size_t)ftile * k_blocks * kChunkWords;
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!wait_bar(&empty[s], ph ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
@@ -547,7 +554,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t d_tmem = tmem + b * BN;
-          for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int kb0 = (tile % p.ksplit) * p.kchunk;
+          const int kb1 = min(k_blocks, kb0 + p.kchunk);
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s = it % STAGES;
             const uint32_t ph = (it / STAGES) & 1;
             if (!wait_bar(&full[s], ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA)) {
@@ -561,7 +570,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int k16 = 0; k16 < BK / 16; ++k16) {
               const uint64_t adesc = make_smem_desc(aaddr + k16 * 32, 16, 1024);
               const uint64_t bdesc = make_smem_desc(xaddr + k16 * 32, 16, 1024);
-              mma_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k16) != 0 ? 1u : 0u);
+              mma_ss_pair(d_tmem, adesc, bdesc, idesc, (kb != kb0 || k16 != 0) ? 1u : 0u);
             }
             tc_commit_pair(&empty[s], 0x3);
           }
@@ -591,7 +600,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t it = 0;
     bool ok = true;
     for (int tile = cid; tile < p.num_tiles && ok; tile += ncl) {
-      for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+      const int kb0 = (tile % p.ksplit) * p.kchunk;
+      const int kb1 = min(k_blocks, kb0 + p.kchunk);
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
         if (it % EXP_PER_G != slot) continue;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -626,8 +637,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t dempty0 = mapa_shared(smem_u32(&dempty[0]), 0);
     uint32_t lt = 0;
     for (int tile = cid; tile < p.num_tiles; tile += ncl, ++lt) {
-      const int ttile = tile / p.npf;
-      const int pf = tile - ttile * p.npf;
+      const int t2 = tile / p.ksplit;
+      const int ttile = t2 / p.npf;
+      const int pf = t2 - ttile * p.npf;
       const int fidx = 2 * pf + (int)rank;
       const uint32_t b = lt & 1;
       const uint32_t dph = (lt >> 1) & 1;
@@ -702,6 +714,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (j < nt) dst[j * stride] = __float2half_rn(gelu_tanh(__uint_as_float(v[j])));
+        } else if (mode == EPI_RESID_F32 && p.ksplit > 1) {
+          // this K part's share of h += gate * acc; the other part adds its own
+          float* dst = reinterpret_cast<float*>(sg.dst) + base + (size_t)t0 * stride;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nt) atomicAdd(dst + (size_t)j * stride, gate * __uint_as_float(v[j]));
         } else if (mode == EPI_RESID_F32) {
           float* dst = reinterpret_cast<float*>(sg.dst) + base + (size_t)t0 * stride;
 #pragma unroll
@@ -1090,6 +1108,27 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
   const long long tiles1 = (long long)nf * n_tt1;
   const long long tiles2 = (long long)((nf + 1) / 2) * n_tt2;
   constexpr double kPairTileCost = 1.63;
+  // K split of the pair kernel: only for launches whose every segment is a
+  // gate-residual that allows it (split_ok: the partitioned multi-GPU step),
+  // where doubling the work units fills the last wave of clusters better
+  // (e.g. 108 tiles on 74 clusters: 2 waves of whole tiles, 3 of half
+  // tiles); BONSAI_B1_SPLITK=n forces n parts on any gate-residual launch
+  // (tests).
+  bool all_resid = true, all_split_ok = true;
+  for (int i = 0; i < nseg; ++i) {
+    all_resid = all_resid && segs[i].mode == EPI_RESID_F32;
+    all_split_ok = all_split_ok && segs[i].mode == EPI_RESID_F32 && segs[i].split_ok;
+  }
+  int ksplit = 1;
+  if (const char* e = getenv("BONSAI_B1_SPLITK")) {
+    if (all_resid) ksplit = std::max(1, std::min(atoi(e), std::max(1, w.k_blocks / 2)));
+  } else if (all_split_ok && w.k_blocks >= 16 && slots >= 1 && tiles2 >= slots) {
+    // (a launch below one wave -- the 512-token text stream -- keeps whole
+    // tiles: its result then stays bit-identical to the unpartitioned step)
+    const double whole = (double)((tiles2 + slots - 1) / slots);
+    const double half = 0.5 * (double)((2 * tiles2 + slots - 1) / slots);
+    if (half < 0.9 * whole) ksplit = 2;
+  }
   bool use_pair = false;
   const B1Kernel force = forced_kernel();
   const bool stall = g_stall_next_gemm;  // test hook: this launch runs the one-CTA kernel idle
@@ -1101,7 +1140,7 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
     use_pair = true;
   } else if (force == B1Kernel::Auto && slots >= 1) {
     const double t1 = (double)((tiles1 + num_sms() - 1) / num_sms());
-    const double t2 = kPairTileCost * (double)((tiles2 + slots - 1) / slots);
+    const double t2 = kPairTileCost * (double)((tiles2 * ksplit + slots - 1) / slots) / ksplit;
     use_pair = t2 < t1;
   }
 
@@ -1129,7 +1168,9 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
     q.fgroups = fgroups;
     for (int g = 0; g < kMaxTileGroups; ++g) q.fbase[g] = fbase[g];
     q.npf = (nf + 1) / 2;
-    q.num_tiles = (int)tiles2;
+    q.kchunk = (w.k_blocks + ksplit - 1) / ksplit;
+    q.ksplit = (w.k_blocks + q.kchunk - 1) / q.kchunk;  // every part gets >= 1 k-block
+    q.num_tiles = (int)(tiles2 * q.ksplit);
     q.chunks = w.chunks;
     q.nseg = nseg;
     for (int i = 0; i < nseg; ++i) q.seg[i] = segs[i];

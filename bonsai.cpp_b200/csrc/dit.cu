@@ -507,11 +507,13 @@ int double_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
     __half* x = m->xm + (size_t)sp.a * H;
     __half* a = m->cat + (size_t)sp.a * C;
     EpiSeg s = seg_of(EPI_RESID_F32, 0, H, h, H, 0, md + 2 * H);
+    s.split_ok = m->world > 1;
     RC(launch_b1_gemm(a, C, sp.n(), w_out, &s, 1, false, ss));
     RC(launch_ln_modulate_f16(h, sp.n(), H, md + 3 * H, md + 4 * H, 1e-6f, x, H, ss));
     s = seg_of(act_mode, 0, c.mlp_in_rows, a, C, H, nullptr);
     RC(launch_b1_gemm(x, H, sp.n(), w_in, &s, 1, false, ss));
     s = seg_of(EPI_RESID_F32, 0, H, h, H, 0, md + 5 * H);
+    s.split_ok = m->world > 1;
     RC(launch_b1_gemm(a + H, C, sp.n(), w_o2, &s, 1, false, ss));
   }
   return join_aux(m, st);
@@ -552,6 +554,7 @@ int single_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
                               m->cat + (size_t)m->h0 * c.hd, C, st, &rr);
     }
     EpiSeg s = seg_of(EPI_RESID_F32, 0, H, m->hidden + (size_t)m->r0 * H, H, 0, md + 2 * H);
+    s.split_ok = m->world > 1;
     return launch_b1_gemm(m->cat + (size_t)m->r0 * C, C, rows, w.out, &s, 1, false, st);
   }
   if (phase == 0)
@@ -579,6 +582,7 @@ int single_phase(bonsai_dit* m, int i, int phase, cudaStream_t st) {
                     m->cat + (size_t)m->r0 * C, C, H, nullptr);
   RC(launch_b1_gemm(m->xm + (size_t)m->r0 * H, H, rows, w.proj, &s, 1, false, st, &mlp));
   s = seg_of(EPI_RESID_F32, 0, H, m->hidden + (size_t)m->r0 * H, H, 0, md + 2 * H);
+  s.split_ok = m->world > 1;
   return launch_b1_gemm(m->cat + (size_t)m->r0 * C, C, rows, w.out, &s, 1, false, st);
 }
 

@@ -84,6 +84,10 @@ struct EpiSeg {
   // system-scope fence after its stores.
   __half* route[kMaxPeers] = {};
   int route_heads = 0;
+  // EPI_RESID_F32 only: the launcher may split K between two CTA pairs whose
+  // epilogues both add into dst (f32 atomic adds, in no fixed order: the sum
+  // can differ in the last bit from run to run).
+  int split_ok = 0;
 };
 
 constexpr int kMaxSegs = 2;

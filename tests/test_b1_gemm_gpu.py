@@ -160,6 +160,38 @@ def test_b1_gemm_epilogues(gpu, kernel):
     torch.cuda.synchronize()
 
 
+@pytest.mark.parametrize("M,K,N,split", [(300, 1024, 512, 2), (2112, 3072, 3072, 2),
+                                         (77, 96 * 32, 384, 3), (513, 9 * 64, 256, 4)])
+def test_b1_gemm_resid_k_split(gpu, monkeypatch, M, K, N, split):
+    """The two-SM kernel with K split into parts whose gate-residual
+    epilogues add atomically (the partitioned step's residual GEMMs at 8
+    GPUs: M = 2112, K = 3072, N = 3072); forced by BONSAI_B1_SPLITK, ragged
+    token counts and k-block counts that do not divide by the split."""
+    import torch
+    monkeypatch.setenv("BONSAI_B1_KERNEL", "pair")
+    rng = np.random.default_rng(M + K + N)
+    packed = bb.random_b1_packed(N, K, rng)
+    w = bb.B1Weight(packed, N, K)
+    wd = torch.from_numpy(bb.dequant_b1(packed, N, K)).cuda()
+    x16 = torch.randn(M, K, device="cuda").half()
+    ref = x16.float() @ wd.t()
+    h0 = torch.randn(M, N, device="cuda")
+    gate = torch.randn(N, device="cuda")
+    h_whole = h0.clone()
+    bb.b1_gemm(x16, w, bb.BONSAI_EPI_RESID, h_whole, gate=gate)
+    monkeypatch.setenv("BONSAI_B1_SPLITK", str(split))
+    h_split = h0.clone()
+    bb.b1_gemm(x16, w, bb.BONSAI_EPI_RESID, h_split, gate=gate)
+    torch.cuda.synchronize()
+    assert bb.device_error() == 0
+    expect = h0 + gate[None, :] * ref
+    torch.testing.assert_close(h_split, expect, rtol=1e-4, atol=1e-4)
+    # the two parts' f32 partial sums are rounded separately: equal to the
+    # unsplit launch up to f32 accumulation order
+    torch.testing.assert_close(h_split, h_whole, rtol=1e-4, atol=1e-4)
+    w.free()
+
+
 def test_b1_linear_f32_two_streams_interleaved(gpu):
     """The drop-in linear's f16 scratch is per (thread, device, stream): calls
     of growing size issued alternately on two streams from one host thread,
