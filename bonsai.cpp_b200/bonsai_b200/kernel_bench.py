@@ -7,6 +7,7 @@
     python -m bonsai_b200.kernel_bench vae LATENT_H LATENT_W [--reps R]
     python -m bonsai_b200.kernel_bench ln_modulate ROWS [--reps R]
     python -m bonsai_b200.kernel_bench qk_norm_rope L [--heads H] [--reps R]
+    python -m bonsai_b200.kernel_bench gemv N K [--reps R]
 
 gemm: B1_0 GEMM of M tokens x K inputs -> N outputs (f16 store epilogue) on
 seeded random weights/activations; attention: joint attention over L tokens,
@@ -15,7 +16,9 @@ out, bias) on the implicit-GEMM kernel; vae: one whole decode of a
 latent_h x latent_w latent (synthetic weights) with the per-kernel time
 split; ln_modulate: LayerNorm + modulate of f32 [ROWS][3072] into f16
 (bytes ROWS*3072*6); qk_norm_rope: Q/K RMSNorm + RoPE in place on f16
-[H][L][128] (bytes H*L*128*4).  Prints one line: mean time per call over R
+[H][L][128] (bytes H*L*128*4); gemv: the B1_0 matrix-vector kernel on one f32
+row (the step's stacked modulation linear is N = 1050624, K = 3072; bytes
+N*K*6/32 + 4K + 4N).  Prints one line: mean time per call over R
 calls after 3 warm-up calls (CUDA events on the current stream) and the
 TFLOP/s (GB/s for the two HBM-bound kernels).
 """
@@ -80,6 +83,10 @@ def main(argv=None) -> int:
     qk.add_argument("L", type=int)
     qk.add_argument("--heads", type=int, default=48)
     qk.add_argument("--reps", type=int, default=20)
+    gv = sub.add_parser("gemv")
+    gv.add_argument("N", type=int)
+    gv.add_argument("K", type=int)
+    gv.add_argument("--reps", type=int, default=20)
     args = ap.parse_args(argv)
     nbytes = 0.0
 
@@ -155,6 +162,21 @@ def main(argv=None) -> int:
             sn.data_ptr(), bb.stream_ptr()), "bonsai_qk_norm_rope"), args.reps)
         flop, nbytes = 0.0, H * L * 128 * 4.0
         desc = f"qk_norm_rope heads={H} L={L}"
+    elif args.op == "gemv":
+        import numpy as np
+        N, K = args.N, args.K
+        nb = K // 32
+        g = torch.Generator().manual_seed(1)
+        raw = torch.randint(0, 256, (N, nb, 6), dtype=torch.uint8, generator=g)
+        scales = (torch.randn(N, nb, generator=g).abs() * 0.02).half()
+        raw[:, :, 0:2] = scales.view(torch.uint8).view(N, nb, 2)
+        w = bb.B1Weight(raw.reshape(N, nb * 6).numpy(), N, K)
+        del raw, scales
+        x = torch.randn(1, K, device="cuda")
+        y = torch.empty(1, N, device="cuda")
+        ms = _time(lambda: bb.b1_linear_f32(x, w, y), args.reps)
+        flop, nbytes = 2.0 * N * K, N * K * 6.0 / 32 + 4.0 * (K + N)
+        desc = f"gemv N={N} K={K}"
     elif args.op == "vae":
         import json
         v = bb.Vae(args.lh, args.lw, seed=1)

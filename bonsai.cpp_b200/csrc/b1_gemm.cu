@@ -883,6 +883,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 // banks: no conflicts.
 constexpr int kGemvThreads = 256;
 constexpr int kGemvMaxKBlocks = 128;  // table = k_blocks KB of shared memory (K <= 8192)
+constexpr int kGemvBatch = 8;         // k-blocks whose weight words are loaded together
 
 __global__ void __launch_bounds__(kGemvThreads) b1_gemv_kernel(
     const float* __restrict__ x, const uint32_t* __restrict__ chunks, int n_rows, int k_in,
@@ -906,20 +907,33 @@ __global__ void __launch_bounds__(kGemvThreads) b1_gemv_kernel(
   for (int ft = blockIdx.x * 2 + (threadIdx.x >> 7); ft < n_ftiles; ft += gridDim.x * 2) {
     const uint32_t* c = chunks + (size_t)ft * k_blocks * kChunkWords;
     float acc = 0.f;
-#pragma unroll 4
-    for (int kb = 0; kb < k_blocks; ++kb) {
-      const uint32_t* ck = c + (size_t)kb * kChunkWords;
-      const uint32_t w0 = __ldcs(ck + r), w1 = __ldcs(ck + 128 + r), sc = __ldcs(ck + 256 + r);
-      const float* l0 = lut + kb * 256;
-      const float* l1 = l0 + 128;
-      float p0 = 0.f, p1 = 0.f;
+    // kGemvBatch k-blocks' words are loaded before any is used, so that
+    // 3 * kGemvBatch loads per thread are in flight (the kernel is bound by
+    // the latency of this weight stream, not by its bandwidth, otherwise).
+    for (int kb0 = 0; kb0 < k_blocks; kb0 += kGemvBatch) {
+      uint32_t w0[kGemvBatch], w1[kGemvBatch], sc[kGemvBatch];
 #pragma unroll
-      for (int nib = 0; nib < 8; ++nib) {
-        p0 += l0[nib * 16 + ((w0 >> (4 * nib)) & 15)];
-        p1 += l1[nib * 16 + ((w1 >> (4 * nib)) & 15)];
+      for (int u = 0; u < kGemvBatch; ++u) {
+        const uint32_t* ck = c + (size_t)(kb0 + u) * kChunkWords;
+        const bool in = kb0 + u < k_blocks;
+        w0[u] = in ? __ldcs(ck + r) : 0u;
+        w1[u] = in ? __ldcs(ck + 128 + r) : 0u;
+        sc[u] = in ? __ldcs(ck + 256 + r) : 0u;
       }
-      acc = fmaf(__half2float(__ushort_as_half((unsigned short)(sc & 0xffffu))), p0, acc);
-      acc = fmaf(__half2float(__ushort_as_half((unsigned short)(sc >> 16))), p1, acc);
+#pragma unroll
+      for (int u = 0; u < kGemvBatch; ++u) {
+        if (kb0 + u >= k_blocks) break;
+        const float* l0 = lut + (kb0 + u) * 256;
+        const float* l1 = l0 + 128;
+        float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+        for (int nib = 0; nib < 8; ++nib) {
+          p0 += l0[nib * 16 + ((w0[u] >> (4 * nib)) & 15)];
+          p1 += l1[nib * 16 + ((w1[u] >> (4 * nib)) & 15)];
+        }
+        acc = fmaf(__half2float(__ushort_as_half((unsigned short)(sc[u] & 0xffffu))), p0, acc);
+        acc = fmaf(__half2float(__ushort_as_half((unsigned short)(sc[u] >> 16))), p1, acc);
+      }
     }
     const int n = ft * 128 + r;
     if (n < n_rows) y[n] = acc;
