@@ -835,8 +835,15 @@ int bonsai_dit_create(const bonsai_dit_config* cfg, bonsai_dit_t* out) {
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->in_txt), (size_t)std::max(c.txt, 1) * c.ctx_dim * 4));
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->in_pooled), (size_t)std::max(c.pooled, 1) * 4));
   RC(dev_alloc(m.get(), reinterpret_cast<void**>(&m->out_buf), (size_t)c.img * c.in_ch * 4));
-  RC(cuda_status(cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking), "capture stream"));
-  RC(cuda_status(cudaStreamCreateWithFlags(&m->aux, cudaStreamNonBlocking), "aux stream"));
+  // The image-stream chain (captured on cap_stream) outranks the text-stream
+  // chain (aux): the persistent image GEMMs take every SM first and the
+  // 512-token text GEMMs fill the SMs their last, partly filled wave leaves
+  // idle, instead of delaying their start (measured -0.35 ms per step).
+  int prio_least = 0, prio_greatest = 0;
+  RC(cuda_status(cudaDeviceGetStreamPriorityRange(&prio_least, &prio_greatest), "stream priorities"));
+  RC(cuda_status(cudaStreamCreateWithPriority(&m->cap_stream, cudaStreamNonBlocking, prio_greatest),
+                 "capture stream"));
+  RC(cuda_status(cudaStreamCreateWithPriority(&m->aux, cudaStreamNonBlocking, prio_least), "aux stream"));
   RC(cuda_status(cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming), "fork event"));
   RC(cuda_status(cudaEventCreateWithFlags(&m->ev_join, cudaEventDisableTiming), "join event"));
   cudaMemset(m->vec_silu16, 0, (size_t)8 * H * 2);
@@ -990,7 +997,7 @@ int bonsai_dit_forward(bonsai_dit_t m, const float* img, const float* txt, const
       return rc;
     }
     if (e != cudaSuccess) return cuda_status(e, "end capture");
-    e = cudaGraphInstantiate(&m->graph, g, 0);
+    e = cudaGraphInstantiate(&m->graph, g, cudaGraphInstantiateFlagUseNodePriority);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) {
       m->graph = nullptr;
