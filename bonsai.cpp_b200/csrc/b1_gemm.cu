@@ -1141,7 +1141,10 @@ int launch_b1_gemm(const void* x, long long ldx, int tokens, const B1Weight& w, 
     // tiles: its result then stays bit-identical to the unpartitioned step)
     const double whole = (double)((tiles2 + slots - 1) / slots);
     const double half = 0.5 * (double)((2 * tiles2 + slots - 1) / slots);
-    if (half < 0.9 * whole) ksplit = 2;
+    // >= 20% fewer waves (8 GPUs: 2 -> 1.5); a smaller modelled gain (rank
+    // 0's image rows at 4 GPUs: 3 -> 2.5 waves) measured nothing, and whole
+    // tiles keep the result bit-identical to the unpartitioned forward
+    if (half < 0.8 * whole) ksplit = 2;
   }
   bool use_pair = false;
   const B1Kernel force = forced_kernel();
