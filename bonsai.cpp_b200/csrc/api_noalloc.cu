@@ -57,6 +57,18 @@ extern "C" int bonsai_b1_linear_f32_noalloc(const float* act, int tokens, bonsai
   if (tokens == 0) return 0;
   if (!act || !out) return fail(BONSAI_ERR_ARG, "b1_linear_f32_noalloc: null tensor");
   const B1Weight& w = h->w;
+  int cur = 0;
+  cudaError_t ce = cudaGetDevice(&cur);
+  if (ce != cudaSuccess) return cuda_status(ce, "b1_linear_f32_noalloc: cudaGetDevice");
+  // One token: the same f32 matrix-vector kernel as bonsai_b1_linear_f32
+  // (it needs no activation copy, so neither the scratch array nor a size limit).
+  if (tokens == 1 && b1_gemv_supported(w)) {
+    if (cur != w.device)
+      return fail(BONSAI_ERR_ARG, "b1_linear_f32_noalloc: the weight lives on device " +
+                                      std::to_string(w.device) + ", the current device is " +
+                                      std::to_string(cur));
+    return launch_b1_gemv_f32(act, w, out, static_cast<cudaStream_t>(stream));
+  }
   const long long n = (long long)tokens * w.k_in;
   if (n > kNoAllocMaxElems)
     return fail(BONSAI_ERR_UNSUPPORTED,

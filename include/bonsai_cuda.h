@@ -142,8 +142,10 @@ int bonsai_b1_linear_f32(const float* act, int tokens, bonsai_b1_t w, float* out
  * address (cudaGetSymbolAddress) with the device current: make that first
  * call before any stream capture.  All calls share the one array, so calls
  * that may overlap on the GPU (different streams, or different host threads
- * on one device) race: serialise them.  The weight must live on the current
- * device (BONSAI_ERR_ARG otherwise). */
+ * on one device) race: serialise them.  A single token (tokens == 1,
+ * in_dim <= 8192) runs the same f32 matrix-vector kernel as
+ * bonsai_b1_linear_f32 and does not touch the array.  The weight must live
+ * on the current device (BONSAI_ERR_ARG otherwise). */
 int bonsai_b1_linear_f32_noalloc(const float* act, int tokens, bonsai_b1_t w, float* out,
                                  void* stream);
 
