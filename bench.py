@@ -430,6 +430,14 @@ def measure_split_2048(args, rank: int, world: int, dist) -> dict:
     # reductions below) is the same on all ranks
     phase_ms = {k: round(max_over_ranks(pt[k]), 3) for k in sorted(pt)}
     phase_ms_min = {k: round(-max_over_ranks(-pt[k]), 3) for k in sorted(pt)}
+    keys = sorted(pt)
+    if dist:  # every rank's own phase times (same key order on all ranks)
+        mine = torch.tensor([pt[k] for k in keys], device="cuda", dtype=torch.float64)
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        by_rank = [{k: round(float(v), 3) for k, v in zip(keys, e.tolist())} for e in every]
+    else:
+        by_rank = [{k: round(pt[k], 3) for k in keys}]
     assert bb.device_error() == 0
 
     res = {"n_gpus": world, "ms_per_step": round(ms, 3), "e2e_ms": round(ms_e2e, 3),
@@ -438,7 +446,7 @@ def measure_split_2048(args, rank: int, world: int, dist) -> dict:
            "order": (ORDER_DESC[args.order] if world > 1 and args.exchange != "nccl" else None),
            "images_per_s": round(1000.0 / ms, 3),
            "step_tflops": round(step_flops(img_n + TXT, img_n) / (ms / 1e3) / 1e12, 1),
-           "phase_ms": phase_ms, "phase_ms_min_rank": phase_ms_min,
+           "phase_ms": phase_ms, "phase_ms_min_rank": phase_ms_min, "phase_ms_by_rank": by_rank,
            "phase_ms_note": "one extra step, a CUDA-event pair around every phase and exchange "
                             "call, summed per stage; phase_ms = max over ranks, "
                             "phase_ms_min_rank = min over ranks (the spread is load imbalance)"}
