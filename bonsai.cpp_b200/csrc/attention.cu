@@ -201,8 +201,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* ks = qs + 2 * Q_BYTES;
   uint8_t* vs = ks + KS * K_SLOT;
   uint64_t* bars = reinterpret_cast<uint64_t*>(vs + VS * V_SLOT);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;
+  uint64_t* q_full = bars;           // [2] per query tile
+  uint64_t* k_full = q_full + 2;
   uint64_t* k_empty = k_full + KS;
   uint64_t* v_full = k_empty + KS;
   uint64_t* v_empty = v_full + VS;
@@ -231,7 +231,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int nkv = kSplit ? min((p.seq + BKV - 1) / BKV - j0, p.kv_chunk) : (p.seq + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
-    bar_init(q_full, 1);
+    bar_init(&q_full[0], 1);
+    bar_init(&q_full[1], 1);
     for (int s = 0; s < KS; ++s) {
       bar_init(&k_full[s], 1);
       bar_init(&k_empty[s], 1);
@@ -275,16 +276,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
       constexpr int ncta = kPair ? 2 : 1;
-      if (leader) bar_arrive_expect_tx(q_full, ncta * 2 * Q_BYTES);
-      for (int g = 0; g < 2; ++g) {
+      // Query tile g on its own barrier: Q0 first, Q1 after the first key
+      // block, so that S_0(0) can start before Q1 has landed.
+      auto load_q = [&](int g) {
+        if (leader) bar_arrive_expect_tx(&q_full[g], ncta * Q_BYTES);
         for (int h = 0; h < 2; ++h) {
           if constexpr (kPair)
-            tma_load_3d_pair(qs + g * Q_BYTES + h * Q_HALF, &qmap, lead_bar(q_full), h * 64,
+            tma_load_3d_pair(qs + g * Q_BYTES + h * Q_HALF, &qmap, lead_bar(&q_full[g]), h * 64,
                              q0 + g * tstride, head);
           else
-            tma_load_3d(qs + g * Q_BYTES + h * Q_HALF, &qmap, q_full, h * 64, q0 + g * tstride, head);
+            tma_load_3d(qs + g * Q_BYTES + h * Q_HALF, &qmap, &q_full[g], h * 64,
+                        q0 + g * tstride, head);
         }
-      }
+      };
+      load_q(0);
       bool ok = true;
       for (int j = 0; j < nkv && ok; ++j) {
         const int sk = j % KS;
@@ -301,6 +306,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tma_load_3d(ks + sk * K_SLOT + h * K_SLOT_HALF, &kmap, &k_full[sk], h * 64,
                         (j0 + j) * BKV, head);
         }
+        if (j == 0) load_q(1);
         const int sv = j % VS;
         if (!wait_bar(&v_empty[sv], ((j / VS) & 1) ^ 1, abort_flag, p.err, DEV_ERR_TIMEOUT_TMA)) {
           ok = false;
@@ -335,11 +341,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         else
           tc_commit(b);
       };
-      bool ok = wait_bar(q_full, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA);
+      bool ok = true;
       // S_g(j) = Q_g K_j^T into S_{g, j&1}; the K stage is released after the
       // second tile's product.
       auto issue_s = [&](int j, int g) -> bool {
         const int sk = j % KS;
+        if (j == 0 && !wait_bar(&q_full[g], 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
+          return false;
         if (g == 0 &&
             !wait_bar(&k_full[sk], (j / KS) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA))
           return false;
